@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""Benchmark of the CDQ-LRR batch-1 dequant-GEMV on B200.
+
+Workload (default, "qwen05"): the 168 projection weights (q/k/v/o/gate/up/down
+of 24 layers) of a random-init Qwen2.5-0.5B-architecture model, bf16
+N(0, 0.02^2) with 1.5% of entries scaled by U(8, 20), quantised with the
+26-state lattice and stc-frac 0.0156 by the GPU quantizer. A step is one
+batch-1 dequant-GEMV over every one of those weights (independent seeded
+N(0, 1) bf16 activations), issued as one grouped launch replayed from a CUDA
+graph. The packed working set (about 261 MB) is larger than the 126 MB L2,
+so no L2 flush is needed between steps.
+
+  value  = algorithmic bytes of the step / device time of the step (GB/s);
+           algorithmic bytes = the reference .cdq tile records of every
+           weight (2 + 20 index bytes + ceil(21 * residuals / 8) per tile)
+           plus the activations read and the outputs written.
+  e2e    = the same metric through the public grouped-linear call with the
+           activations copied in from pinned host memory and the outputs
+           copied back every step.
+  roofline = the GEMV kernel's achieved bandwidth against the measured HBM
+           copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline = the reference's CPU forward (dequant + F.linear, restated
+           with the same torch ops) on a sample of the workload.
+
+``--impl reference`` times that CPU forward alone, on all host threads.
+Multi-GPU (torchrun): every rank runs its own replica of the workload (weak
+scaling, no collective on the data path); value = total bytes of all ranks /
+the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "dequant-GEMV HBM GB/s (% of B200 peak); batch-1 decode tokens/s"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("qwen05",), default="qwen05")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config() -> dict:
+    return {"workload": "Qwen2.5-0.5B-shape CDQ-26 projections (24 layers x 7), batch-1 "
+                        "dequant-GEMV, stc-frac 0.0156",
+            "batch": 1, "projections": 168, "lattice_states": 26,
+            "weights": "bf16 N(0,0.02^2) + 1.5% x U(8,20), seeded",
+            "l2": "packed working set > 126 MB L2; no flush needed",
+            "launch": "one grouped launch per step, CUDA graph replay"}
+
+
+def layer_list():
+    from cdq_lrr_b200.synth import QWEN05, layer_shapes
+    out = []
+    for layer in range(QWEN05["layers"]):
+        for name, rows, cols in layer_shapes(QWEN05):
+            out.append((f"model.layers.{layer}.{name}", rows, cols))
+    return out
+
+
+def measured_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """SM clock and throttle reasons sampled through NVML while the GPU works."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+        self.t = None
+
+    def start(self):
+        if not self.ok:
+            return
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                    rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.samples.append((time.perf_counter(), mhz, rs))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+        self.t = threading.Thread(target=run, daemon=True)
+        self.t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self.t:
+            self.t.join()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        note = None
+        if len(win) < 3:
+            win = self.samples[-20:]
+            note = "timed region shorter than the sampling period: last samples of the run"
+        mhz = statistics.median([s[1] for s in win]) if win else None
+        reasons = set()
+        for _, _, rs in win:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        out = {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+               "samples": len(win)}
+        if note:
+            out["note"] = note
+        return out
+
+
+def dist_setup(n_gpus: int):
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, v: float) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(ws, v: float) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# --------------------------------------------------------------- CPU baseline
+
+
+def cpu_baseline(seconds: float, use_product_quantizer_packs=None) -> dict:
+    """The reference CPU forward on layer 0's seven projections, repeated."""
+    import numpy as np
+    import torch
+    from oracle import cdq_oracle as O
+    from oracle.cdq_oracle_torch import OracleCDQLinear
+    from cdq_lrr_b200.synth import QWEN05, layer_shapes, synth_activation, synth_weight
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    mods, xs = [], []
+    for i, (name, rows, cols) in enumerate(layer_shapes(QWEN05)):
+        w = synth_weight(rows, cols, std=0.02, seed=1000 + i)
+        p = O.quantize(w.view(torch.int16).numpy().view(np.uint16), n_states=26)
+        mods.append(OracleCDQLinear(p))
+        xs.append(synth_activation(1, cols, seed=2000 + i))
+    step_bytes = sum(m.reference_bytes() + x.numel() * 2 + m.orig_shape[0] * 2
+                     for m, x in zip(mods, xs))
+    with torch.no_grad():
+        for m, x in zip(mods, xs):
+            m(x)  # warm-up
+        times = []
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            for m, x in zip(mods, xs):
+                m(x)
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": step_bytes / med / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"layer-0 projections of the workload (7 weights, {step_bytes / 1e6:.2f} MB "
+                      f"algorithmic), {len(times)} passes, median {med * 1e3:.2f} ms/pass; "
+                      f"reference forward = lattice gather, bf16 scale multiply, residual "
+                      f"scatter, F.linear (torch CPU)",
+            "ms_per_pass": med * 1e3}
+
+
+# ------------------------------------------------------------------- our arm
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+
+    ws_, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    # weights: generated and quantised on the GPU, one at a time
+    tasks = []
+    alg_bytes = 0
+    packed_bytes = 0
+    for i, (name, rows, cols) in enumerate(layer_list()):
+        w = synth_weight(rows, cols, std=0.02, seed=i, device=dev)
+        pack, info = ops.quantize(w, n_states=26, stc_frac=0.0156)
+        del w
+        x = synth_activation(1, cols, seed=10000 + i, device=dev)
+        y = torch.empty(1, rows, dtype=torch.bfloat16, device=dev)
+        tasks.append(ops.GemvTask(pack, x, y))
+        alg_bytes += pack.reference_bytes() + x.numel() * 2 + y.numel() * 2
+        packed_bytes += pack.device_bytes()
+    torch.cuda.synchronize()
+    grouped = ops.GroupedLinear(tasks, m=1)
+    launches_per_step = grouped.launches
+
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            grouped()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        grouped()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    stream.synchronize()
+    barrier(ws_)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    t1 = time.perf_counter()
+    barrier(ws_)
+    torch.cuda.synchronize()
+    sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ws_, ms)
+    total_bytes = sum_over_ranks(ws_, float(alg_bytes))
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    kernel_gbs = alg_bytes / (ms * 1e-3) / 1e9  # one grouped launch per step
+
+    # end to end: host activations in, host outputs out, through the public call
+    xs_host = torch.empty(sum(t.x.numel() for t in tasks), dtype=torch.bfloat16).pin_memory()
+    ys_host = torch.empty(sum(t.y.numel() for t in tasks), dtype=torch.bfloat16).pin_memory()
+    xs_dev = torch.empty_like(xs_host, device=dev)
+    ys_dev = torch.empty_like(ys_host, device=dev)
+    xo = yo = 0
+    e2e_tasks = []
+    for t in tasks:
+        nx, ny = t.x.numel(), t.y.numel()
+        xs_dev[xo:xo + nx].copy_(t.x.view(-1))
+        e2e_tasks.append(ops.GemvTask(t.pack, xs_dev[xo:xo + nx].view_as(t.x),
+                                      ys_dev[yo:yo + ny].view_as(t.y)))
+        xo += nx
+        yo += ny
+    xs_host.copy_(xs_dev.cpu())
+    e2e_call = ops.GroupedLinear(e2e_tasks, m=1)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            xs_dev.copy_(xs_host, non_blocking=True)
+            e2e_call()
+            ys_host.copy_(ys_dev, non_blocking=True)
+    stream.synchronize()
+    barrier(ws_)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            xs_dev.copy_(xs_host, non_blocking=True)
+            e2e_call()
+            ys_host.copy_(ys_dev, non_blocking=True)
+        e1.record(stream)
+    stream.synchronize()
+    barrier(ws_)
+    ms_e2e = max_over_ranks(ws_, e0.elapsed_time(e1) / args.steps)
+    e2e_value = total_bytes / (ms_e2e * 1e-3) / 1e9
+    # the e2e outputs equal the device-resident run's
+    ok = torch.equal(ys_host.to(dev)[: tasks[0].y.numel()], tasks[0].y.view(-1))
+
+    peak, peak_kind = measured_peak()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemv_qwen05_traffic.json")
+    if os.path.exists(tp):
+        try:
+            with open(tp) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and ws_ == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws_,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights and activations)",
+            "config": {**workload_config(), "packed_mb_reference_format": round(alg_bytes / 1e6, 2),
+                       "packed_mb_device_layout": round(packed_bytes / 1e6, 2),
+                       "parallelism": f"replicas x{ws_}" if ws_ > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(kernel_gbs / peak, 4),
+                         "peak_kind": f"of {peak_kind}", "traffic": traffic,
+                         "kernel": "cdq gemv_kernel<26,1,192> (one grouped launch per step)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": int(xs_host.numel() * 2),
+                    "d2h_bytes_per_step": int(ys_host.numel() * 2),
+                    "ms_per_step": round(ms_e2e, 5), "outputs_match": bool(ok)},
+            "gpu_launches": int(args.steps * launches_per_step),
+            "clocks": sampler.summary(t0, t1),
+            "cpu_baseline": cpu,
+            "decode": None,
+        }
+        print(json.dumps(line), flush=True)
+    if ws_ > 1:
+        import torch.distributed as dist
+        del graph
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the reference arm runs on rank 0 only
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    import numpy as np
+    from oracle import cdq_oracle as O
+    from oracle.cdq_oracle_torch import OracleCDQLinear
+    from cdq_lrr_b200.synth import QWEN05, layer_shapes, synth_activation, synth_weight
+    mods, xs = [], []
+    for i, (name, rows, cols) in enumerate(layer_shapes(QWEN05)):
+        w = synth_weight(rows, cols, std=0.02, seed=i)
+        p = O.quantize(w.view(torch.int16).numpy().view(np.uint16), n_states=26)
+        mods.append(OracleCDQLinear(p))
+        xs.append(synth_activation(1, cols, seed=10000 + i))
+    step_bytes = sum(m.reference_bytes() + x.numel() * 2 + m.orig_shape[0] * 2
+                     for m, x in zip(mods, xs))
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            for m, x in zip(mods, xs):
+                m(x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for m, x in zip(mods, xs):
+                m(x)
+        dt = (time.perf_counter() - t0) / args.steps
+    value = step_bytes / dt / 1e9
+    sample = (f"each step = the reference CPU forward over layer 0's 7 projections of the "
+              f"workload ({step_bytes / 1e6:.2f} MB algorithmic); GB/s is size-independent")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,115 @@
+"""ctypes binding of libcdq_b200.so (the C ABI declared in include/cdq.h).
+
+The library is built in-tree by ``cdq_lrr_b200.build`` and loaded from the
+package directory. There is no fallback: if the library is missing or does
+not load, every product entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libcdq_b200.so"
+
+STATUS = {
+    0: "CDQ_OK", 1: "CDQ_ERR_SHAPE", 2: "CDQ_ERR_STATES", 3: "CDQ_ERR_ARG", 4: "CDQ_ERR_CUDA",
+    5: "CDQ_ERR_FORMAT", 6: "CDQ_ERR_CAPACITY", 7: "CDQ_ERR_WORKSPACE", 8: "CDQ_ERR_UNSUPPORTED",
+}
+MAX_BATCH = 8
+MAX_COLS = 65536
+
+
+class CdqError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what} failed: {STATUS.get(status, status)}")
+
+
+class cdq_packed(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("n_states", C.c_int32),
+                ("reserved0", C.c_int32), ("n_res", C.c_int64),
+                ("codes", C.c_void_p), ("scales", C.c_void_p), ("res_ptr", C.c_void_p),
+                ("res_ent", C.c_void_p), ("res_q", C.c_void_p)]
+
+
+class cdq_sizes(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "row_blocks", "tile_cols", "res_groups", "codes_bytes", "scales_bytes", "res_ptr_count",
+        "max_res", "linear_workspace_bytes", "quantize_workspace_bytes")]
+
+
+class cdq_gemv_job(C.Structure):
+    _fields_ = [("w", cdq_packed), ("x", C.c_void_p), ("y", C.c_void_p), ("bias", C.c_void_p),
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
+                ("out_f32", C.c_int32), ("reserved0", C.c_int32)]
+
+
+class cdq_quant_info(C.Structure):
+    _fields_ = [("n_res", C.c_int64), ("k", C.c_int64), ("threshold", C.c_float),
+                ("topk_fallback", C.c_int32), ("mask_count", C.c_int64)]
+
+
+class cdq_file_tensor(C.Structure):
+    _fields_ = [("name", C.c_char * 256), ("rows", C.c_int32), ("cols", C.c_int32),
+                ("n_tiles", C.c_int64), ("n_res", C.c_int64), ("record_offset", C.c_int64),
+                ("record_bytes", C.c_int64)]
+
+
+_P = C.c_void_p
+_SIGS = {
+    "cdq_get_sizes": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_double, C.c_int32,
+                                C.POINTER(cdq_sizes)]),
+    "cdq_version": (C.c_char_p, []),
+    "cdq_linear": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P, C.c_size_t, _P]),
+    "cdq_linear_f32": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P, C.c_size_t, _P]),
+    "cdq_linear_grouped": (C.c_int, [C.POINTER(cdq_gemv_job), C.c_int32, C.c_int64, _P]),
+    "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
+    "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,
+                               C.POINTER(cdq_packed), _P, _P, C.c_size_t, _P]),
+    "cdq_host_from_reference": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P,
+                                          C.c_int64, C.POINTER(cdq_packed)]),
+    "cdq_host_to_reference": (C.c_int, [C.POINTER(cdq_packed), _P, _P, _P, _P]),
+    "cdq_file_scan": (C.c_int, [_P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(cdq_file_tensor),
+                                C.c_int32, C.POINTER(C.c_int32)]),
+    "cdq_file_decode": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), _P, _P,
+                                  _P, _P]),
+    "cdq_file_encode_header": (C.c_int, [C.c_int32, C.c_int32, _P, C.c_int64,
+                                         C.POINTER(C.c_int64)]),
+    "cdq_file_encode_tensor": (C.c_int, [C.c_char_p, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P,
+                                         _P, C.c_int64, _P, C.c_int64, C.POINTER(C.c_int64)]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m cdq_lrr_b200.build`")
+        h = C.CDLL(os.fspath(LIB_PATH))
+        for name, (res, args) in _SIGS.items():
+            f = getattr(h, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = h
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise CdqError(status, what)
+
+
+def sizes(rows: int, cols: int, n_states: int, stc_frac: float = 0.0156,
+          max_batch: int = MAX_BATCH) -> cdq_sizes:
+    s = cdq_sizes()
+    check(lib().cdq_get_sizes(rows, cols, n_states, stc_frac, max_batch, C.byref(s)), "cdq_get_sizes")
+    return s

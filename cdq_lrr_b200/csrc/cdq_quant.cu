@@ -1,0 +1,537 @@
+// GPU tile quantizer, bit-exact with quantize_cdq_lrr
+// (code/cdq_lrr_qwen05.py:63-133) on torch 2.x CPU semantics.
+//
+// Pipeline (all asynchronous on one stream, no host round trip):
+//  1. tile statistics: sigma = max|w| (NaN propagates), float8 code of the
+//     clamped sigma (:83-84, :117), unbiased tile variance by a sequential
+//     float64 Welford recurrence rounded to float32 (torch's CPU var, :87);
+//  2. radix select (three digit passes over the float32 bit patterns of the
+//     saliency |w| * (var + 1e-6), :88) of the two order statistics that
+//     torch.quantile(..., 1 - stc_frac) interpolates (:90), then the
+//     fused-multiply-add lerp; any NaN saliency makes the threshold NaN;
+//  3. per residual bucket, the count of saliency >= threshold (:91);
+//  4. if more than 2k weights qualify (:93-96): radix select of the k-th
+//     largest saliency, and the k largest with ties taken at the lowest flat
+//     indices (torch 2.11's CPU topk choice among equal values);
+//  5. exclusive scan of the bucket counts -> residual CSR offsets;
+//  6. per tile: nearest-centroid index of w / sigma_q (float32 division,
+//     first index on ties, NaN first, :104-110), residual substitution, pair
+//     codes, residual entries (:98-99).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "cdq.h"
+#include "cdq_common.cuh"
+#include "cdq_internal.cuh"
+
+namespace cdq {
+
+namespace {
+
+__constant__ float q_lat26[26];
+__constant__ float q_lat16[16];
+
+constexpr int kHistBins = 2048;
+constexpr int kSel = 3;  // selections: 0 lower rank, 1 upper rank, 2 k-th largest
+
+struct QState {
+    unsigned long long rank[kSel];   // remaining 0-based rank inside the prefix
+    unsigned long long below[kSel];  // keys below the prefix
+    unsigned long long equal[kSel];  // keys equal to the selected key
+    unsigned long long mask_count;
+    unsigned long long need;         // fallback: ties to include
+    uint32_t prefix[kSel];
+    uint32_t nan_flag;
+    uint32_t fallback;
+    float thr;
+    float vk;
+};
+
+struct WS {
+    float* var;
+    uint32_t* tie;
+    uint32_t* hist;  // [kSel][kHistBins]
+    QState* st;
+};
+
+WS carve(uint8_t* ws, int64_t n_tiles) {
+    auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+    WS w;
+    w.var = reinterpret_cast<float*>(ws);
+    ws += al(n_tiles * 4);
+    w.tie = reinterpret_cast<uint32_t*>(ws);
+    ws += al((n_tiles + 1) * 4);
+    w.hist = reinterpret_cast<uint32_t*>(ws);
+    ws += al(4 * kHistBins * 4);
+    w.st = reinterpret_cast<QState*>(ws);
+    return w;
+}
+
+__device__ __forceinline__ float sal_of(float x, float var) {
+    return __fmul_rn(fabsf(x), __fadd_rn(var, 1e-6f));
+}
+
+__device__ __forceinline__ void load_tile(const uint16_t* w, int64_t t, float (&x)[32]) {
+    const uint4* p = reinterpret_cast<const uint4*>(w + t * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint4 v = p[q];
+        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            x[q * 8 + 2 * k] = __uint_as_float(u[k] << 16);
+            x[q * 8 + 2 * k + 1] = __uint_as_float(u[k] & 0xFFFF0000u);
+        }
+    }
+}
+
+// 1. per-tile sigma code and variance
+__global__ void k_stats(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, int ns,
+                        uint8_t* __restrict__ scales, WS ws) {
+    const Geometry g = geometry(rows, cols, ns);
+    const int64_t n_tiles = (int64_t)rows * g.kt;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        float x[32];
+        load_tile(w, t, x);
+        float sig = 0.f;
+        bool nan = false;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            float a = fabsf(x[e]);
+            nan |= isnan(a);
+            sig = fmaxf(sig, a);
+        }
+        if (nan) sig = __uint_as_float(0x7FC00000u);
+        else if (sig < 1e-8f) sig = __uint_as_float(0x322C0000u);  // bf16(1e-8): clamp(min=1e-8)
+        const int64_t row = t / g.kt, c = t % g.kt;
+        scales[scale_index(g, row / 32, c, (int)(row % 32))] = fp8_encode(sig);
+        double mean = 0.0, m2 = 0.0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            double xe = (double)x[e];
+            double d = __dsub_rn(xe, mean);
+            mean = __dadd_rn(mean, __ddiv_rn(d, (double)(e + 1)));
+            m2 = __dadd_rn(m2, __dmul_rn(d, __dsub_rn(xe, mean)));
+        }
+        float var = __double2float_rn(__ddiv_rn(m2, 31.0));
+        ws.var[t] = var;
+        bool sal_nan = false;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sal_nan |= isnan(sal_of(x[e], var));
+        if (sal_nan) ws.st->nan_flag = 1u;
+    }
+}
+
+// 2. one digit pass of the radix select for the active selections
+template <int PASS>
+__global__ void k_hist(const uint16_t* __restrict__ w, int64_t n_tiles, uint32_t active,
+                       int fallback_only, WS ws) {
+    constexpr int shift = PASS == 0 ? 21 : (PASS == 1 ? 10 : 0);
+    constexpr uint32_t dmask = PASS == 2 ? 0x3FFu : 0x7FFu;
+    if (fallback_only && !ws.st->fallback) return;
+    __shared__ uint32_t h[kSel][kHistBins];
+    for (int i = threadIdx.x; i < kSel * kHistBins; i += blockDim.x) (&h[0][0])[i] = 0;
+    __syncthreads();
+    uint32_t pre[kSel];
+#pragma unroll
+    for (int s = 0; s < kSel; ++s) pre[s] = ws.st->prefix[s];
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        float x[32];
+        load_tile(w, t, x);
+        const float var = ws.var[t];
+#pragma unroll 4
+        for (int e = 0; e < 32; ++e) {
+            const uint32_t key = __float_as_uint(sal_of(x[e], var));
+            const uint32_t d = (key >> shift) & dmask;
+#pragma unroll
+            for (int s = 0; s < kSel; ++s) {
+                if (!((active >> s) & 1u)) continue;
+                if (PASS == 0 || (key >> (shift + (PASS == 2 ? 10 : 11))) == pre[s])
+                    atomicAdd(&h[s][d], 1u);
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kSel * kHistBins; i += blockDim.x) {
+        const uint32_t v = (&h[0][0])[i];
+        if (v) atomicAdd(&ws.hist[i], v);
+    }
+}
+
+// pick the digit that holds each active selection's rank; reset the histogram
+template <int PASS>
+__global__ void k_find(uint32_t active, int fallback_only, WS ws) {
+    constexpr int bits = PASS == 2 ? 10 : 11;
+    constexpr int nb = 1 << bits;
+    QState* st = ws.st;
+    if (fallback_only && !st->fallback) return;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSel; ++s) {
+            if (!((active >> s) & 1u)) continue;
+            unsigned long long cum = 0;
+            const uint32_t* h = ws.hist + s * kHistBins;
+            for (int d = 0; d < nb; ++d) {
+                const unsigned long long c = h[d];
+                if (cum + c > st->rank[s]) {
+                    st->rank[s] -= cum;
+                    st->below[s] += cum;
+                    st->prefix[s] = (PASS == 0 ? 0u : (st->prefix[s] << bits)) | (uint32_t)d;
+                    st->equal[s] = c;
+                    break;
+                }
+                cum += c;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kSel * kHistBins; i += blockDim.x) ws.hist[i] = 0;
+}
+
+__global__ void k_init(WS ws, unsigned long long r_lo, unsigned long long r_hi) {
+    QState* st = ws.st;
+    st->rank[0] = r_lo;
+    st->rank[1] = r_hi;
+    st->rank[2] = 0;
+    for (int s = 0; s < kSel; ++s) {
+        st->below[s] = 0;
+        st->equal[s] = 0;
+        st->prefix[s] = 0;
+    }
+    st->mask_count = 0;
+    st->need = 0;
+    st->nan_flag = 0;
+    st->fallback = 0;
+    st->thr = 0.f;
+    st->vk = 0.f;
+}
+
+// torch's lerp: |w| < 0.5 ? fma(w, b - a, a) : fma(w - 1, b - a, b)
+__global__ void k_threshold(WS ws, float weight) {
+    QState* st = ws.st;
+    if (st->nan_flag) {
+        st->thr = __uint_as_float(0x7FC00000u);
+        return;
+    }
+    const float a = __uint_as_float(st->prefix[0]), b = __uint_as_float(st->prefix[1]);
+    const float diff = __fsub_rn(b, a);
+    st->thr = fabsf(weight) < 0.5f ? fmaf(weight, diff, a) : fmaf(__fsub_rn(weight, 1.0f), diff, b);
+}
+
+// does weight (tile t, element e) become a residual
+struct Rule {
+    float thr, vk;
+    unsigned long long need;
+    bool fallback;
+};
+
+__device__ __forceinline__ Rule make_rule(const QState* st) {
+    Rule r;
+    r.thr = st->thr;
+    r.vk = st->vk;
+    r.need = st->need;
+    r.fallback = st->fallback != 0;
+    return r;
+}
+
+// 3/4b. residual count of every bucket (row, residual group)
+__global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, int ns,
+                        uint32_t* __restrict__ counts, WS ws, int fallback_pass) {
+    const QState* st = ws.st;
+    if (fallback_pass && !st->fallback) return;
+    const Geometry g = geometry(rows, cols, ns);
+    const int64_t nb = g.rb * g.kg * 32;
+    const Rule rule = make_rule(st);
+    unsigned long long total = 0;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
+         b += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rb = b / (g.kg * 32), grp = (b / 32) % g.kg;
+        const int64_t row = rb * 32 + (b & 31);
+        uint32_t cnt = 0;
+        if (row < rows) {
+            const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
+            for (int64_t c = c0; c < c1; ++c) {
+                const int64_t t = row * g.kt + c;
+                float x[32];
+                load_tile(w, t, x);
+                const float var = ws.var[t];
+                uint32_t tie = fallback_pass ? ws.tie[t] : 0u;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const float s = sal_of(x[e], var);
+                    bool inc;
+                    if (fallback_pass) {
+                        inc = s > rule.vk;
+                        if (s == rule.vk) {
+                            inc = tie < rule.need;
+                            ++tie;
+                        }
+                    } else {
+                        inc = s >= rule.thr;
+                    }
+                    cnt += inc;
+                }
+            }
+        }
+        counts[b] = cnt;
+        total += cnt;
+    }
+    if (!fallback_pass && total) atomicAdd(&ws.st->mask_count, total);
+}
+
+__global__ void k_decide(WS ws, unsigned long long n, unsigned long long k) {
+    QState* st = ws.st;
+    if (st->mask_count > 2ull * k) {
+        st->fallback = 1u;
+        st->rank[2] = n - k;  // ascending rank of the k-th largest
+    }
+}
+
+__global__ void k_fallback_key(WS ws, unsigned long long n, unsigned long long k) {
+    QState* st = ws.st;
+    if (!st->fallback) return;
+    st->vk = __uint_as_float(st->prefix[2]);
+    const unsigned long long gt = n - st->below[2] - st->equal[2];
+    st->need = k - gt;
+}
+
+// 4. ties (saliency == v_k) per tile, flat row-major tile order
+__global__ void k_ties(const uint16_t* __restrict__ w, int64_t n_tiles, WS ws) {
+    if (!ws.st->fallback) return;
+    const float vk = ws.st->vk;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        float x[32];
+        load_tile(w, t, x);
+        const float var = ws.var[t];
+        uint32_t c = 0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) c += sal_of(x[e], var) == vk;
+        ws.tie[t] = c;
+    }
+}
+
+// exclusive scan in place over n entries by one block of 1024 threads
+__global__ void __launch_bounds__(1024) k_scan(uint32_t* data, int64_t n, const QState* gate) {
+    if (gate && !gate->fallback) return;
+    __shared__ uint32_t wsum[32];
+    __shared__ uint32_t carry_s;
+    constexpr int kItems = 8;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    if (tid == 0) carry_s = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < n; base += 1024 * kItems) {
+        uint32_t v[kItems], s = 0;
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+            const int64_t idx = base + (int64_t)tid * kItems + i;
+            v[i] = idx < n ? data[idx] : 0u;
+            s += v[i];
+        }
+        uint32_t incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += u;
+        }
+        if (lane == 31) wsum[wid] = incl;
+        __syncthreads();
+        if (wid == 0) {
+            uint32_t ws_ = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                uint32_t u = __shfl_up_sync(0xFFFFFFFFu, ws_, o);
+                if (lane >= o) ws_ += u;
+            }
+            wsum[lane] = ws_;  // inclusive warp totals
+        }
+        __syncthreads();
+        uint32_t run = carry_s + (wid ? wsum[wid - 1] : 0u) + incl - s;
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+            const int64_t idx = base + (int64_t)tid * kItems + i;
+            if (idx < n) data[idx] = run;
+            run += v[i];
+        }
+        __syncthreads();
+        if (tid == 0) carry_s += wsum[31];
+        __syncthreads();
+    }
+}
+
+// 6. per bucket: lattice snap, residual substitution, codes and residual entries
+template <int NS>
+__global__ void k_pack(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, cdq_packed out,
+                       WS ws) {
+    const Geometry g = geometry(rows, cols, NS);
+    const int64_t nb = g.rb * g.kg * 32;
+    const Rule rule = make_rule(ws.st);
+    constexpr int kStates = NS;
+    constexpr uint32_t kRes = NS == 26 ? kResidualSym26 : kResidualSym16;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
+         b += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rb = b / (g.kg * 32), grp = (b / 32) % g.kg;
+        const int lane = (int)(b & 31);
+        const int64_t row = rb * 32 + lane;
+        const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
+        uint32_t pos = out.res_ptr[b];
+        for (int64_t c = c0; c < c1; ++c) {
+            uint8_t sym[32];
+            if (row < rows) {
+                const int64_t t = row * g.kt + c;
+                float x[32];
+                load_tile(w, t, x);
+                const float var = ws.var[t];
+                const float sq = bf16_to_f32(fp8_to_bf16(out.scales[scale_index(g, rb, c, lane)]));
+                uint32_t tie = rule.fallback ? ws.tie[t] : 0u;
+                const uint16_t* wt = w + t * 32;
+#pragma unroll 1
+                for (int e = 0; e < 32; ++e) {
+                    const float nrm = __fdiv_rn(x[e], sq);
+                    uint32_t q = 0;
+                    float best = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[0] : q_lat16[0]));
+                    if (!isnan(best)) {
+                        for (int j = 1; j < kStates; ++j) {
+                            const float d = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[j] : q_lat16[j]));
+                            if (isnan(d)) {
+                                q = j;
+                                break;
+                            }
+                            if (d < best) {
+                                best = d;
+                                q = j;
+                            }
+                        }
+                    }
+                    const float s = sal_of(x[e], var);
+                    bool inc;
+                    if (rule.fallback) {
+                        inc = s > rule.vk;
+                        if (s == rule.vk) {
+                            inc = tie < rule.need;
+                            ++tie;
+                        }
+                    } else {
+                        inc = s >= rule.thr;
+                    }
+                    if (inc) {
+                        out.res_ent[pos] = ((uint32_t)(c * 32 + e) << 16) | wt[e];
+                        out.res_q[pos] = (uint8_t)q;
+                        ++pos;
+                        sym[e] = (uint8_t)kRes;
+                    } else {
+                        sym[e] = (uint8_t)q;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) sym[e] = (uint8_t)kRes;
+            }
+            // pair codes
+            if (NS == 26) {
+                uint32_t acc[5] = {0, 0, 0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t code = (uint32_t)sym[2 * j] * 27u + sym[2 * j + 1];
+                    const int bit = 10 * j, wd = bit >> 5, off = bit & 31;
+                    acc[wd] |= code << off;
+                    if (off > 22) acc[wd + 1] |= code >> (32 - off);
+                }
+#pragma unroll
+                for (int wd = 0; wd < 5; ++wd) out.codes[code_word_index(g, rb, c, lane, wd)] = acc[wd];
+            } else {
+#pragma unroll
+                for (int wd = 0; wd < 4; ++wd) {
+                    uint32_t v = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int j = wd * 4 + k;
+                        v |= (uint32_t)(sym[2 * j] | (sym[2 * j + 1] << 4)) << (8 * k);
+                    }
+                    out.codes[code_word_index(g, rb, c, lane, wd)] = v;
+                }
+            }
+        }
+    }
+}
+
+__global__ void k_info(WS ws, const uint32_t* res_ptr, int64_t nb, cdq_quant_info* info,
+                       unsigned long long k) {
+    const QState* st = ws.st;
+    info->n_res = res_ptr[nb];
+    info->k = (int64_t)k;
+    info->threshold = st->thr;
+    info->topk_fallback = (int32_t)st->fallback;
+    info->mask_count = (int64_t)st->mask_count;
+}
+
+}  // namespace
+
+// Once per device (called by the C-ABI set-up).
+cudaError_t quantize_setup() {
+    float l26[26], l16[16];
+    for (int i = 0; i < 26; ++i) l26[i] = bf16_to_f32(kLattice26[i]);
+    for (int i = 0; i < 16; ++i) l16[i] = bf16_to_f32(kLattice16[i]);
+    cudaError_t e = cudaMemcpyToSymbol(q_lat26, l26, sizeof l26);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyToSymbol(q_lat16, l16, sizeof l16);
+}
+
+cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
+    cudaError_t e;
+    const Geometry g = geometry(a.rows, a.cols, a.n_states);
+    const int64_t numel = (int64_t)a.rows * a.cols, n_tiles = numel / 32;
+    const int64_t nb = g.rb * g.kg * 32;
+    WS ws = carve(a.ws, n_tiles);
+
+    // torch.quantile's rank rule in float32, evaluated here once
+    const float qf = (float)(1.0 - a.stc_frac);
+    const float r = qf * (float)(numel - 1);
+    const unsigned long long r_lo = (unsigned long long)floorf(r);
+    const unsigned long long r_hi = (unsigned long long)ceilf(r);
+    const float weight = r - (float)r_lo;
+    const double kd = nearbyint((double)numel * a.stc_frac);
+    const unsigned long long k = kd < 1.0 ? 1ull : (unsigned long long)kd;
+
+    const int threads = 256;
+    const int tile_blocks = (int)std::min<int64_t>((n_tiles + threads - 1) / threads, (int64_t)sms * 8);
+    const int bucket_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((nb + threads - 1) / threads, (int64_t)sms * 8));
+
+    if ((e = cudaMemsetAsync(a.out.scales, 0, (size_t)(g.rb * g.kt4 * 128), s)) != cudaSuccess) return e;
+    if ((e = cudaMemsetAsync(ws.hist, 0, (size_t)kSel * kHistBins * 4, s)) != cudaSuccess) return e;
+    if ((e = cudaMemsetAsync(a.out.res_ptr + nb, 0, 4, s)) != cudaSuccess) return e;
+    k_init<<<1, 1, 0, s>>>(ws, r_lo, r_hi);
+    k_stats<<<tile_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.scales, ws);
+    k_hist<0><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 3u, 0, ws);
+    k_find<0><<<1, 256, 0, s>>>(3u, 0, ws);
+    k_hist<1><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 3u, 0, ws);
+    k_find<1><<<1, 256, 0, s>>>(3u, 0, ws);
+    k_hist<2><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 3u, 0, ws);
+    k_find<2><<<1, 256, 0, s>>>(3u, 0, ws);
+    k_threshold<<<1, 1, 0, s>>>(ws, weight);
+    k_count<<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.res_ptr, ws, 0);
+    k_decide<<<1, 1, 0, s>>>(ws, (unsigned long long)numel, k);
+    // top-k fallback (each kernel returns at once unless the tie guard fired)
+    k_hist<0><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 4u, 1, ws);
+    k_find<0><<<1, 256, 0, s>>>(4u, 1, ws);
+    k_hist<1><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 4u, 1, ws);
+    k_find<1><<<1, 256, 0, s>>>(4u, 1, ws);
+    k_hist<2><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 4u, 1, ws);
+    k_find<2><<<1, 256, 0, s>>>(4u, 1, ws);
+    k_fallback_key<<<1, 1, 0, s>>>(ws, (unsigned long long)numel, k);
+    k_ties<<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, ws);
+    k_scan<<<1, 1024, 0, s>>>(ws.tie, n_tiles, ws.st);
+    k_count<<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.res_ptr, ws, 1);
+    // residual CSR offsets
+    k_scan<<<1, 1024, 0, s>>>(a.out.res_ptr, nb + 1, nullptr);
+    if (a.n_states == 26)
+        k_pack<26><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+    else
+        k_pack<16><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+    k_info<<<1, 1, 0, s>>>(ws, a.out.res_ptr, nb, a.info, k);
+    return cudaGetLastError();
+}
+
+}  // namespace cdq

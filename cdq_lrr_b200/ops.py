@@ -1,0 +1,292 @@
+"""Torch-facing calls into the C ABI: device packs, fused linear, dequant, quantize.
+
+PyTorch provides device memory and the current CUDA stream; every piece of
+arithmetic runs in libcdq_b200.so. CPU tensors are rejected: there is no CPU
+path in the product.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+TILE = 32
+
+
+def _vp(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what}: expected a CUDA tensor (the CDQ kernels have no CPU path)")
+
+
+@dataclass
+class DevicePack:
+    """One packed weight in the device layout of include/cdq.h.
+
+    uint32 buffers are held as int32 tensors (bit patterns)."""
+    rows: int
+    cols: int
+    n_states: int
+    n_res: int
+    codes: torch.Tensor
+    scales: torch.Tensor
+    res_ptr: torch.Tensor
+    res_ent: torch.Tensor
+    res_q: torch.Tensor
+    _ws: dict = field(default_factory=dict, repr=False)
+
+    @property
+    def device(self) -> torch.device:
+        return self.codes.device
+
+    @property
+    def n_tiles(self) -> int:
+        return self.rows * self.cols // TILE
+
+    def struct(self) -> L.cdq_packed:
+        p = L.cdq_packed()
+        p.rows, p.cols, p.n_states, p.reserved0 = self.rows, self.cols, self.n_states, 0
+        p.n_res = self.n_res
+        p.codes = self.codes.data_ptr()
+        p.scales = self.scales.data_ptr()
+        p.res_ptr = self.res_ptr.data_ptr()
+        p.res_ent = self.res_ent.data_ptr() if self.res_ent.numel() else None
+        p.res_q = self.res_q.data_ptr() if self.res_q.numel() else None
+        return p
+
+    def tensors(self) -> dict[str, torch.Tensor]:
+        return {"codes": self.codes, "scales": self.scales, "res_ptr": self.res_ptr,
+                "res_ent": self.res_ent, "res_q": self.res_q}
+
+    @classmethod
+    def empty(cls, rows: int, cols: int, n_states: int, res_capacity: int,
+              device) -> "DevicePack":
+        s = L.sizes(rows, cols, n_states)
+        dev = torch.device(device)
+        return cls(rows, cols, n_states, 0,
+                   torch.empty(s.codes_bytes // 4, dtype=torch.int32, device=dev),
+                   torch.empty(s.scales_bytes, dtype=torch.uint8, device=dev),
+                   torch.empty(s.res_ptr_count, dtype=torch.int32, device=dev),
+                   torch.empty(max(res_capacity, 0), dtype=torch.int32, device=dev),
+                   torch.empty(max(res_capacity, 0), dtype=torch.uint8, device=dev))
+
+    def to(self, device) -> "DevicePack":
+        t = {k: v.to(device) for k, v in self.tensors().items()}
+        return DevicePack(self.rows, self.cols, self.n_states, self.n_res, **t)
+
+    # ---- reference-format conversion (host C code) ----
+    @classmethod
+    def from_reference(cls, quant_indices, scales_f8, residual_indices, residual_values,
+                       rows: int, cols: int, n_states: int, device="cpu") -> "DevicePack":
+        """Reference pack tensors (code/cdq_lrr_qwen05.py:121-133) -> device layout."""
+        q = np.ascontiguousarray(_np(quant_indices, np.uint8).reshape(-1))
+        sc = np.ascontiguousarray(_np(scales_f8, np.uint8).reshape(-1))
+        ri = np.ascontiguousarray(_np(residual_indices, np.int64).reshape(-1))
+        rv = np.ascontiguousarray(_np(residual_values, np.uint16).reshape(-1))
+        if q.size != rows * cols or sc.size != rows * cols // TILE or ri.size != rv.size:
+            raise ValueError("reference pack tensors do not match the weight shape")
+        host = cls.empty(rows, cols, n_states, ri.size, "cpu")
+        st = host.struct()
+        L.check(L.lib().cdq_host_from_reference(
+            rows, cols, n_states, q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p),
+            ri.ctypes.data_as(C.c_void_p) if ri.size else None,
+            rv.ctypes.data_as(C.c_void_p) if rv.size else None, ri.size, C.byref(st)),
+            "cdq_host_from_reference")
+        host.n_res = int(ri.size)
+        return host if torch.device(device).type == "cpu" else host.to(device)
+
+    def to_reference(self) -> dict[str, np.ndarray]:
+        """Device layout -> reference pack arrays (numpy, host)."""
+        host = self.to("cpu")
+        n_tiles = self.n_tiles
+        q = np.empty((n_tiles, TILE), dtype=np.uint8)
+        sc = np.empty(n_tiles, dtype=np.uint8)
+        ri = np.empty(self.n_res, dtype=np.int64)
+        rv = np.empty(self.n_res, dtype=np.uint16)
+        st = host.struct()
+        L.check(L.lib().cdq_host_to_reference(
+            C.byref(st), q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p),
+            ri.ctypes.data_as(C.c_void_p) if ri.size else None,
+            rv.ctypes.data_as(C.c_void_p) if rv.size else None), "cdq_host_to_reference")
+        return {"quant_indices": q, "scales_f8": sc, "residual_indices": ri, "residual_values": rv}
+
+    # ---- byte accounting ----
+    def device_bytes(self) -> int:
+        return sum(int(t.numel() * t.element_size()) for t in self.tensors().values()
+                   if t is not self.res_q)
+
+    def reference_bytes(self) -> int:
+        """Bytes of the reference .cdq tile records of this weight:
+        sum over tiles of 2 + index bytes + ceil(21 * residuals / 8)."""
+        ib = 20 if self.n_states == 26 else 16
+        kt = self.cols // TILE
+        rp = self.res_ptr.to("cpu", torch.int64)
+        ent = self.res_ent[: self.n_res].to("cpu", torch.int64)
+        counts = (rp[1:] - rp[:-1])
+        kg = (kt + 31) // 32
+        b = torch.arange(counts.numel())
+        rows = (b // (kg * 32)) * 32 + (b % 32)
+        row_of = torch.repeat_interleave(rows, counts)
+        col = (ent >> 16) & 0xFFFF
+        tile = row_of * kt + col // TILE
+        tc = torch.bincount(tile, minlength=self.n_tiles)
+        return int(self.n_tiles * (2 + ib) + ((tc * 21 + 7) // 8).sum().item())
+
+    # ---- workspace of cdq_linear (zero-filled once, kept by the pack) ----
+    def linear_workspace(self, m: int) -> torch.Tensor:
+        dev = self.device
+        key = (dev, m)
+        ws = self._ws.get(key)
+        if ws is None:
+            s = L.sizes(self.rows, self.cols, self.n_states, max_batch=m)
+            ws = torch.zeros(max(s.linear_workspace_bytes, 256), dtype=torch.uint8, device=dev)
+            self._ws[key] = ws
+        return ws
+
+
+def _np(t, dtype) -> np.ndarray:
+    if isinstance(t, torch.Tensor):
+        t = t.detach().cpu()
+        if t.dtype in (torch.bfloat16, torch.float16):
+            t = t.view(torch.int16)
+        elif t.dtype == torch.float8_e4m3fn:
+            t = t.view(torch.uint8)
+        return t.numpy().view(dtype) if t.numpy().dtype.itemsize == np.dtype(dtype).itemsize \
+            else t.numpy().astype(dtype)
+    a = np.asarray(t)
+    return a.view(dtype) if a.dtype.itemsize == np.dtype(dtype).itemsize else a.astype(dtype)
+
+
+# ------------------------------------------------------------------ kernels
+
+
+def linear(pack: DevicePack, x: torch.Tensor, bias: torch.Tensor | None = None,
+           out_f32: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ w_hat^T (+ bias) with the fused kernel; x bf16 [..., cols] on CUDA."""
+    _require_cuda(x, "cdq linear")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("cdq linear: x must be bf16")
+    if x.shape[-1] != pack.cols:
+        raise ValueError(f"cdq linear: x has {x.shape[-1]} features, weight has {pack.cols}")
+    if x.device != pack.device:
+        raise ValueError("cdq linear: x and the packed weight are on different devices")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, pack.cols)
+    if x2.data_ptr() % 16 or not x2.is_contiguous():
+        x2 = x2.contiguous().clone()
+    m_total = x2.shape[0]
+    ydt = torch.float32 if out_f32 else torch.bfloat16
+    y = out if out is not None else torch.empty(m_total, pack.rows, dtype=ydt, device=x.device)
+    if bias is not None:
+        _require_cuda(bias, "cdq linear bias")
+        bias = bias.to(torch.bfloat16).contiguous()
+    fn = L.lib().cdq_linear_f32 if out_f32 else L.lib().cdq_linear
+    st = pack.struct()
+    stream = _stream(x.device)
+    for m0 in range(0, m_total, L.MAX_BATCH):
+        m = min(L.MAX_BATCH, m_total - m0)
+        ws = pack.linear_workspace(L.MAX_BATCH)
+        L.check(fn(C.byref(st), _vp(x2[m0:m0 + m]), m, _vp(y[m0:m0 + m]), _vp(bias),
+                   _vp(ws), ws.numel(), stream), "cdq_linear")
+    return y.reshape(*lead, pack.rows)
+
+
+@dataclass
+class GemvTask:
+    pack: DevicePack
+    x: torch.Tensor
+    y: torch.Tensor
+    bias: torch.Tensor | None = None
+
+
+def linear_grouped(tasks: list[GemvTask], m: int) -> None:
+    """Independent GEMVs with the same batch m in one launch (per lattice size)."""
+    if not tasks:
+        return
+    jobs = (L.cdq_gemv_job * len(tasks))()
+    for j, t in zip(jobs, tasks):
+        _require_cuda(t.x, "cdq grouped linear")
+        ws = t.pack.linear_workspace(L.MAX_BATCH)
+        j.w = t.pack.struct()
+        j.x = t.x.data_ptr()
+        j.y = t.y.data_ptr()
+        j.bias = t.bias.data_ptr() if t.bias is not None else None
+        j.workspace = ws.data_ptr()
+        j.workspace_bytes = ws.numel()
+        j.out_f32 = 1 if t.y.dtype == torch.float32 else 0
+    L.check(L.lib().cdq_linear_grouped(jobs, len(tasks), m, _stream(tasks[0].x.device)),
+            "cdq_linear_grouped")
+
+
+class GroupedLinear:
+    """A prepared grouped GEMV: the job table is built once, each call is one
+    C-ABI call (one launch per lattice size). The tensors given here must stay
+    alive and keep their storage between calls (the decode-step pattern)."""
+
+    def __init__(self, tasks: list[GemvTask], m: int):
+        self.tasks = list(tasks)
+        self.m = m
+        self.jobs = (L.cdq_gemv_job * len(self.tasks))()
+        for j, t in zip(self.jobs, self.tasks):
+            _require_cuda(t.x, "cdq grouped linear")
+            ws = t.pack.linear_workspace(L.MAX_BATCH)
+            j.w = t.pack.struct()
+            j.x = t.x.data_ptr()
+            j.y = t.y.data_ptr()
+            j.bias = t.bias.data_ptr() if t.bias is not None else None
+            j.workspace = ws.data_ptr()
+            j.workspace_bytes = ws.numel()
+            j.out_f32 = 1 if t.y.dtype == torch.float32 else 0
+        self.device = self.tasks[0].x.device if self.tasks else None
+        self.launches = len({t.pack.n_states for t in self.tasks}) if self.tasks else 0
+
+    def __call__(self) -> None:
+        if self.tasks:
+            L.check(L.lib().cdq_linear_grouped(self.jobs, len(self.tasks), self.m,
+                                               _stream(self.device)), "cdq_linear_grouped")
+
+
+def dequant(pack: DevicePack) -> torch.Tensor:
+    """Bit-exact w_hat [rows, cols] bf16 on the pack's device."""
+    if pack.device.type != "cuda":
+        raise RuntimeError("cdq dequant: the pack must be on a CUDA device")
+    out = torch.empty(pack.rows, pack.cols, dtype=torch.bfloat16, device=pack.device)
+    st = pack.struct()
+    L.check(L.lib().cdq_dequant(C.byref(st), _vp(out), _stream(pack.device)), "cdq_dequant")
+    return out
+
+
+def quantize(w: torch.Tensor, n_states: int = 26, stc_frac: float = 0.0156
+             ) -> tuple[DevicePack, dict]:
+    """GPU tile quantizer: bf16 [rows, cols] CUDA tensor -> (device pack, info)."""
+    _require_cuda(w, "cdq quantize")
+    if w.dim() != 2:
+        raise ValueError(f"expected 2D, got {tuple(w.shape)}")
+    rows, cols = w.shape
+    w = w.detach().to(torch.bfloat16).contiguous()
+    s = L.sizes(rows, cols, n_states, stc_frac)
+    pack = DevicePack.empty(rows, cols, n_states, s.max_res, w.device)
+    ws = torch.empty(s.quantize_workspace_bytes, dtype=torch.uint8, device=w.device)
+    info_t = torch.zeros(C.sizeof(L.cdq_quant_info), dtype=torch.uint8, device=w.device)
+    st = pack.struct()
+    L.check(L.lib().cdq_quantize(_vp(w), rows, cols, n_states, stc_frac, C.byref(st), _vp(info_t),
+                                 _vp(ws), ws.numel(), _stream(w.device)), "cdq_quantize")
+    raw = bytes(info_t.cpu().numpy().tobytes())
+    info = L.cdq_quant_info.from_buffer_copy(raw)
+    pack.n_res = int(info.n_res)
+    # release the unused residual capacity
+    pack.res_ent = pack.res_ent[: pack.n_res].clone()
+    pack.res_q = pack.res_q[: pack.n_res].clone()
+    return pack, {"n_res": int(info.n_res), "k": int(info.k), "threshold": float(info.threshold),
+                  "topk_fallback": bool(info.topk_fallback), "mask_count": int(info.mask_count)}

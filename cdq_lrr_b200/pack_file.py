@@ -1,0 +1,295 @@
+""".cdq file codec and packer, mirroring code/cdq_pack.py.
+
+Same names and formats as the reference module: the bit packers
+(``pack_5bit_row``, ``unpack_5bit_row``, ``pack_indices_nibble``,
+``unpack_nibble_row``, ``pack_residuals``, ``unpack_residuals``,
+code/cdq_pack.py:50-119), ``write_cdq(path, tensors, n_states=26)`` and
+``read_cdq(path)`` (:162-234), ``dequant_tile`` (:237-248) and the packer
+CLI (:251-318). Encoding and decoding of whole tensors run in the C library
+(cdq_file_*), byte-exact with the reference writer. ``write_cdq`` also
+accepts tensors given as flat residual lists (``residual_indices`` /
+``residual_values``) instead of per-tile blobs, which avoids the per-tile
+Python loop, and ``read_device_packs`` returns device packs directly.
+
+The CLI quantises on the GPU with the top-k tie guard of
+quantize_cdq_lrr; the reference CLI's inline quantiser (:283-291) has no
+guard, so the two differ only on tensors where the guard fires.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .ops import DevicePack
+
+MAGIC = b"CDQ1"
+VERSION = 1
+VERSION2 = 2
+TILE = 32
+IDX_BYTES_PER_TILE = 20
+NIBBLE_BYTES_PER_TILE = 16
+
+
+def pack_5bit_row(q32) -> bytes:
+    q = [int(v) for v in (q32.tolist() if hasattr(q32, "tolist") else q32)]
+    assert len(q) == 32
+    acc = 0
+    for i, v in enumerate(q):
+        acc |= (v & 0x1F) << (5 * i)
+    return acc.to_bytes(20, "little")
+
+
+def unpack_5bit_row(buf: bytes) -> torch.Tensor:
+    assert len(buf) == 20
+    acc = int.from_bytes(buf, "little")
+    return torch.tensor([(acc >> (5 * i)) & 0x1F for i in range(32)], dtype=torch.uint8)
+
+
+def pack_indices_nibble(indices_32) -> bytes:
+    q = torch.as_tensor(indices_32).to(torch.uint8)
+    assert q.numel() == 32
+    return bytes((((q[1::2] & 0x0F) << 4) | (q[0::2] & 0x0F)).tolist())
+
+
+def unpack_nibble_row(buf: bytes) -> torch.Tensor:
+    assert len(buf) == 16
+    out = torch.empty(32, dtype=torch.uint8)
+    for i, b in enumerate(buf):
+        out[2 * i] = b & 0x0F
+        out[2 * i + 1] = (b >> 4) & 0x0F
+    return out
+
+
+def pack_residuals(offsets, values_bf16) -> bytes:
+    offs = torch.as_tensor(offsets).tolist()
+    if len(offs) == 0:
+        return b""
+    vals = torch.as_tensor(values_bf16).to(torch.bfloat16).view(torch.int16).tolist()
+    acc, pos = 0, 0
+    for o, v in zip(offs, vals):
+        acc |= (int(o) & 0x1F) << pos
+        pos += 5
+        acc |= (int(v) & 0xFFFF) << pos
+        pos += 16
+    return acc.to_bytes((pos + 7) // 8, "little")
+
+
+def unpack_residuals(buf: bytes, tag_count: int):
+    if tag_count == 0:
+        return torch.empty(0, dtype=torch.uint8), torch.empty(0, dtype=torch.bfloat16)
+    acc = int.from_bytes(buf, "little")
+    offs = torch.empty(tag_count, dtype=torch.uint8)
+    raw = torch.empty(tag_count, dtype=torch.int32)
+    pos = 0
+    for i in range(tag_count):
+        offs[i] = (acc >> pos) & 0x1F
+        pos += 5
+        raw[i] = (acc >> pos) & 0xFFFF
+        pos += 16
+    return offs, raw.to(torch.int16).view(torch.bfloat16)
+
+
+def _u8(a) -> np.ndarray:
+    if isinstance(a, torch.Tensor):
+        a = a.detach().cpu()
+        if a.dtype == torch.float8_e4m3fn:
+            a = a.view(torch.uint8)
+        a = a.numpy()
+    return np.ascontiguousarray(np.asarray(a).astype(np.uint8, copy=False)).reshape(-1)
+
+
+def _flat_residuals(t: dict) -> tuple[np.ndarray, np.ndarray]:
+    if "residual_indices" in t:
+        ri = t["residual_indices"]
+        rv = t["residual_values"]
+        ri = np.ascontiguousarray(np.asarray(ri.cpu() if isinstance(ri, torch.Tensor) else ri,
+                                             dtype=np.int64)).reshape(-1)
+        if isinstance(rv, torch.Tensor):
+            rv = rv.detach().cpu()
+            rv = (rv.view(torch.int16) if rv.dtype == torch.bfloat16 else rv).numpy()
+        rv = np.ascontiguousarray(np.asarray(rv).view(np.uint16) if np.asarray(rv).dtype.itemsize == 2
+                                  else np.asarray(rv).astype(np.uint16)).reshape(-1)
+        return ri, rv
+    tags = _u8(t["tag_counts"])
+    ri, rv = [], []
+    for ti, (tc, blob) in enumerate(zip(tags.tolist(), t["res_blobs"])):
+        if tc:
+            acc = int.from_bytes(blob, "little")
+            pos = 0
+            for _ in range(tc):
+                ri.append(ti * TILE + ((acc >> pos) & 0x1F))
+                pos += 5
+                rv.append((acc >> pos) & 0xFFFF)
+                pos += 16
+    order = np.argsort(np.asarray(ri, dtype=np.int64), kind="stable")
+    return (np.asarray(ri, dtype=np.int64)[order], np.asarray(rv, dtype=np.uint16)[order])
+
+
+def encode_cdq(tensors: dict, n_states: int = 26) -> bytes:
+    """The .cdq bytes of ``tensors`` (see write_cdq)."""
+    assert n_states in (26, 16)
+    lib = L.lib()
+    n = C.c_int64()
+    L.check(lib.cdq_file_encode_header(n_states, len(tensors), None, 0, C.byref(n)), "encode header")
+    hdr = np.empty(n.value, dtype=np.uint8)
+    L.check(lib.cdq_file_encode_header(n_states, len(tensors), hdr.ctypes.data_as(C.c_void_p),
+                                       hdr.size, C.byref(n)), "encode header")
+    parts = [hdr.tobytes()]
+    for name, t in tensors.items():
+        rows, cols = int(t["rows"]), int(t["cols"])
+        q = _u8(t["q"] if "q" in t else t["quant_indices"])
+        sc = _u8(t["scales_f8_u8"] if "scales_f8_u8" in t else t["scales_f8"])
+        ri, rv = _flat_residuals(t)
+        args = (name.encode(), rows, cols, n_states, q.ctypes.data_as(C.c_void_p),
+                sc.ctypes.data_as(C.c_void_p),
+                ri.ctypes.data_as(C.c_void_p) if ri.size else None,
+                rv.ctypes.data_as(C.c_void_p) if rv.size else None, ri.size)
+        L.check(lib.cdq_file_encode_tensor(*args, None, 0, C.byref(n)), f"encode {name}")
+        buf = np.empty(n.value, dtype=np.uint8)
+        L.check(lib.cdq_file_encode_tensor(*args, buf.ctypes.data_as(C.c_void_p), buf.size,
+                                           C.byref(n)), f"encode {name}")
+        parts.append(buf.tobytes())
+    return b"".join(parts)
+
+
+def write_cdq(path, tensors: dict, n_states: int = 26) -> None:
+    """tensors: {name: dict(rows, cols, scales_f8_u8[N,1], q[N,32] u8,
+    tag_counts[N] u8, res_blobs[list])} as in code/cdq_pack.py:162-190, or
+    with residual_indices / residual_values in place of the per-tile blobs."""
+    data = encode_cdq(tensors, n_states)
+    with open(path, "wb") as f:
+        f.write(data)
+
+
+def scan_cdq(data: bytes) -> tuple[int, list]:
+    lib = L.lib()
+    buf = np.frombuffer(data, dtype=np.uint8)
+    ns, cnt = C.c_int32(), C.c_int32()
+    L.check(lib.cdq_file_scan(buf.ctypes.data_as(C.c_void_p), buf.size, C.byref(ns), None, 0,
+                              C.byref(cnt)), "cdq_file_scan")
+    tabs = (L.cdq_file_tensor * max(cnt.value, 1))()
+    L.check(lib.cdq_file_scan(buf.ctypes.data_as(C.c_void_p), buf.size, C.byref(ns), tabs,
+                              cnt.value, C.byref(cnt)), "cdq_file_scan")
+    return ns.value, [tabs[i] for i in range(cnt.value)]
+
+
+def decode_tensor(data: bytes, n_states: int, t) -> dict:
+    """One scanned tensor -> reference pack arrays (numpy)."""
+    buf = np.frombuffer(data, dtype=np.uint8)
+    q = np.empty((t.n_tiles, TILE), dtype=np.uint8)
+    sc = np.empty(t.n_tiles, dtype=np.uint8)
+    ri = np.empty(t.n_res, dtype=np.int64)
+    rv = np.empty(t.n_res, dtype=np.uint16)
+    L.check(L.lib().cdq_file_decode(
+        buf.ctypes.data_as(C.c_void_p), buf.size, n_states, C.byref(t),
+        q.ctypes.data_as(C.c_void_p), sc.ctypes.data_as(C.c_void_p),
+        ri.ctypes.data_as(C.c_void_p) if ri.size else None,
+        rv.ctypes.data_as(C.c_void_p) if rv.size else None), f"decode {t.name.decode()}")
+    return {"quant_indices": q, "scales_f8": sc, "residual_indices": ri, "residual_values": rv}
+
+
+def read_cdq(path) -> dict:
+    """code/cdq_pack.py:193-234: {name: {rows, cols, n_tiles, scales_f8_u8, q,
+    tag_counts, res_blobs, n_states}}."""
+    with open(path, "rb") as f:
+        data = f.read()
+    assert data[:4] == MAGIC, "bad magic"
+    (ver,) = struct.unpack_from("<H", data, 4)
+    assert ver in (VERSION, VERSION2), f"unsupported version {ver}"
+    n_states, tabs = scan_cdq(data)
+    ib = IDX_BYTES_PER_TILE if n_states == 26 else NIBBLE_BYTES_PER_TILE
+    out = {}
+    raw = np.frombuffer(data, dtype=np.uint8)
+    for t in tabs:
+        d = decode_tensor(data, n_states, t)
+        nt = int(t.n_tiles)
+        base = int(t.record_offset)
+        tags = raw[base + 1: base + 1 + 1]  # placeholder, rebuilt below
+        # walk the records once with numpy: record length = 2 + ib + blob
+        tc = np.bincount(d["residual_indices"] // TILE, minlength=nt).astype(np.int64)
+        blen = (tc * 21 + 7) // 8
+        roff = base + np.concatenate([[0], np.cumsum(2 + ib + blen)[:-1]])
+        boff = roff + 2 + ib
+        blobs = [bytes(data[o:o + n]) for o, n in zip(boff.tolist(), blen.tolist())]
+        tags = tc.astype(np.uint8)
+        out[t.name.decode()] = {
+            "rows": int(t.rows), "cols": int(t.cols), "n_tiles": nt,
+            "scales_f8_u8": torch.from_numpy(d["scales_f8"].reshape(nt, 1).copy()),
+            "q": torch.from_numpy(d["quant_indices"]),
+            "tag_counts": torch.from_numpy(tags),
+            "res_blobs": blobs,
+            "n_states": n_states,
+        }
+    return out
+
+
+def read_device_packs(path, device="cuda") -> dict[str, DevicePack]:
+    """Each tensor of a .cdq file straight to a device pack."""
+    with open(path, "rb") as f:
+        data = f.read()
+    n_states, tabs = scan_cdq(data)
+    out = {}
+    for t in tabs:
+        d = decode_tensor(data, n_states, t)
+        out[t.name.decode()] = DevicePack.from_reference(
+            d["quant_indices"], d["scales_f8"], d["residual_indices"], d["residual_values"],
+            int(t.rows), int(t.cols), n_states, device=device)
+    return out
+
+
+def dequant_tile(q32, scale_bf16, res_blob, tag_count, lattice=None):
+    """One tile -> 32 bf16 values (code/cdq_pack.py:237-248)."""
+    from .quant import CAMKII_LATTICE
+    lat = CAMKII_LATTICE if lattice is None else lattice
+    w = lat[torch.as_tensor(q32).long()].to(torch.bfloat16) * scale_bf16
+    if tag_count:
+        offs, vals = unpack_residuals(res_blob, int(tag_count))
+        w[offs.long()] = vals.to(torch.bfloat16)
+    return w
+
+
+def main():
+    import argparse
+    import os
+    import time
+    from .ops import quantize
+    ap = argparse.ArgumentParser(description="quantise a safetensors checkpoint to .cdq on the GPU")
+    ap.add_argument("--model", default=os.environ.get("CDQ_MODEL", "models/qwen-local"))
+    ap.add_argument("--out", default="qwen05.cdq")
+    ap.add_argument("--max-tensors", type=int, default=-1, help="-1 = all")
+    ap.add_argument("--states", type=int, choices=(26, 16), default=16)
+    ap.add_argument("--stc-frac", type=float, default=0.0156)
+    args = ap.parse_args()
+    from safetensors import safe_open
+    f = safe_open(os.path.join(args.model, "model.safetensors"), framework="pt")
+    keys = [k for k in f.keys() if k.endswith(".weight") and any(
+        s in k for s in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"))]
+    if args.max_tensors > 0:
+        keys = keys[:args.max_tensors]
+    print(f"lattice: {args.states}-state ({5 if args.states == 26 else 4}-bit indices)")
+    print(f"packing {len(keys)} tensors ...")
+    t0 = time.time()
+    tensors, tot_w, tot_res = {}, 0, 0
+    for k in keys:
+        w = f.get_tensor(k).to(torch.bfloat16).cuda()
+        pack, info = quantize(w, n_states=args.states, stc_frac=args.stc_frac)
+        ref = pack.to_reference()
+        rows, cols = w.shape
+        tensors[k] = {"rows": rows, "cols": cols, "q": ref["quant_indices"],
+                      "scales_f8_u8": ref["scales_f8"], "residual_indices": ref["residual_indices"],
+                      "residual_values": ref["residual_values"]}
+        tot_w += w.numel()
+        tot_res += info["n_res"]
+    write_cdq(args.out, tensors, n_states=args.states)
+    size = os.path.getsize(args.out)
+    print(f"wrote {args.out} ({size / 1e6:.1f} MB) in {time.time() - t0:.1f}s")
+    print(f"params={tot_w} residuals={tot_res} ({100 * tot_res / max(1, tot_w):.2f}%)")
+    print(f"on-disk = {size * 8 / max(1, tot_w):.3f} bpw")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,249 @@
+/*
+ * cdq.h - C ABI of the B200 (sm_100a) CDQ-LRR decode path.
+ *
+ * CDQ-LRR stores a projection weight [rows, cols] (cols % 32 == 0) as tiles of
+ * 32 consecutive weights of one row. Each tile keeps one float8 e4m3fn scale
+ * sigma = max|w|, one lattice index per weight (26-state lattice, 5 bits, or
+ * 16-state lattice, 4 bits) and, for the top fraction of weights by saliency,
+ * the original bf16 value (a "residual"). Decoding is
+ *     w_hat = bf16(LATTICE[q] * bf16(sigma)), residual positions take their value.
+ *
+ * Every function borrows raw pointers and never frees them. Device pointers
+ * are CUDA global memory of the current device; stream arguments are
+ * cudaStream_t passed as void*. All functions return a cdq_status (0 = OK).
+ * Kernels are enqueued asynchronously on the given stream unless the
+ * comment says otherwise. bf16 values travel as uint16_t bit patterns.
+ *
+ * Citations name the reference interface each entry point replaces
+ * (file:line within the CDQ-LRR project).
+ */
+#ifndef CDQ_B200_H
+#define CDQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CDQ_API __attribute__((visibility("default")))
+#else
+#define CDQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum cdq_status {
+    CDQ_OK = 0,
+    CDQ_ERR_SHAPE = 1,       /* cols % 32 != 0, a zero or oversized dimension   */
+    CDQ_ERR_STATES = 2,      /* lattice size other than 26 or 16               */
+    CDQ_ERR_ARG = 3,         /* null pointer or out-of-range argument          */
+    CDQ_ERR_CUDA = 4,        /* a CUDA runtime call or kernel launch failed     */
+    CDQ_ERR_FORMAT = 5,      /* malformed or truncated .cdq bytes              */
+    CDQ_ERR_CAPACITY = 6,    /* a caller buffer is too small                    */
+    CDQ_ERR_WORKSPACE = 7,   /* workspace missing or smaller than required     */
+    CDQ_ERR_UNSUPPORTED = 8  /* valid request this build cannot serve          */
+} cdq_status;
+
+/* Largest supported cols: residual entries store the column in 16 bits. */
+#define CDQ_MAX_COLS 65536
+#define CDQ_TILE 32
+#define CDQ_MAX_BATCH 8         /* cdq_linear serves M <= CDQ_MAX_BATCH      */
+
+/*
+ * Device layout of one packed weight ("device pack").
+ *
+ * Rows are grouped in row blocks of 32 (RB = ceil(rows/32)); a row block's
+ * tile column c (KT = cols/32 columns) holds the 32 tiles of its rows at c.
+ *   codes   : per (row block, tile column) 32 lanes x W words, W = 5 (26-state)
+ *             or 4 (16-state). Lane l is row 32*rb + l. Words 0..3 of all
+ *             lanes come first as 16-byte groups (lane l at byte 16*l), then
+ *             word 4 of all lanes (26-state only).
+ *             26-state: element pair j (weights 2j, 2j+1) has the code
+ *             s[2j]*27 + s[2j+1] in bits [10j, 10j+10) of the tile's 160-bit
+ *             little-endian word stream, with s = lattice index 0..25, or 26
+ *             at a residual position (contributes zero).
+ *             16-state: byte j = s[2j] | s[2j+1] << 4, residual positions
+ *             hold 7 (the lattice's exact zero).
+ *   scales  : float8 e4m3fn sigma codes, [RB][ceil(KT/4)][32 lanes][4 tiles].
+ *   res_ptr : residual CSR offsets, RB*KG*32 + 1 entries (KG = ceil(KT/32));
+ *             bucket (rb, g, l) lists row 32*rb+l, tile columns [32g, 32g+32).
+ *   res_ent : n_res words (col << 16) | bf16 bits, sorted by bucket then col.
+ *   res_q   : n_res lattice indices the quantizer chose at the residual
+ *             positions (read only by format conversion, never by cdq_linear).
+ * Padding rows of the last row block hold residual-slot codes and sigma 0.
+ */
+typedef struct cdq_packed {
+    int32_t rows;
+    int32_t cols;
+    int32_t n_states;      /* 26 or 16 */
+    int32_t reserved0;
+    int64_t n_res;         /* residual entries in res_ent / res_q */
+    uint32_t* codes;
+    uint8_t* scales;
+    uint32_t* res_ptr;
+    uint32_t* res_ent;
+    uint8_t* res_q;
+} cdq_packed;
+
+/* Byte and element counts of a device pack and of the workspaces. */
+typedef struct cdq_sizes {
+    int64_t row_blocks;        /* RB */
+    int64_t tile_cols;         /* KT */
+    int64_t res_groups;        /* KG */
+    int64_t codes_bytes;
+    int64_t scales_bytes;
+    int64_t res_ptr_count;     /* uint32 entries */
+    int64_t max_res;           /* upper bound on n_res from cdq_quantize: 2k */
+    int64_t linear_workspace_bytes;    /* per call of cdq_linear (zeroed once) */
+    int64_t quantize_workspace_bytes;
+} cdq_sizes;
+
+/* Sizes for a [rows, cols] weight, the given lattice and residual fraction
+ * (stc_frac only affects max_res). No CUDA calls. */
+CDQ_API cdq_status cdq_get_sizes(int32_t rows, int32_t cols, int32_t n_states, double stc_frac,
+                         int32_t max_batch, cdq_sizes* out);
+
+/* Library version string and the compiled device architecture. */
+CDQ_API const char* cdq_version(void);
+
+/*
+ * y[M, rows] = x[M, cols] * w_hat^T (+ bias), fused: the packed weight is
+ * streamed from HBM and dequantized in registers (bit-exact w_hat), FP32
+ * accumulation, result rounded once to bf16. M <= CDQ_MAX_BATCH.
+ * workspace: linear_workspace_bytes of device memory, zero-filled before the
+ * first call and left zero-filled by every call (split-K accumulators); calls
+ * that share one workspace must not overlap on the GPU.
+ * bias may be NULL. x, y, bias: bf16 bit patterns, row-major.
+ * Replaces CDQLinear.forward, code/cdq_lrr_qwen05.py:196-198, and the
+ * loader's CDQLinear.forward, code/cdq_loader.py:53-58.
+ */
+CDQ_API cdq_status cdq_linear(const cdq_packed* w, const uint16_t* x, int64_t m, uint16_t* y,
+                      const uint16_t* bias, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* As cdq_linear, output in float32 (no final bf16 rounding). */
+CDQ_API cdq_status cdq_linear_f32(const cdq_packed* w, const uint16_t* x, int64_t m, float* y,
+                          const uint16_t* bias, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* One GEMV of a grouped launch. */
+typedef struct cdq_gemv_job {
+    cdq_packed w;          /* by value */
+    const uint16_t* x;     /* [m, cols] bf16 */
+    void* y;               /* [m, rows] bf16 or float32 */
+    const uint16_t* bias;  /* NULL or [rows] */
+    void* workspace;       /* this job's linear workspace (distinct per job) */
+    int64_t workspace_bytes;
+    int32_t out_f32;       /* 0: bf16 y, 1: float32 y */
+    int32_t reserved0;
+} cdq_gemv_job;
+
+/*
+ * Runs n independent jobs (same batch m) in one launch: the work of all jobs
+ * is spread over every SM, which a decode step uses for the projections that
+ * share an input (q/k/v, gate/up) or that are otherwise independent.
+ * jobs: host array, copied by the call. No counterpart in the reference (it
+ * runs one projection per F.linear call, code/cdq_lrr_qwen05.py:198).
+ */
+CDQ_API cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, void* stream);
+
+/*
+ * Bit-exact w_hat [rows, cols] bf16 from a device pack.
+ * Replaces dequantize, code/cdq_lrr_qwen05.py:141-152, and
+ * CDQLinear.dequant_weight, code/cdq_lrr_qwen05.py:188-194.
+ */
+CDQ_API cdq_status cdq_dequant(const cdq_packed* w, uint16_t* w_hat, void* stream);
+
+/* Diagnostics of one cdq_quantize call, written to device memory. */
+typedef struct cdq_quant_info {
+    int64_t n_res;          /* residual count (<= max_res) */
+    int64_t k;              /* max(1, round(numel * stc_frac)) */
+    float threshold;        /* saliency quantile */
+    int32_t topk_fallback;  /* 1 if more than 2k weights reached the threshold */
+    int64_t mask_count;     /* weights with saliency >= threshold */
+} cdq_quant_info;
+
+/*
+ * GPU tile quantizer: bf16 weight [rows, cols] (device) -> device pack.
+ * Bit-exact with quantize_cdq_lrr, code/cdq_lrr_qwen05.py:63-133 (and its
+ * packer twin code/cdq_pack.py:283-305, which lacks the top-k tie guard):
+ * sigma = max|w| as float8 e4m3fn, unbiased float64-Welford tile variance,
+ * saliency |w|*(var+1e-6), linear quantile threshold at 1 - stc_frac,
+ * top-k fallback on severe ties (lowest flat indices win ties), nearest
+ * lattice centroid of w / sigma_q (first index on ties).
+ * out: buffers sized by cdq_get_sizes (res_ent / res_q hold max_res entries);
+ * out->n_res is not touched (read info->n_res). info: device memory.
+ * workspace: quantize_workspace_bytes of device memory (no zeroing needed).
+ */
+CDQ_API cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
+                        double stc_frac, cdq_packed* out, cdq_quant_info* info,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Host-side conversions between the reference's pack tensors and the device
+ * layout. All pointers are HOST memory; synchronous.
+ * Reference pack tensors (code/cdq_lrr_qwen05.py:121-133):
+ *   quant_indices uint8 [n_tiles, 32] (row-major tile order),
+ *   scales_f8 uint8 [n_tiles] (e4m3fn codes), residual_indices int64 [n_res]
+ *   (flat, ascending), residual_values uint16 [n_res] (bf16 bits).
+ * The loader (code/cdq_loader.py:94-105) holds the same data as q, the
+ * decoded scales, offs (= residual_indices) and vals.
+ */
+CDQ_API cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
+                                   const uint8_t* quant_indices, const uint8_t* scales_f8,
+                                   const int64_t* residual_indices,
+                                   const uint16_t* residual_values, int64_t n_res,
+                                   cdq_packed* out_host);
+
+CDQ_API cdq_status cdq_host_to_reference(const cdq_packed* in_host, uint8_t* quant_indices,
+                                 uint8_t* scales_f8, int64_t* residual_indices,
+                                 uint16_t* residual_values);
+
+/*
+ * .cdq file codec (host memory, synchronous), byte-exact with write_cdq /
+ * read_cdq, code/cdq_pack.py:162-234, and the loader's parser,
+ * code/cdq_loader.py:61-100. Layout: "CDQ1", u16 version (1: 26-state, 2:
+ * 16-state), u16 tensor count, bf16 lattice; per tensor u16 name length,
+ * name, u32 rows, u32 cols, u32 n_tiles; per tile u8 scale, u8 residual
+ * count, 20 or 16 index bytes, residual stream of ceil(21*count/8) bytes.
+ */
+typedef struct cdq_file_tensor {
+    char name[256];
+    int32_t rows;
+    int32_t cols;
+    int64_t n_tiles;
+    int64_t n_res;
+    int64_t record_offset;   /* byte offset of the first tile record */
+    int64_t record_bytes;    /* bytes of all tile records */
+} cdq_file_tensor;
+
+/* Parses the header and tensor table. *n_states gets 26 or 16. At most
+ * max_tensors entries are written; *n_tensors gets the file's count. */
+CDQ_API cdq_status cdq_file_scan(const uint8_t* data, int64_t len, int32_t* n_states,
+                         cdq_file_tensor* tensors, int32_t max_tensors, int32_t* n_tensors);
+
+/* Decodes one scanned tensor into reference pack tensors (sizes from t). */
+CDQ_API cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
+                           const cdq_file_tensor* t, uint8_t* quant_indices,
+                           uint8_t* scales_f8, int64_t* residual_indices,
+                           uint16_t* residual_values);
+
+/* Encodes the header (magic, version, count, lattice) into out (capacity
+ * cap); *written gets the byte count (8 + 52 or 8 + 32). */
+CDQ_API cdq_status cdq_file_encode_header(int32_t n_states, int32_t n_tensors, uint8_t* out,
+                                  int64_t cap, int64_t* written);
+
+/* Encodes one tensor (name, dims, tile records) from reference pack tensors.
+ * With out == NULL only *written (the required bytes) is computed. */
+CDQ_API cdq_status cdq_file_encode_tensor(const char* name, int32_t rows, int32_t cols,
+                                  int32_t n_states, const uint8_t* quant_indices,
+                                  const uint8_t* scales_f8, const int64_t* residual_indices,
+                                  const uint16_t* residual_values, int64_t n_res,
+                                  uint8_t* out, int64_t cap, int64_t* written);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CDQ_B200_H */

@@ -191,9 +191,13 @@ def quantile_linear(values: np.ndarray, q: float) -> np.float32:
 
     Used at code/cdq_lrr_qwen05.py:90 and code/cdq_pack.py:288. torch refuses
     inputs above 2**24 elements; beyond that size this restatement keeps the
-    same float32 rank rule, which is this implementation's convention.
+    same float32 rank rule, which is this implementation's convention. Any
+    NaN input makes the result NaN, as in torch (then no weight reaches the
+    threshold and the tensor keeps no residuals).
     """
     v = np.sort(np.asarray(values, dtype=np.float32).ravel())
+    if np.isnan(v[-1]):
+        return np.float32(np.nan)  # torch propagates NaN through quantile
     lo, hi, w = quantile_rank(v.size, q)
     return lerp_f32(v[lo], v[hi], w)
 

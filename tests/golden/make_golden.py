@@ -99,11 +99,20 @@ def weight_case(name: str) -> tuple[torch.Tensor, int, float]:
         w[:, 0] = 1.0
         w[:, 1:] = mids[torch.randint(0, 25, (32, 63), generator=g)]
         return w.to(torch.bfloat16), 26, 0.0156
+    if name == "nanweight":
+        w = synth_weight(8, 64, seed=19)
+        w[1, 3] = float("nan")
+        return w, 26, 0.0156
+    if name == "infweight":
+        w = synth_weight(8, 64, seed=20)
+        w[5, 60] = float("inf")
+        return w, 16, 0.0156
     raise KeyError(name)
 
 
 SMALL_CASES = ["small26", "small16", "rect26", "frac03125", "frac50", "onetile", "zeros",
-               "constant", "zerotiles", "tiny", "huge", "wide16", "mid26"]
+               "constant", "zerotiles", "tiny", "huge", "wide16", "mid26", "nanweight",
+               "infweight"]
 
 
 def lattice_of(n_states: int) -> torch.Tensor:

@@ -1,0 +1,210 @@
+"""GPU parity: every kernel through the C ABI against the oracle.
+
+* cdq_dequant: w_hat bit-exact (NaN compared as NaN) on every golden case;
+* cdq_quantize: indices, fp8 scales, residual indices and values bit-exact
+  with the reference's own outputs, including the [4864, 896] digests;
+* cdq_linear / cdq_linear_f32: fp32 output within 1e-3 relative (normwise
+  and per element against the fp64 dot of the oracle's w_hat); the bf16
+  output is the fp32 output rounded once;
+* cdq_linear_grouped: bit-identical to one launch per job.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cdq_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CASES = ["small26", "small16", "rect26", "frac03125", "frac50", "onetile", "zeros",
+         "constant", "zerotiles", "tiny", "huge", "wide16", "mid26", "nanweight", "infweight"]
+REL_TOL = 1e-3   # GEMV bar: fp32 accumulation vs the fp64 dot of the oracle's w_hat
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _nan_equal(a, b):
+    a = np.asarray(a, np.uint16)
+    b = np.asarray(b, np.uint16)
+    an = ((a & 0x7F80) == 0x7F80) & ((a & 0x7F) != 0)
+    bn = ((b & 0x7F80) == 0x7F80) & ((b & 0x7F) != 0)
+    return bool(np.array_equal(an, bn) and np.array_equal(a[~an], b[~bn]))
+
+
+def _digest(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def _dev_pack(golden, name, n_states):
+    from cdq_lrr_b200.ops import DevicePack
+    w = golden[f"{name}.weight"]
+    return DevicePack.from_reference(
+        golden[f"{name}.quant_indices"], golden[f"{name}.scales_f8"],
+        golden[f"{name}.residual_indices"], golden[f"{name}.residual_values"],
+        w.shape[0], w.shape[1], n_states, device="cuda")
+
+
+def _t(bits_u16: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits_u16).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def _check_gemv(y32: torch.Tensor, y64: np.ndarray):
+    y = y32.double().cpu().numpy()
+    fin = np.isfinite(y64)
+    assert np.array_equal(fin, np.isfinite(y)), "NaN/inf pattern differs"
+    if fin.any():
+        d = np.abs(y[fin] - y64[fin])
+        norm = np.linalg.norm(y64[fin])
+        assert np.linalg.norm(d) <= REL_TOL * max(norm, 1e-30), (np.linalg.norm(d), norm)
+        scale = np.sqrt(np.mean(y64[fin] ** 2)) + 1e-30
+        assert np.all(d <= REL_TOL * (np.abs(y64[fin]) + scale)), float(d.max())
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_dequant_bit_exact(golden, golden_meta, name):
+    from cdq_lrr_b200 import ops
+    ns = golden_meta["cases"][name]["n_states"]
+    dp = _dev_pack(golden, name, ns)
+    w_hat = ops.dequant(dp)
+    torch.cuda.synchronize()
+    assert _nan_equal(_bits(w_hat), golden[f"{name}.w_hat"])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_quantize_bit_exact(golden, golden_meta, name):
+    from cdq_lrr_b200 import ops
+    meta = golden_meta["cases"][name]
+    w = _t(golden[f"{name}.weight"])
+    pack, info = ops.quantize(w, n_states=meta["n_states"], stc_frac=meta["stc_frac"])
+    ref = pack.to_reference()
+    assert info["n_res"] == meta["outlier_count"]
+    assert np.array_equal(ref["quant_indices"], golden[f"{name}.quant_indices"])
+    assert np.array_equal(ref["scales_f8"], golden[f"{name}.scales_f8"])
+    assert np.array_equal(ref["residual_indices"], golden[f"{name}.residual_indices"])
+    assert np.array_equal(ref["residual_values"], golden[f"{name}.residual_values"])
+    p = O.quantize(golden[f"{name}.weight"], n_states=meta["n_states"], stc_frac=meta["stc_frac"])
+    assert info["topk_fallback"] == p["topk_fallback"]
+    if not np.isnan(p["threshold"]):
+        assert np.float32(info["threshold"]) == p["threshold"]
+
+
+@pytest.mark.parametrize("ns", [26, 16])
+def test_quantize_4864x896_digests(golden_meta, ns):
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_weight
+    d = golden_meta["digests"][f"cfg1_{ns}"]
+    w = synth_weight(4864, 896, std=0.02, seed=0)
+    assert _digest(_bits(w)) == d["weight"]
+    pack, info = ops.quantize(w.cuda(), n_states=ns)
+    ref = pack.to_reference()
+    assert info["n_res"] == d["outlier_count"]
+    assert _digest(ref["quant_indices"]) == d["quant_indices"]
+    assert _digest(ref["scales_f8"]) == d["scales_f8"]
+    assert _digest(ref["residual_indices"]) == d["residual_indices"]
+    assert _digest(ref["residual_values"]) == d["residual_values"]
+    assert _digest(_bits(ops.dequant(pack))) == d["w_hat"]
+
+
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_linear_against_oracle(golden, golden_meta, name, m):
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation
+    meta = golden_meta["cases"][name]
+    dp = _dev_pack(golden, name, meta["n_states"])
+    rows, cols = golden[f"{name}.weight"].shape
+    x = synth_activation(m, cols, seed=40 + m)
+    bias = golden[f"{name}.bias"]
+    y32 = ops.linear(dp, x.cuda(), _t(bias), out_f32=True)
+    y16 = ops.linear(dp, x.cuda(), _t(bias))
+    y64 = O.linear_f64(golden[f"{name}.w_hat"], _bits(x), bias)
+    _check_gemv(y32, y64)
+    # the bf16 output is the fp32 result rounded once (same kernel, same order)
+    assert _nan_equal(_bits(y16), O.f32_to_bf16_bits(y32.cpu().numpy()))
+
+
+@pytest.mark.parametrize("shape,ns", [((256, 4864), 26), ((64, 2080), 26), ((45, 96), 26),
+                                      ((33, 3104), 16), ((4864, 896), 26), ((896, 4864), 16)])
+@pytest.mark.parametrize("m", [1, 4])
+def test_linear_split_k_and_ragged(shape, ns, m):
+    """Several residual groups per row (split K through the workspace), rows
+    not a multiple of 32, a last group of one tile; repeated calls reuse the
+    self-resetting workspace and give identical results."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    rows, cols = shape
+    w = synth_weight(rows, cols, seed=rows + cols)
+    p = O.quantize(_bits(w), n_states=ns)
+    from cdq_lrr_b200.ops import DevicePack
+    dp = DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                   p["residual_values"], rows, cols, ns, device="cuda")
+    x = synth_activation(m, cols, seed=5).cuda()
+    y1 = ops.linear(dp, x, out_f32=True)
+    y2 = ops.linear(dp, x, out_f32=True)
+    assert torch.equal(y1, y2)
+    _check_gemv(y1, O.linear_f64(O.dequantize(p), _bits(x)))
+
+
+def test_linear_batch_above_8_splits():
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    w = synth_weight(128, 512, seed=9)
+    p = O.quantize(_bits(w))
+    dp = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                       p["residual_values"], 128, 512, 26, device="cuda")
+    x = synth_activation(19, 512, seed=2).cuda()
+    y = ops.linear(dp, x, out_f32=True)
+    _check_gemv(y, O.linear_f64(O.dequantize(p), _bits(x)))
+
+
+def test_grouped_equals_single_launches():
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    shapes = [(896, 896, 26), (128, 896, 26), (4864, 896, 26), (896, 4864, 26), (96, 320, 16),
+              (40, 2080, 16)]
+    tasks, singles = [], []
+    for i, (r, c, ns) in enumerate(shapes):
+        w = synth_weight(r, c, seed=100 + i).cuda()
+        pack, _ = ops.quantize(w, n_states=ns)
+        for m in (1,):
+            x = synth_activation(m, c, seed=200 + i).cuda()
+            y = torch.empty(m, r, dtype=torch.float32, device="cuda")
+            tasks.append(ops.GemvTask(pack, x, y))
+            singles.append(ops.linear(pack, x, out_f32=True))
+    ops.linear_grouped(tasks, 1)
+    torch.cuda.synchronize()
+    for t, s in zip(tasks, singles):
+        assert torch.equal(t.y, s)
+
+
+def test_large_projection_properties():
+    """[18944, 3584] (a 7B MLP projection, 67.9 M weights: beyond torch.quantile's
+    limit, so no oracle run): quantizer invariants and GEMV vs the dequantized
+    weight in fp64."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    rows, cols = 18944, 3584
+    w = synth_weight(rows, cols, std=0.015, seed=7, device="cuda")
+    pack, info = ops.quantize(w, n_states=26)
+    k = int(round(rows * cols * 0.0156))
+    assert not info["topk_fallback"]
+    assert abs(info["n_res"] - k) <= max(2, k // 1000)
+    w_hat = ops.dequant(pack)
+    # residual positions hold the original weights exactly
+    ent = pack.res_ent[: pack.n_res].long() & 0xFFFFFFFF
+    rp = pack.res_ptr.long()
+    counts = rp[1:] - rp[:-1]
+    kg = (cols // 32 + 31) // 32
+    b = torch.arange(counts.numel(), device="cuda")
+    row_of = torch.repeat_interleave((b // (kg * 32)) * 32 + (b % 32), counts)
+    col = ent >> 16
+    assert torch.equal(w_hat[row_of, col], w[row_of, col])
+    # every non-residual weight is within half a lattice gap of sigma-scaled value
+    x = synth_activation(2, cols, seed=3, device="cuda")
+    y = ops.linear(pack, x, out_f32=True)
+    y64 = (x.double() @ w_hat.double().T).cpu().numpy()
+    _check_gemv(y, y64)

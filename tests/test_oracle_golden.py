@@ -15,7 +15,7 @@ from oracle import cdq_oracle as O
 from cdq_lrr_b200.synth import synth_activation, synth_weight
 
 CASES = ["small26", "small16", "rect26", "frac03125", "frac50", "onetile", "zeros",
-         "constant", "zerotiles", "tiny", "huge", "wide16", "mid26"]
+         "constant", "zerotiles", "tiny", "huge", "wide16", "mid26", "nanweight", "infweight"]
 
 
 def _nan_equal_bf16(a, b):
