@@ -64,6 +64,7 @@ _SIGS = {
     "cdq_version": (C.c_char_p, []),
     "cdq_linear": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P, C.c_size_t, _P]),
     "cdq_linear_f32": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P, C.c_size_t, _P]),
+    "cdq_linear_noalloc": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P]),
     "cdq_linear_grouped": (C.c_int, [C.POINTER(cdq_gemv_job), C.c_int32, C.c_int64, _P]),
     "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,

@@ -346,3 +346,108 @@ cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cud
 }
 
 }  // namespace cdq
+
+// ---------------------------------------------------------------------------
+// cdq_linear_noalloc: the fused linear for callers that cannot allocate device
+// memory. Its split-K scratch (per-group partial sums and per-row-block arrival
+// counters, the same layout as cdq_linear's workspace) lives in the file-scope
+// array below, which every GPU that loads this library holds until the process
+// exits. Host code never touches the array by name: the array's host-side
+// symbol is only a stand-in, so set-up asks the runtime for its device address
+// once per device (with that device current) and passes that address on.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#define CDQ_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)  // 4 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CDQ_NOALLOC_SCRATCH_BYTES];
+
+namespace cdq {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = CDQ_NOALLOC_SCRATCH_BYTES;
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[128] = {};
+int g_noalloc_sms[128] = {};
+
+// Once per device: lattice tables, SM count and the scratch's device address.
+cdq_status noalloc_setup(void** scratch, int* sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return CDQ_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        if (upload_lattices() != cudaSuccess) return CDQ_ERR_CUDA;
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return CDQ_ERR_CUDA;
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+            return CDQ_ERR_CUDA;
+        g_noalloc_sms[dev] = n;
+        g_noalloc_ptr[dev] = p;
+    }
+    *scratch = g_noalloc_ptr[dev];
+    *sms = g_noalloc_sms[dev];
+    return CDQ_OK;
+}
+
+inline int64_t al256(int64_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace cdq
+
+extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x, int64_t m,
+                                         uint16_t* y, const uint16_t* bias, void* stream) {
+    using namespace cdq;
+    if (!w) return CDQ_ERR_ARG;
+    if (w->n_states != 26 && w->n_states != 16) return CDQ_ERR_STATES;
+    if (w->rows <= 0 || w->cols <= 0 || w->cols % 32 || w->cols > CDQ_MAX_COLS) return CDQ_ERR_SHAPE;
+    if (!w->codes || !w->scales || !w->res_ptr || (w->n_res > 0 && !w->res_ent)) return CDQ_ERR_ARG;
+    if (m < 1 || m > CDQ_MAX_BATCH || !x || !y) return CDQ_ERR_ARG;
+    if ((uintptr_t)w->codes % 16 || (uintptr_t)w->scales % 4 || (uintptr_t)w->res_ptr % 4 ||
+        (uintptr_t)x % 16 || (uintptr_t)y % 2 || (bias && (uintptr_t)bias % 2))
+        return CDQ_ERR_ARG;
+    const Geometry g = geometry(w->rows, w->cols, w->n_states);
+    const int64_t slots = al256(m * g.kg * g.rb * 32 * 4);
+    const int64_t need = slots + al256(g.rb * 4);
+    if (g.kg > 1 && need > (int64_t)kNoAllocScratchBytes) return CDQ_ERR_WORKSPACE;
+
+    void* scratch = nullptr;
+    int sms = 0;
+    cdq_status st = noalloc_setup(&scratch, &sms);
+    if (st) return st;
+
+    GemvBatch<1> b;
+    b.n = 1;
+    b.pad_ = 0;
+    GemvJob& J = b.jobs[0];
+    J.codes = w->codes;
+    J.scales = w->scales;
+    J.res_ptr = w->res_ptr;
+    J.res_ent = w->res_ent;
+    J.x = x;
+    J.y = y;
+    J.bias = bias;
+    J.rows = w->rows;
+    J.cols = w->cols;
+    J.rb = (int32_t)g.rb;
+    J.kt = (int32_t)g.kt;
+    J.kt4 = (int32_t)g.kt4;
+    J.kg = (int32_t)g.kg;
+    J.out_f32 = 0;
+    J.pad_ = 0;
+    J.item_begin = 0;
+    J.partial = nullptr;
+    J.counters = nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (g.kg > 1) {
+        unsigned char* base = static_cast<unsigned char*>(scratch);
+        J.partial = reinterpret_cast<float*>(base);
+        J.counters = reinterpret_cast<uint32_t*>(base + slots);
+        // the array keeps the previous call's contents: the arrival counters
+        // must start at zero (the partial slots are written before they are read)
+        if (cudaMemsetAsync(J.counters, 0, (size_t)g.rb * 4, s) != cudaSuccess) return CDQ_ERR_CUDA;
+    }
+    b.total_items = (int64_t)J.rb * J.kg;
+    return gemv_launch_single(b, w->n_states, (int)m, s, sms) == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}

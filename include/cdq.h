@@ -127,6 +127,24 @@ CDQ_API cdq_status cdq_linear_f32(const cdq_packed* w, const uint16_t* x, int64_
                           const uint16_t* bias, void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/*
+ * As cdq_linear (bf16 output), for callers that cannot allocate device
+ * memory: a plugin whose host process owns all device memory through its own
+ * pool, or a path where a cudaMalloc, which may synchronise the device, is
+ * not allowed. It allocates nothing and takes no workspace: its split-K
+ * scratch is a 4 MiB array that the library holds on every GPU that loads it,
+ * until the process exits. Weights whose scratch would exceed 4 MiB
+ * (m * ceil(cols/1024) * ceil(rows/32) * 128 bytes, plus 4 bytes per 32 rows;
+ * only weights with cols > 1024 use scratch) are rejected with
+ * CDQ_ERR_WORKSPACE. All calls share the one array: calls that overlap on the
+ * GPU race, so issue them on one stream. The first call on a device sets up
+ * the scratch address and lattice tables (host-side runtime calls); make it
+ * before any stream capture.
+ * No counterpart in the reference.
+ */
+CDQ_API cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x, int64_t m,
+                                      uint16_t* y, const uint16_t* bias, void* stream);
+
 /* One GEMV of a grouped launch. */
 typedef struct cdq_gemv_job {
     cdq_packed w;          /* by value */
