@@ -55,6 +55,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--packs", choices=("quantized", "random"), default="quantized",
+                    help="quantized: weights quantised by the GPU quantizer (the benchmark); "
+                         "random: seeded random valid packs built on the host, so that the "
+                         "only kernels of the run are the GEMV's (profiling)")
     return ap.parse_args()
 
 
@@ -231,6 +235,22 @@ def cpu_baseline(seconds: float, use_product_quantizer_packs=None) -> dict:
 # ------------------------------------------------------------------- our arm
 
 
+def random_pack(rows: int, cols: int, seed: int, device, stc_frac: float = 0.0156):
+    """A valid 26-state pack with seeded random symbols, fp8 scales in
+    [2^-6, 2^-2) and round(stc_frac * numel) residuals at random positions,
+    laid out on the host (no kernel launches)."""
+    import numpy as np
+    from cdq_lrr_b200 import ops
+    rng = np.random.default_rng(seed)
+    n = rows * cols
+    q = rng.integers(0, 26, (n // 32, 32), dtype=np.uint8)
+    scales = rng.integers(0x08, 0x28, n // 32, dtype=np.uint8)
+    k = int(round(n * stc_frac))
+    ridx = np.sort(rng.choice(n, k, replace=False)).astype(np.int64)
+    rval = rng.integers(0x3C00, 0x3F00, k, dtype=np.uint16)
+    return ops.DevicePack.from_reference(q, scales, ridx, rval, rows, cols, 26, device=device)
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -238,6 +258,8 @@ def run_ours(args) -> None:
     from cdq_lrr_b200.synth import synth_activation, synth_weight
 
     ws_, rank, local = dist_setup(args.gpus)
+    kernel_name = ("gemv_kernel<26,1,192> (bulk-copy quad ring + mma.sync) then fixup_kernel<1,192>; "
+                   "one grouped launch pair per step")
     dev = torch.device("cuda", torch.cuda.current_device())
 
     # weights: generated and quantised on the GPU, one at a time
@@ -245,9 +267,12 @@ def run_ours(args) -> None:
     alg_bytes = 0
     packed_bytes = 0
     for i, (name, rows, cols) in enumerate(layer_list()):
-        w = synth_weight(rows, cols, std=0.02, seed=i, device=dev)
-        pack, info = ops.quantize(w, n_states=26, stc_frac=0.0156)
-        del w
+        if args.packs == "random":
+            pack = random_pack(rows, cols, seed=i, device=dev)
+        else:
+            w = synth_weight(rows, cols, std=0.02, seed=i, device=dev)
+            pack, info = ops.quantize(w, n_states=26, stc_frac=0.0156)
+            del w
         x = synth_activation(1, cols, seed=10000 + i, device=dev)
         y = torch.empty(1, rows, dtype=torch.bfloat16, device=dev)
         tasks.append(ops.GemvTask(pack, x, y))
@@ -350,14 +375,15 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws_,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random-init weights and activations)",
+            "data": ("synthetic (seeded random-init weights and activations)" if args.packs == "quantized"
+                     else "synthetic (seeded random packs, profiling mode)"),
             "config": {**workload_config(), "packed_mb_reference_format": round(alg_bytes / 1e6, 2),
                        "packed_mb_device_layout": round(packed_bytes / 1e6, 2),
                        "parallelism": f"replicas x{ws_}" if ws_ > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(kernel_gbs / peak, 4),
                          "peak_kind": f"of {peak_kind}", "traffic": traffic,
-                         "kernel": "cdq gemv_kernel<26,1,192> (one grouped launch per step)"},
+                         "kernel": kernel_name},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": int(xs_host.numel() * 2),
                     "d2h_bytes_per_step": int(ys_host.numel() * 2),

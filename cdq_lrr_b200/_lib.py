@@ -19,6 +19,7 @@ STATUS = {
 }
 MAX_BATCH = 8
 MAX_COLS = 65536
+MAX_JOBS = 192  # jobs per grouped launch (the launch record fits the kernel-parameter space)
 
 
 class CdqError(RuntimeError):
@@ -30,13 +31,13 @@ class CdqError(RuntimeError):
 class cdq_packed(C.Structure):
     _fields_ = [("rows", C.c_int32), ("cols", C.c_int32), ("n_states", C.c_int32),
                 ("reserved0", C.c_int32), ("n_res", C.c_int64),
-                ("codes", C.c_void_p), ("scales", C.c_void_p), ("res_ptr", C.c_void_p),
+                ("units", C.c_void_p), ("res_ptr", C.c_void_p),
                 ("res_ent", C.c_void_p), ("res_q", C.c_void_p)]
 
 
 class cdq_sizes(C.Structure):
     _fields_ = [(n, C.c_int64) for n in (
-        "row_blocks", "tile_cols", "res_groups", "codes_bytes", "scales_bytes", "res_ptr_count",
+        "row_blocks", "tile_pairs", "res_groups", "units_bytes", "res_ptr_count",
         "max_res", "linear_workspace_bytes", "quantize_workspace_bytes")]
 
 

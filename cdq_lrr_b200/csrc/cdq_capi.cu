@@ -39,19 +39,15 @@ cdq_status device_setup(int* sms) {
 }
 
 inline bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+inline int64_t al256(int64_t b) { return (b + 255) / 256 * 256; }
 
 cdq_status check_pack(const cdq_packed* w) {
     if (!w) return CDQ_ERR_ARG;
     if (w->n_states != 26 && w->n_states != 16) return CDQ_ERR_STATES;
     if (w->rows <= 0 || w->cols <= 0 || w->cols % 32 || w->cols > CDQ_MAX_COLS) return CDQ_ERR_SHAPE;
-    if (!w->codes || !w->scales || !w->res_ptr || (w->n_res > 0 && !w->res_ent)) return CDQ_ERR_ARG;
-    if (!aligned(w->codes, 16) || !aligned(w->scales, 4) || !aligned(w->res_ptr, 4)) return CDQ_ERR_ARG;
+    if (!w->units || !w->res_ptr || (w->n_res > 0 && !w->res_ent)) return CDQ_ERR_ARG;
+    if (!aligned(w->units, 16) || !aligned(w->res_ptr, 4)) return CDQ_ERR_ARG;
     return CDQ_OK;
-}
-
-int64_t linear_ws_bytes(const Geometry& g, int64_t m) {
-    auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
-    return al(m * g.kg * g.rb * 32 * 4) + al(g.rb * 4);
 }
 
 cdq_status fill_job(const cdq_packed* w, const uint16_t* x, int64_t m, void* y, int out_f32,
@@ -62,8 +58,7 @@ cdq_status fill_job(const cdq_packed* w, const uint16_t* x, int64_t m, void* y, 
     if (!x || !y || !aligned(x, 16) || !aligned(y, out_f32 ? 4 : 2) || (bias && !aligned(bias, 2)))
         return CDQ_ERR_ARG;
     const Geometry g = geometry(w->rows, w->cols, w->n_states);
-    J->codes = w->codes;
-    J->scales = w->scales;
+    J->units = w->units;
     J->res_ptr = w->res_ptr;
     J->res_ent = w->res_ent;
     J->x = x;
@@ -71,23 +66,19 @@ cdq_status fill_job(const cdq_packed* w, const uint16_t* x, int64_t m, void* y, 
     J->bias = bias;
     J->rows = w->rows;
     J->cols = w->cols;
-    J->rb = (int32_t)g.rb;
+    J->r16 = (int32_t)g.r16;
     J->kt = (int32_t)g.kt;
-    J->kt4 = (int32_t)g.kt4;
+    J->kp = (int32_t)g.kp;
     J->kg = (int32_t)g.kg;
     J->out_f32 = out_f32;
-    J->pad_ = 0;
-    J->partial = nullptr;
-    J->counters = nullptr;
-    if (g.kg > 1) {
-        // split K over residual groups needs the caller's workspace
-        const int64_t need = linear_ws_bytes(g, m);
-        if (!ws || (int64_t)ws_bytes < need || !aligned(ws, 256)) return CDQ_ERR_WORKSPACE;
-        auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
-        J->partial = reinterpret_cast<float*>(ws);
-        J->counters = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(ws) +
-                                                  al(m * g.kg * g.rb * 32 * 4));
-    }
+    J->n_res = (uint32_t)w->n_res;
+    J->reserved_ptr = nullptr;
+    J->rb_begin = 0;
+    J->reserved0 = 0;
+    // the per-group partial sums of the streaming pass live in the caller's workspace
+    const int64_t need = linear_workspace_need(g, m);
+    if (!ws || (int64_t)ws_bytes < need || !aligned(ws, 256)) return CDQ_ERR_WORKSPACE;
+    J->partial = reinterpret_cast<float*>(ws);
     return CDQ_OK;
 }
 
@@ -98,11 +89,11 @@ cdq_status linear_common(const cdq_packed* w, const uint16_t* x, int64_t m, void
     if (st) return st;
     GemvBatch<1> b;
     b.n = 1;
-    b.pad_ = 0;
     st = fill_job(w, x, m, y, out_f32, bias, ws, ws_bytes, &b.jobs[0]);
     if (st) return st;
     b.jobs[0].item_begin = 0;
-    b.total_items = (int64_t)b.jobs[0].rb * b.jobs[0].kg;
+    b.total_items = (int64_t)b.jobs[0].r16 * b.jobs[0].kg;
+    b.total_row_blocks = b.jobs[0].r16;
     cudaError_t e = gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms);
     return e == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }
@@ -128,18 +119,17 @@ cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, vo
     int sms = 0;
     cdq_status st = device_setup(&sms);
     if (st) return st;
+    for (int i = 0; i < n; ++i)
+        if (jobs[i].w.n_states != 26 && jobs[i].w.n_states != 16) return CDQ_ERR_STATES;
     // one launch per lattice size, at most kMaxJobs jobs each
     for (int ns : {26, 16}) {
         std::vector<int> idx;
         for (int i = 0; i < n; ++i)
             if (jobs[i].w.n_states == ns) idx.push_back(i);
-            else if (jobs[i].w.n_states != 26 && jobs[i].w.n_states != 16) return CDQ_ERR_STATES;
         for (size_t s0 = 0; s0 < idx.size(); s0 += kMaxJobs) {
-            auto* b = new GemvBatch<kMaxJobs>;
-            std::unique_ptr<GemvBatch<kMaxJobs>> guard(b);
+            std::unique_ptr<GemvBatch<kMaxJobs>> b(new GemvBatch<kMaxJobs>);
             b->n = 0;
-            b->pad_ = 0;
-            int64_t items = 0;
+            int64_t items = 0, blocks = 0;
             for (size_t s1 = s0; s1 < std::min(idx.size(), s0 + (size_t)kMaxJobs); ++s1) {
                 const cdq_gemv_job& jb = jobs[idx[s1]];
                 GemvJob& J = b->jobs[b->n];
@@ -147,10 +137,14 @@ cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, vo
                               (size_t)std::max<int64_t>(0, jb.workspace_bytes), &J);
                 if (st) return st;
                 J.item_begin = items;
-                items += (int64_t)J.rb * J.kg;
+                J.rb_begin = (int32_t)blocks;
+                items += (int64_t)J.r16 * J.kg;
+                blocks += J.r16;
                 b->n++;
+                if (items >= INT32_MAX || blocks >= INT32_MAX) return CDQ_ERR_SHAPE;
             }
             b->total_items = items;
+            b->total_row_blocks = (int32_t)blocks;
             cudaError_t e = gemv_launch_grouped(*b, ns, (int)m, (cudaStream_t)stream, sms);
             if (e != cudaSuccess) return CDQ_ERR_CUDA;
         }
@@ -178,9 +172,9 @@ cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n
     cdq_sizes sz;
     st = cdq_get_sizes(rows, cols, n_states, stc_frac, 1, &sz);
     if (st) return st;
-    if (!w || !aligned(w, 16) || !out || !info || !out->codes || !out->scales || !out->res_ptr ||
-        !out->res_ent || !out->res_q || !aligned(out->codes, 16) || !aligned(out->scales, 4) ||
-        !aligned(out->res_ptr, 4) || !aligned(out->res_ent, 4) || !aligned(info, 8))
+    if (!w || !aligned(w, 16) || !out || !info || !out->units || !out->res_ptr || !out->res_ent ||
+        !out->res_q || !aligned(out->units, 16) || !aligned(out->res_ptr, 4) ||
+        !aligned(out->res_ent, 4) || !aligned(info, 8))
         return CDQ_ERR_ARG;
     if (!workspace || (int64_t)workspace_bytes < sz.quantize_workspace_bytes ||
         !aligned(workspace, 256))

@@ -1,4 +1,5 @@
-// Shared constants and number-format helpers of the CDQ-LRR B200 library.
+// Shared constants, number-format helpers and the device-pack geometry of the
+// CDQ-LRR B200 library.
 //
 // Lattices: the bf16 bit patterns of CAMKII_LATTICE (26 states,
 // code/cdq_lrr_qwen05.py:27-32) and CAMKII_LATTICE_16 (16 states, zero at
@@ -6,6 +7,34 @@
 // Float8 e4m3fn: round to nearest even, NaN at 0x7F/0xFF, no infinities;
 // magnitudes that round to 480 or beyond become NaN (torch's conversion used
 // at code/cdq_lrr_qwen05.py:52 and :117).
+//
+// Device pack geometry ("fragment units" in "quads"). Rows are grouped in
+// blocks of 16 (R16 = ceil(rows/16)), tile columns (32 weights of a row) in
+// pairs (KP = ceil(KT/2), KT = cols/32). One unit = (16-row block, tile-column
+// pair) = 32 tiles = 640 code bytes + 32 scale bytes (26 states) or 512 + 32
+// (16 states). Units of a row block are stored in quads of four consecutive
+// units (the last quad of a row block holds KP mod 4 units when that is not
+// zero); a quad of u units, starting at byte (b16 * KP + 4 * quad) * unit, is
+//   [0, 512u)           unit i, lane l: code words 0..3 (uint4 at 512i + 16l)
+//   [512u, 640u)        26 states: code word 4 of unit i, lane l at 4(u*l + i)
+//                       from the start of this part (lane-major)
+//   next 32u bytes      scale half-words: lane pair k = l >> 1, unit i at
+//                       2(u*k + i): fp8 codes (row g, tile t), (row g+8, tile t)
+// so a full quad is read with four 16-byte loads per lane for the code words,
+// one 16-byte load for the four fifth words and one 8-byte load for the four
+// scale half-words.
+// Lane l = 4g + c holds the 16 pair codes of the m16n8k16 A fragments of rows
+// g and g+8 of the block over the unit's columns 16c .. 16c+15 (all in tile
+// t = c>>1): slot q = 4s + i (s = k16 slice, i = h + 2j) is row g + 8h,
+// unit columns 16c + 4s + 2j and +1, i.e. element pair p = 8(c&1) + 2s + j
+// of tile t. The k order inside a slice is permuted so that a lane's
+// activation operands are 16 contiguous columns (two 16-byte loads).
+// A pair code covers weights 2p, 2p+1 of the tile:
+// 26 states -> s[2p]*27 + s[2p+1] (10 bits, symbol 26 = residual slot, value
+// zero) at bits [10q, 10q+10) of the lane's 160-bit word stream; 16 states ->
+// byte q = s[2p] | s[2p+1] << 4 (residual slots use index 7, the exact zero).
+// A phantom tile (odd KT) and rows beyond `rows` hold residual slots, scale 0.
+// Residual CSR buckets: (16-row block, group of 32 tile columns, row 0..15).
 #pragma once
 
 #include <stdint.h>
@@ -21,7 +50,8 @@
 namespace cdq {
 
 constexpr int kTile = 32;
-constexpr int kGroupTiles = 32;      // residual CSR group: 32 tile columns
+constexpr int kGroupTiles = 32;      // residual CSR group: 32 tile columns (16 pairs)
+constexpr int kGroupPairs = 16;
 constexpr int kResidualSym26 = 26;   // 26-state pair-code symbol of a residual slot
 constexpr int kResidualSym16 = 7;    // 16-state: the lattice's exact zero
 constexpr int kPairs26 = 27 * 27;    // 729 pair codes (26 states + residual slot)
@@ -92,36 +122,72 @@ CDQ_HD uint16_t fp8_to_bf16(uint8_t c) {
     return (uint16_t)(s | (exp << 7) | mant);
 }
 
-// ---- device pack geometry (see include/cdq.h) ----
+// ---- device pack geometry ----
 struct Geometry {
-    int64_t rows, cols, rb, kt, kt4, kg;
-    int words;  // code words per tile: 5 (26-state) or 4 (16-state)
+    int64_t rows, cols, kt, r16, kp, kg;
+    int words;        // code words per lane: 5 (26 states) or 4 (16 states)
+    int64_t unit;     // bytes per unit: 672 or 544
+    int64_t sig_off;  // code bytes per unit: 640 or 512
 };
 
 CDQ_HD Geometry geometry(int64_t rows, int64_t cols, int n_states) {
     Geometry g;
     g.rows = rows;
     g.cols = cols;
-    g.rb = (rows + 31) / 32;
     g.kt = cols / 32;
-    g.kt4 = (g.kt + 3) / 4;
+    g.r16 = (rows + 15) / 16;
+    g.kp = (g.kt + 1) / 2;
     g.kg = (g.kt + kGroupTiles - 1) / kGroupTiles;
     g.words = n_states == 26 ? 5 : 4;
+    g.sig_off = n_states == 26 ? 640 : 512;
+    g.unit = g.sig_off + 32;
     return g;
 }
 
-// Word index (uint32 units) of word wd of lane l in tile column (rb, c).
-CDQ_HD int64_t code_word_index(const Geometry& g, int64_t rb, int64_t c, int lane, int wd) {
-    int64_t base = (rb * g.kt + c) * (int64_t)(g.words * 32);
-    return wd < 4 ? base + lane * 4 + wd : base + 128 + lane;
+// Quad holding unit (b16, cp): byte offset of the quad, its unit count u and
+// the unit's index i inside it.
+CDQ_HD int64_t quad_base(const Geometry& g, int64_t b16, int64_t cp, int* u, int* i) {
+    const int64_t q = cp >> 2;
+    const int64_t left = g.kp - 4 * q;
+    *u = (int)(left < 4 ? left : 4);
+    *i = (int)(cp & 3);
+    return (b16 * g.kp + 4 * q) * g.unit;
 }
 
-CDQ_HD int64_t scale_index(const Geometry& g, int64_t rb, int64_t c, int lane) {
-    return ((rb * g.kt4 + c / 4) * 32 + lane) * 4 + (c & 3);
+// Byte offset (in the units buffer) of code word wd of lane l of unit (b16, cp).
+CDQ_HD int64_t word_offset(const Geometry& g, int64_t b16, int64_t cp, int lane, int wd) {
+    int u, i;
+    const int64_t base = quad_base(g, b16, cp, &u, &i);
+    return wd < 4 ? base + 512 * i + 16 * lane + 4 * wd : base + 512 * u + 4 * (u * lane + i);
 }
 
-CDQ_HD int64_t bucket_index(const Geometry& g, int64_t rb, int64_t grp, int lane) {
-    return (rb * g.kg + grp) * 32 + lane;
+// (row within block ri, tile of the pair t, element pair p of the tile)
+// -> (lane, slot)
+CDQ_HD void slot_of(int ri, int t, int p, int* lane, int* slot) {
+    const int g = ri & 7, h = ri >> 3, c = 2 * t + (p >> 3), s = (p >> 1) & 3, j = p & 1;
+    *lane = 4 * g + c;
+    *slot = 4 * s + (h | (j << 1));
+}
+
+// (lane, slot) -> (row within block, tile of the pair, element pair)
+CDQ_HD void slot_pos(int lane, int slot, int* ri, int* t, int* p) {
+    const int g = lane >> 2, c = lane & 3, s = slot >> 2, i = slot & 3;
+    *t = c >> 1;
+    *ri = g + 8 * (i & 1);
+    *p = 8 * (c & 1) + 2 * s + (i >> 1);
+}
+
+// Byte offset (in the units buffer) of the scale of (row within block ri,
+// tile t) of unit (b16, cp).
+CDQ_HD int64_t scale_offset(const Geometry& g, int64_t b16, int64_t cp, int ri, int t) {
+    int u, i;
+    const int64_t base = quad_base(g, b16, cp, &u, &i);
+    const int k = 2 * (ri & 7) + t;
+    return base + g.sig_off * u + 2 * (u * k + i) + (ri >> 3);
+}
+
+CDQ_HD int64_t bucket_index(const Geometry& g, int64_t r16, int64_t grp, int ri) {
+    return (r16 * g.kg + grp) * 16 + ri;
 }
 
 }  // namespace cdq

@@ -18,43 +18,43 @@ namespace {
 __constant__ uint16_t d_lat26[26];
 __constant__ uint16_t d_lat16[16];
 
+// One thread per (unit, lane): its 16 element pairs.
 template <int NS>
-__global__ void dequant_tiles(const uint32_t* __restrict__ codes, const uint8_t* __restrict__ scales,
-                              int32_t rows, int32_t cols, uint16_t* __restrict__ out) {
+__global__ void dequant_units(const uint8_t* __restrict__ units, int32_t rows, int32_t cols,
+                              uint16_t* __restrict__ out) {
     const Geometry g = geometry(rows, cols, NS);
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t total = g.rb * g.kt * 32;
-    if (tid >= total) return;
+    if (tid >= g.r16 * g.kp * 32) return;
     const int lane = (int)(tid & 31);
-    const int64_t tc = tid >> 5;  // rb * kt + c
-    const int64_t rb = tc / g.kt, c = tc % g.kt;
-    const int64_t row = rb * 32 + lane;
-    if (row >= rows) return;
-    uint32_t w[5];
-    for (int wd = 0; wd < g.words; ++wd) w[wd] = codes[code_word_index(g, rb, c, lane, wd)];
-    const float sig = bf16_to_f32(fp8_to_bf16(scales[scale_index(g, rb, c, lane)]));
-    uint32_t packed[16];
-    for (int j = 0; j < 16; ++j) {
+    const int64_t un = tid >> 5, b16 = un / g.kp, cp = un % g.kp;
+    uint32_t w[5] = {0, 0, 0, 0, 0};
+    for (int wd = 0; wd < g.words; ++wd)
+        w[wd] = *reinterpret_cast<const uint32_t*>(units + word_offset(g, b16, cp, lane, wd));
+    for (int q = 0; q < 16; ++q) {
+        int ri, t, p;
+        slot_pos(lane, q, &ri, &t, &p);
+        const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+        if (row >= rows || c >= g.kt) continue;
         uint32_t a, b;
         if (NS == 26) {
-            const int bit = 10 * j, wd = bit >> 5, off = bit & 31;
-            uint32_t code = (off <= 22 ? (w[wd] >> off) : __funnelshift_r(w[wd], w[wd + 1], off)) & 0x3FFu;
+            const int bit = 10 * q, wd = bit >> 5, off = bit & 31;
+            const uint32_t code =
+                (off <= 22 ? (w[wd] >> off) : __funnelshift_r(w[wd], w[wd + 1], off)) & 0x3FFu;
             a = code / 27u;
             b = code % 27u;
         } else {
-            uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+            const uint32_t byte = (w[q >> 2] >> (8 * (q & 3))) & 0xFFu;
             a = byte & 0xFu;
             b = byte >> 4;
         }
+        const float sig = bf16_to_f32(fp8_to_bf16(units[scale_offset(g, b16, cp, ri, t)]));
         uint16_t va = 0, vb = 0;
         // residual slots (26-state symbol 26) are overwritten by the scatter pass
         if (NS == 16 || a < 26) va = f32_to_bf16(bf16_to_f32(NS == 26 ? d_lat26[a] : d_lat16[a]) * sig);
         if (NS == 16 || b < 26) vb = f32_to_bf16(bf16_to_f32(NS == 26 ? d_lat26[b] : d_lat16[b]) * sig);
-        packed[j] = (uint32_t)va | ((uint32_t)vb << 16);
+        *reinterpret_cast<uint32_t*>(out + row * (int64_t)cols + c * 32 + 2 * p) =
+            (uint32_t)va | ((uint32_t)vb << 16);
     }
-    uint4* dst = reinterpret_cast<uint4*>(out + row * (int64_t)cols + c * 32);
-    for (int q = 0; q < 4; ++q)
-        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
 }
 
 __global__ void dequant_residuals(const uint32_t* __restrict__ res_ptr,
@@ -62,8 +62,8 @@ __global__ void dequant_residuals(const uint32_t* __restrict__ res_ptr,
                                   int ns, uint16_t* __restrict__ out) {
     const Geometry g = geometry(rows, cols, ns);
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= g.rb * g.kg * 32) return;
-    const int64_t row = (b / (g.kg * 32)) * 32 + (b & 31);
+    if (b >= g.r16 * g.kg * 16) return;
+    const int64_t row = (b / (g.kg * 16)) * 16 + (b & 15);
     if (row >= rows) return;
     for (uint32_t e = res_ptr[b]; e < res_ptr[b + 1]; ++e) {
         const uint32_t ent = res_ent[e];
@@ -82,16 +82,16 @@ cudaError_t dequant_setup() {
 
 cudaError_t dequant_launch(const cdq_packed& w, uint16_t* out, cudaStream_t s) {
     const Geometry g = geometry(w.rows, w.cols, w.n_states);
-    const int64_t total = g.rb * g.kt * 32;
+    const int64_t total = g.r16 * g.kp * 32;
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;
     if (w.n_states == 26)
-        dequant_tiles<26><<<(unsigned)blocks, threads, 0, s>>>(w.codes, w.scales, w.rows, w.cols, out);
+        dequant_units<26><<<(unsigned)blocks, threads, 0, s>>>(w.units, w.rows, w.cols, out);
     else
-        dequant_tiles<16><<<(unsigned)blocks, threads, 0, s>>>(w.codes, w.scales, w.rows, w.cols, out);
+        dequant_units<16><<<(unsigned)blocks, threads, 0, s>>>(w.units, w.rows, w.cols, out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int64_t nb = g.rb * g.kg * 32;
+    const int64_t nb = g.r16 * g.kg * 16;
     dequant_residuals<<<(unsigned)((nb + threads - 1) / threads), threads, 0, s>>>(
         w.res_ptr, w.res_ent, w.rows, w.cols, w.n_states, out);
     return cudaGetLastError();

@@ -1,33 +1,38 @@
-// Fused dequant-GEMV for the CDQ-LRR device pack, batch M <= 8 (CUDA cores).
+// Fused dequant-GEMV for the CDQ-LRR device pack, batch M <= 8.
 //
 // y[m, row] = sum_col w_hat[row, col] * x[m, col] (+ bias[row]) where
 // w_hat = bf16(LATTICE[q] * sigma) is rebuilt in registers from the packed
 // tiles and never written to memory (the reference materialises w_hat and
 // calls F.linear: code/cdq_lrr_qwen05.py:188-198, code/cdq_loader.py:53-58).
 //
-// Work decomposition. A work item is (job, row block rb of 32 rows, residual
-// group g of up to 32 tile columns); one warp processes one item with lane l
-// owning row 32*rb + l, so every load of the pack is a coalesced 512-byte
-// (plus 128-byte) sweep and the activations are warp-uniform broadcast loads.
-// Items of all jobs of a launch are spread over the grid's warps.
+// Work decomposition. A work item is (job, 16-row block, residual group of
+// up to 32 tile columns = 16 units = 4 quads). Items of every job of a launch
+// are dealt round-robin to the warps of the grid (grouped launch).
 //
-// Dequantisation. Each pair of neighbouring weights has one pair code
-// (26-state: 10 bits, 27 x 27 codes including the zero-valued residual slot;
-// 16-state: one byte). A shared-memory table maps the pair code to the bf16
-// pair (LATTICE[a], LATTICE[b]); every lane owns a private copy of the table
-// in its own bank, so the 32 lookups of a warp never conflict. One bf16x2
-// multiply by (sigma, sigma) then yields the two exact w_hat values (a single
-// rounding of the exact product, which is what torch's bf16 multiply does),
-// and two mixed-precision FMAs (bf16 x bf16 + fp32) accumulate in fp32.
+// Memory pipeline. Each warp streams its items' quads (2688 or 2176
+// contiguous bytes; the last quad of a row block may be shorter) into a
+// private two-slot ring in shared memory with bulk copies (cp.async.bulk,
+// completion counted on one mbarrier per slot), so two quads are in flight
+// per warp while it decodes the previous one; lane 0 issues the copy of the
+// warp's next quad, across item boundaries, as soon as a slot is consumed.
 //
-// Residuals. Residual positions carry the zero symbol in the codes; their
-// bf16 values come from the item's CSR bucket (one per lane) and are added as
-// value * x[col] in the same warp after the tile sweep.
+// Dequantisation. Lane l = 4g + c reads from the slot exactly the 16 pair
+// codes of its m16n8k16 A fragments (rows g and g+8 of the block over 16
+// contiguous columns of the unit). A shared-memory table maps a pair code to
+// the bf16 pair (LATTICE[a], LATTICE[b]); every lane owns a private copy of
+// the table in its own bank, so the 32 lookups of a warp never conflict.
+// One bf16x2 multiply by (sigma, sigma) then yields the exact w_hat pair (a
+// single rounding of the exact product, as torch's bf16 multiply), which is
+// the A operand of a tensor-core mma (bf16 inputs, fp32 accumulators); the
+// activations form the B operand (batch = the mma's N dimension). Residual
+// positions carry the zero symbol; their bf16 values are added by the fix-up
+// pass from the CSR buckets of each row.
 //
-// Split K. When a row has more than one residual group the warp writes its
-// partial sums to a per-group slot of the workspace and bumps the row block's
-// arrival counter; the warp that arrives last adds the slots in group order
-// (deterministic), applies bias, stores y and resets the counter to zero.
+// Two passes. The streaming pass writes each item's fp32 sums to a per-group
+// slot of the workspace (no residuals, fences or atomics on its path); the
+// fix-up pass adds, per output, the group slots in group order, the row's
+// residual entries (bf16 value x activation in fp32) and the bias, and
+// rounds once. Both passes are deterministic.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -41,6 +46,7 @@ namespace cdq {
 
 __constant__ uint16_t c_lat26[27];
 __constant__ uint16_t c_lat16[16];
+__device__ int g_gemv_error;
 
 namespace {
 
@@ -48,36 +54,80 @@ template <int NS>
 struct PackTraits;
 template <>
 struct PackTraits<26> {
-    static constexpr int kWords = 5;
     static constexpr int kPairs = kPairs26;
+    static constexpr int kUnit = 672;
+    static constexpr int kSigOff = 640;  // code bytes per unit
 };
 template <>
 struct PackTraits<16> {
-    static constexpr int kWords = 4;
     static constexpr int kPairs = kPairs16;
+    static constexpr int kUnit = 544;
+    static constexpr int kSigOff = 512;
 };
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kSlots = 2;                 // quads in flight per warp
+constexpr uint32_t kSmemBytes = 232448;   // 227 KB window
+constexpr uint32_t kSpinLimit = 1u << 22; // mbarrier polls before a wait gives up
 
-__device__ __forceinline__ uint32_t ldg_nc(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
+// Shared-memory map in absolute shared-window addresses (the dynamic window
+// starts within the first 1 KB, which the system reserves):
+//   [1K, 32K)           rings of warps 0 .. kLowWarps-1
+//   [32K, 128K)         26-state pair table: code p at entry p ^ 0x300 (128 B
+//                       entries, so the entry address is ((code << 7) & mask)
+//                       ^ lane_base: one lop3); 16-state table in [64K, 128K)
+//                       (256 B entries: the code byte is address byte 1)
+//   [61K, 64K)          (unused by both tables) first work item of every job
+//                       (binary-search keys), the scale table (fp8 code b ->
+//                       (sigma, sigma) at 4b) and one mbarrier per (warp, slot)
+//   [128K, ...)         rings of warps kLowWarps .. kWarps-1
+// A ring is kSlots slots; a slot holds one quad (its units' bytes as stored)
+// followed, for batch M <= kXSlotBatch, by the quad's activation columns of
+// every batch row (128 bytes per unit per row).
+constexpr uint32_t kLowStage = 1024;
+constexpr int kLowWarps = 4;
+constexpr uint32_t kLat26Xor = 0x300u << 7;
+constexpr uint32_t kLat16Base = 64u << 10;
+constexpr uint32_t kBeginAddr = 61u << 10;
+constexpr uint32_t kSigAddr = 62u << 10;
+constexpr uint32_t kBarAddr = 63u << 10;
+constexpr uint32_t kHighStage = 128u << 10;
+constexpr int kXSlotBatch = 2;
+
+template <int NS, int M>
+struct SlotTraits {
+    static constexpr uint32_t kQuadBytes = 4 * PackTraits<NS>::kUnit;
+    static constexpr bool kX = M <= kXSlotBatch;
+    static constexpr uint32_t kSlot = kQuadBytes + (kX ? M * 512 : 0);
+    static constexpr uint32_t kRing = kSlots * kSlot;
+    static constexpr uint32_t kTop = kHighStage + (kWarps - kLowWarps) * kRing;
+};
+static_assert(kLowStage + kLowWarps * SlotTraits<26, kXSlotBatch>::kRing <= (32u << 10),
+              "low rings overlap the table");
+static_assert(SlotTraits<26, kXSlotBatch>::kTop <= 232448 && SlotTraits<26, 8>::kTop <= 232448,
+              "rings exceed the window");
+static_assert(kBeginAddr >= (473u << 7) && kBeginAddr + 4 * kMaxJobs <= kSigAddr &&
+                  kSigAddr + 1024 <= kBarAddr && kBarAddr + kWarps * kSlots * 8 <= (512u << 7),
+              "keys, scale table and barriers must sit in the 26-state table's unused entries 473..511");
+
+template <int NS, int M>
+__device__ __forceinline__ uint32_t slot_base(int warp) {
+    constexpr uint32_t kRing = SlotTraits<NS, M>::kRing;
+    return warp < kLowWarps ? kLowStage + warp * kRing : kHighStage + (warp - kLowWarps) * kRing;
 }
-__device__ __forceinline__ uint4 ldg_nc4(const uint4* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-// Activations: read by every lane of a warp (broadcast), cached in L1.
+
+// activations: reused by every row block of the job, so cached in L1
 __device__ __forceinline__ uint4 ldg_x4(const uint16_t* p) {
     uint4 v;
     asm volatile("ld.global.nc.v4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 
@@ -87,222 +137,518 @@ __device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
     return d;
 }
 
-// acc0 += lo(w2) * lo(x2), acc1 += hi(w2) * hi(x2), single rounding in fp32.
-__device__ __forceinline__ void fma_pair(float& acc0, float& acc1, uint32_t w2, uint32_t x2) {
-    asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
-        "mov.b32 {wl, wh}, %2;\n\t"
-        "mov.b32 {xl, xh}, %3;\n\t"
-        "fma.rn.f32.bf16 %0, wl, xl, %0;\n\t"
-        "fma.rn.f32.bf16 %1, wh, xh, %1;\n\t}"
-        : "+f"(acc0), "+f"(acc1)
-        : "r"(w2), "r"(x2));
+// Table lookups: the tables are written before the block barrier and only
+// read afterwards, so these loads carry no ordering constraints.
+__device__ __forceinline__ uint32_t lds(uint32_t addr) {
+    uint32_t v;
+    asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+// Slot reads: ordered after the mbarrier wait that published the data.
+__device__ __forceinline__ uint4 lds_slot4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 lds_slot2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_slot(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_slot_u16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
+    return v;
 }
 
-__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
 }
 
-// Pair code j of a tile from its code words.
-template <int NS, int J>
-__device__ __forceinline__ uint32_t pair_code(const uint32_t (&w)[5]) {
+// ---- bulk copies into a slot (one mbarrier per slot, arrival count 1) ----
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+// Arms a slot's mbarrier for `bytes` of copies (the slot's previous contents
+// were read through the generic proxy, hence the proxy fence).
+__device__ __forceinline__ void slot_arm(uint32_t bar, uint32_t bytes) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+// Waits for the phase of the given parity; false after kSpinLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t spin = 0; spin < kSpinLimit; ++spin) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+// D (16 x 8, fp32) += A (16 x 16, bf16, row) * B (16 x 8, bf16, col)
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory address of slot Q's table entry for this lane.
+//   26 states: ((code << 7) & mask) ^ lane_base, the code cut from the 160-bit stream
+//   16 states: address byte 1 = the code byte, bytes 0 and 2 from lane_base
+template <int NS, int Q>
+__device__ __forceinline__ uint32_t slot_addr(const uint32_t (&w)[5], uint32_t lane_base) {
     if constexpr (NS == 26) {
-        constexpr int bit = 10 * J, wd = bit / 32, off = bit % 32;
-        if constexpr (off <= 22) {
-            return (w[wd] >> off) & 0x3FFu;
+        constexpr int bit = 10 * Q;
+        constexpr uint32_t mask = 0x3FFu << 7;
+        if constexpr (bit < 7) {
+            return ((w[0] << (7 - bit)) & mask) ^ lane_base;
         } else {
-            return __funnelshift_r(w[wd], w[wd + 1], off) & 0x3FFu;
+            constexpr int b7 = bit - 7, wd = b7 / 32, s = b7 % 32;
+            if constexpr (s + 17 <= 32 || wd + 1 >= 5) {
+                return ((w[wd] >> s) & mask) ^ lane_base;
+            } else {
+                return (__funnelshift_r(w[wd], w[wd + 1], s) & mask) ^ lane_base;
+            }
         }
     } else {
-        return (w[J / 4] >> (8 * (J % 4))) & 0xFFu;
+        return prmt(w[Q >> 2], lane_base, 0x7604u | ((Q & 3) << 4));
     }
 }
 
-template <int NS, int M, int Q>
-__device__ __forceinline__ void tile_quarter(const uint32_t (&w)[5], const uint32_t* tab,
-                                             uint32_t ss, const uint4 (&xv)[M],
-                                             float (&acc)[M][2]) {
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-        uint32_t code;
-        switch (jj) {  // J must be a compile-time constant
-            case 0: code = pair_code<NS, Q * 4 + 0>(w); break;
-            case 1: code = pair_code<NS, Q * 4 + 1>(w); break;
-            case 2: code = pair_code<NS, Q * 4 + 2>(w); break;
-            default: code = pair_code<NS, Q * 4 + 3>(w); break;
-        }
-        uint32_t pair = tab[code * 32];
-        uint32_t wp = bmul2(pair, ss);
-#pragma unroll
-        for (int m = 0; m < M; ++m) fma_pair(acc[m][0], acc[m][1], wp, word_of(xv[m], jj));
-    }
+template <int NS, int Q>
+__device__ __forceinline__ uint32_t what_pair(const uint32_t (&w)[5], uint32_t lane_base, uint32_t ss) {
+    return bmul2(lds(slot_addr<NS, Q>(w, lane_base)), ss);
 }
 
-template <int NS, int M>
-__device__ __forceinline__ void tile_dot(const uint32_t (&w)[5], const uint32_t* tab, uint32_t ss,
-                                         const uint16_t* xcol, int64_t cols, float (&acc)[M][2]) {
-    uint4 xv[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) xv[m] = ldg_x4(xcol + m * cols + 0);
-    tile_quarter<NS, M, 0>(w, tab, ss, xv, acc);
-#pragma unroll
-    for (int m = 0; m < M; ++m) xv[m] = ldg_x4(xcol + m * cols + 8);
-    tile_quarter<NS, M, 1>(w, tab, ss, xv, acc);
-#pragma unroll
-    for (int m = 0; m < M; ++m) xv[m] = ldg_x4(xcol + m * cols + 16);
-    tile_quarter<NS, M, 2>(w, tab, ss, xv, acc);
-#pragma unroll
-    for (int m = 0; m < M; ++m) xv[m] = ldg_x4(xcol + m * cols + 24);
-    tile_quarter<NS, M, 3>(w, tab, ss, xv, acc);
+// One unit: 16 rows x 64 columns, four m16n8k16 mmas over the k16 slices.
+// w4 = fifth code word (26 states); sw = scale half-word at bits SH.. of sw
+// (fp8 code of row g, then row g + 8).
+template <int NS, int SH>
+__device__ __forceinline__ void unit_mma(const uint4& a, uint32_t w4, uint32_t sw, const uint4& xa,
+                                         const uint4& xb, uint32_t lane_base, uint32_t sig_base,
+                                         float (&d)[4]) {
+    const uint32_t w[5] = {a.x, a.y, a.z, a.w, w4};
+    const uint32_t lo = SH <= 2 ? (sw << (2 - SH)) : (sw >> (SH - 2));
+    const uint32_t hi = sw >> (SH + 6);
+    const uint32_t ss0 = lds((lo & 0x3FCu) | sig_base);  // (sigma, sigma) of row g
+    const uint32_t ss1 = lds((hi & 0x3FCu) | sig_base);  // row g + 8
+    mma16816(d, what_pair<NS, 0>(w, lane_base, ss0), what_pair<NS, 1>(w, lane_base, ss1),
+             what_pair<NS, 2>(w, lane_base, ss0), what_pair<NS, 3>(w, lane_base, ss1), xa.x, xa.y);
+    mma16816(d, what_pair<NS, 4>(w, lane_base, ss0), what_pair<NS, 5>(w, lane_base, ss1),
+             what_pair<NS, 6>(w, lane_base, ss0), what_pair<NS, 7>(w, lane_base, ss1), xa.z, xa.w);
+    mma16816(d, what_pair<NS, 8>(w, lane_base, ss0), what_pair<NS, 9>(w, lane_base, ss1),
+             what_pair<NS, 10>(w, lane_base, ss0), what_pair<NS, 11>(w, lane_base, ss1), xb.x, xb.y);
+    mma16816(d, what_pair<NS, 12>(w, lane_base, ss0), what_pair<NS, 13>(w, lane_base, ss1),
+             what_pair<NS, 14>(w, lane_base, ss0), what_pair<NS, 15>(w, lane_base, ss1), xb.z, xb.w);
 }
 
-__device__ __forceinline__ void store_out(const GemvJob& J, int m, int row, float v) {
+__device__ __forceinline__ void store_out(const GemvJob& J, int n, int row, float v) {
     if (J.bias) v += bf16_to_f32(J.bias[row]);
     if (J.out_f32) {
-        reinterpret_cast<float*>(J.y)[(int64_t)m * J.rows + row] = v;
+        reinterpret_cast<float*>(J.y)[(int64_t)n * J.rows + row] = v;
     } else {
-        reinterpret_cast<uint16_t*>(J.y)[(int64_t)m * J.rows + row] =
+        reinterpret_cast<uint16_t*>(J.y)[(int64_t)n * J.rows + row] =
             __bfloat16_as_ushort(__float2bfloat16_rn(v));
     }
 }
 
-template <int NS, int M, int MAXJ>
-__global__ void __launch_bounds__(kThreads, 2)
-gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
-    using T = PackTraits<NS>;
-    extern __shared__ __align__(16) uint32_t smem[];
-    uint32_t* sig2 = smem + T::kPairs * 32;
+// Activations of unit column block `unit` (64 columns) for this lane; the
+// phantom second tile of an odd tile count takes zeros (lanes c >= 2).
+__device__ __forceinline__ void load_x(const uint16_t* xp, int unit, bool phantom, int c, uint4& xa,
+                                       uint4& xb) {
+    if (!phantom) {
+        xa = ldg_x4(xp + 64 * unit);
+        xb = ldg_x4(xp + 64 * unit + 8);
+    } else {
+        xa = make_uint4(0u, 0u, 0u, 0u);
+        xb = xa;
+        if (c < 2) {
+            xa = ldg_x4(xp + 64 * unit);
+            xb = ldg_x4(xp + 64 * unit + 8);
+        }
+    }
+}
 
-    // Lane-private pair table and the (sigma, sigma) table of every fp8 code.
-    for (int i = threadIdx.x; i < T::kPairs * 32; i += blockDim.x) {
-        int p = i >> 5;
-        uint32_t lo, hi;
+// Where a work item lives: its job, row block, residual group and units.
+struct ItemInfo {
+    int job, b16, grp, cp0, n_units;
+};
+
+template <int MAXJ>
+__device__ __forceinline__ ItemInfo item_info(const GemvBatch<MAXJ>& batch, int64_t item) {
+    ItemInfo I;
+    int j = 0;
+    if constexpr (MAXJ > 1) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {  // last job with item_begin <= item (keys in shared memory)
+            const int mid = (lo + hi + 1) >> 1;
+            if ((int64_t)(int32_t)lds(kBeginAddr + 4 * mid) <= item) lo = mid; else hi = mid - 1;
+        }
+        j = lo;
+    }
+    const GemvJob& J = batch.jobs[j];
+    const int local = (int)(item - J.item_begin);
+    I.job = j;
+    I.b16 = local / J.kg;
+    I.grp = local - I.b16 * J.kg;
+    I.cp0 = I.grp * kGroupPairs;
+    I.n_units = min(I.cp0 + kGroupPairs, J.kp) - I.cp0;
+    return I;
+}
+
+template <int NS, int M, int MAXJ>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    using Tr = PackTraits<NS>;
+    using Sl = SlotTraits<NS, M>;
+    constexpr uint32_t kU = Tr::kUnit;
+    constexpr uint32_t kQuad = Sl::kQuadBytes;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+    if (s0 > kLowStage || s0 + kSmemBytes < Sl::kTop) {
+        if (threadIdx.x == 0) atomicExch(&g_gemv_error, 1);
+        return;
+    }
+    uint8_t* const base = smem - s0;  // generic pointer of shared address 0
+    for (int i = threadIdx.x; i < Tr::kPairs * 32; i += blockDim.x) {
+        const uint32_t p = (uint32_t)i >> 5, l = (uint32_t)i & 31;
+        uint32_t lo, hi, addr;
         if constexpr (NS == 26) {
             lo = c_lat26[p / 27];
             hi = c_lat26[p % 27];
+            addr = ((p << 7) ^ kLat26Xor) + 4 * l;
         } else {
             lo = c_lat16[p & 15];
             hi = c_lat16[p >> 4];
+            addr = kLat16Base + (p << 8) + 4 * l;
         }
-        smem[i] = lo | (hi << 16);
+        *reinterpret_cast<uint32_t*>(base + addr) = lo | (hi << 16);
     }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-        uint32_t s = fp8_to_bf16((uint8_t)i);
-        sig2[i] = s | (s << 16);
+        const uint32_t s = fp8_to_bf16((uint8_t)i);
+        *reinterpret_cast<uint32_t*>(base + kSigAddr + 4 * i) = s | (s << 16);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    if constexpr (MAXJ > 1) {  // warp-uniform reads of the launch record
+        for (int i = warp; i < batch.n; i += kWarps) {
+            const int32_t v = (int32_t)batch.jobs[i].item_begin;
+            if (lane == 0) *reinterpret_cast<int32_t*>(base + kBeginAddr + 4 * i) = v;
+        }
+    }
+    const uint32_t ring = slot_base<NS, M>(warp);
+    const uint32_t bars = kBarAddr + warp * kSlots * 8;
+    if (lane == 0) {
+        for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
-    const int lane = threadIdx.x & 31;
-    const uint32_t* tab = smem + lane;
-    const int64_t warp0 = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-    const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+    const uint32_t lane_base = NS == 26 ? (kLat26Xor | (4u * lane)) : (kLat16Base + 4u * lane);
+    const uint32_t sig_base = kSigAddr;
+    const int64_t total = batch.total_items;
+    const int64_t stride = (int64_t)gridDim.x * kWarps;
+    const int64_t first = (int64_t)blockIdx.x * kWarps + warp;
+    // lanes of batch columns >= M read row 0: their mma output columns are
+    // never stored, so any finite or non-finite value there is harmless
+    const int xrow = g < M ? g : 0;
 
-    for (int64_t item = warp0; item < batch.total_items; item += nwarps) {
-        int j = 0;
-        if constexpr (MAXJ > 1) {
-            int lo = 0, hi = batch.n - 1;
-            while (lo < hi) {  // last job with item_begin <= item
-                int mid = (lo + hi + 1) >> 1;
-                if (batch.jobs[mid].item_begin <= item) lo = mid; else hi = mid - 1;
-            }
-            j = lo;
+    // Producer cursor (lane 0 issues; every lane keeps the same values): the
+    // next quad of this warp's stream of items.
+    int64_t p_item = first;
+    int p_q = 0, p_nq = 0, p_units = 0, p_cols = 0, p_xleft = 0;
+    const uint8_t* p_base = nullptr;
+    const uint16_t* p_x = nullptr;
+    uint32_t p_slot = 0;
+    auto p_load = [&]() {
+        if (p_item < total) {
+            const ItemInfo I = item_info(batch, p_item);
+            const GemvJob& J = batch.jobs[I.job];
+            p_base = J.units + ((int64_t)I.b16 * J.kp + I.cp0) * kU;
+            p_units = I.n_units;
+            p_nq = (I.n_units + 3) >> 2;
+            p_q = 0;
+            p_x = J.x + 64 * I.cp0;
+            p_cols = J.cols;
+            p_xleft = 2 * (J.cols - 64 * I.cp0);  // activation bytes of a row from the item's first column
         }
-        const GemvJob& J = batch.jobs[j];
-        const int64_t local = item - J.item_begin;
-        const int rb = (int)(local / J.kg), g = (int)(local % J.kg);
-        const int row = rb * 32 + lane;
-        const int c0 = g * kGroupTiles;
-        const int c1 = min(c0 + kGroupTiles, J.kt);
-
-        float acc[M][2];
+    };
+    auto produce = [&]() {
+        if (p_item >= total) return;
+        const int left = p_units - 4 * p_q;
+        const int u = left < 4 ? left : 4;
+        const uint32_t bytes = (uint32_t)u * kU;
+        if (lane == 0) {
+            const uint32_t slot = ring + p_slot * Sl::kSlot, bar = bars + 8 * p_slot;
+            if constexpr (Sl::kX) {
+                // the quad's activation columns, cut at the row's end (a phantom tile)
+                const int xb = min(128 * u, p_xleft - 512 * p_q);
+                slot_arm(bar, bytes + (uint32_t)(M * xb));
+                bulk_copy(slot, p_base + (int64_t)p_q * kQuad, bytes, bar);
 #pragma unroll
-        for (int m = 0; m < M; ++m) acc[m][0] = acc[m][1] = 0.f;
-
-        const uint32_t* cbase = J.codes + ((int64_t)rb * J.kt) * (T::kWords * 32);
-        const uint32_t* sbase = reinterpret_cast<const uint32_t*>(J.scales) + (int64_t)rb * J.kt4 * 32;
-
-        for (int c = c0; c < c1; c += 4) {
-            const uint32_t sw = ldg_nc(sbase + (c >> 2) * 32 + lane);
-            uint32_t w[4][5];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                if (c + t < c1) {
-                    const uint32_t* cw = cbase + (int64_t)(c + t) * (T::kWords * 32);
-                    uint4 v = ldg_nc4(reinterpret_cast<const uint4*>(cw) + lane);
-                    w[t][0] = v.x;
-                    w[t][1] = v.y;
-                    w[t][2] = v.z;
-                    w[t][3] = v.w;
-                    w[t][4] = (T::kWords == 5) ? ldg_nc(cw + 128 + lane) : 0u;
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                if (c + t < c1) {
-                    const uint32_t ss = sig2[(sw >> (8 * t)) & 0xFFu];
-                    tile_dot<NS, M>(w[t], tab, ss, J.x + (int64_t)(c + t) * 32, J.cols, acc);
-                }
+                for (int m = 0; m < M; ++m)
+                    bulk_copy(slot + kQuad + 512 * m, p_x + (int64_t)m * p_cols + 256 * p_q, (uint32_t)xb, bar);
+            } else {
+                slot_arm(bar, bytes);
+                bulk_copy(slot, p_base + (int64_t)p_q * kQuad, bytes, bar);
             }
         }
-
-        // residuals of this lane's row within the group
-        const int64_t bidx = ((int64_t)rb * J.kg + g) * 32 + lane;
-        const uint32_t e0 = J.res_ptr[bidx], e1 = J.res_ptr[bidx + 1];
-        for (uint32_t e = e0; e < e1; ++e) {
-            const uint32_t ent = J.res_ent[e];
-            const float v = bf16_to_f32((uint16_t)(ent & 0xFFFFu));
-            const int col = (int)(ent >> 16);
-            if (col >= J.cols) continue;  // only a corrupted pack has one
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-                acc[m][0] = fmaf(v, bf16_to_f32(J.x[(int64_t)m * J.cols + col]), acc[m][0]);
+        p_slot ^= 1u;
+        if (++p_q == p_nq) {
+            p_item += stride;
+            p_load();
         }
+    };
+    p_load();
+    produce();
+    produce();
 
-        if (J.kg == 1) {
-            if (row < J.rows) {
-#pragma unroll
-                for (int m = 0; m < M; ++m) store_out(J, m, row, acc[m][0] + acc[m][1]);
+    uint32_t c_slot = 0, c_phase = 0;
+    bool failed = false;
+    for (int64_t item = first; item < total && !failed; item += stride) {
+        const ItemInfo I = item_info(batch, item);
+        const GemvJob& J = batch.jobs[I.job];
+        const int n_units = I.n_units, nq = (n_units + 3) >> 2;
+        // a phantom second tile (odd tile count) sits in the row's last unit
+        const int phantom_u = (J.kt & 1) && I.cp0 + n_units == J.kp ? n_units - 1 : -1;
+        const uint16_t* xp = J.x + (int64_t)xrow * J.cols + 64 * I.cp0 + 16 * c;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < nq; ++q) {
+            if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
+                failed = true;
+                break;
             }
-        } else {
-            const int64_t rpad = (int64_t)J.rb * 32;
-            // partial sums of this group: slot [m][g][row]
+            const uint32_t slot = ring + c_slot * Sl::kSlot;
+            const int uq = min(4, n_units - 4 * q);
+            // the quad's words into registers, then the slot goes back to the copy engine
+            uint4 A[4], X[4][2];
+            uint4 W;
+            uint2 S;
+            if (uq == 4) {
 #pragma unroll
-            for (int m = 0; m < M; ++m)
-                J.partial[((int64_t)m * J.kg + g) * rpad + row] = acc[m][0] + acc[m][1];
-            __threadfence();
-            __syncwarp();
-            uint32_t last = 0;
-            if (lane == 0) last = (atomicAdd(&J.counters[rb], 1u) == (uint32_t)(J.kg - 1));
-            last = __shfl_sync(0xFFFFFFFFu, last, 0);
-            if (last) {
-                __threadfence();
-                if (row < J.rows) {
+                for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+            } else {  // the short last quad of a row block (1..3 units, compact)
+                uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
 #pragma unroll
-                    for (int m = 0; m < M; ++m) {
-                        float s = 0.f;
-                        for (int gg = 0; gg < J.kg; ++gg)
-                            s += __ldcg(&J.partial[((int64_t)m * J.kg + gg) * rpad + row]);
-                        store_out(J, m, row, s);
+                for (int i = 0; i < 3; ++i) {
+                    A[i] = make_uint4(0u, 0u, 0u, 0u);
+                    if (i < uq) {
+                        A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                        if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
+                        h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
                     }
                 }
-                __syncwarp();
-                if (lane == 0) atomicExch(&J.counters[rb], 0u);
+                A[3] = make_uint4(0u, 0u, 0u, 0u);
+                W = make_uint4(w4[0], w4[1], w4[2], 0u);
+                S = make_uint2(h[0] | (h[1] << 16), h[2]);
+            }
+            uint32_t dep = W.x ^ W.y ^ W.z ^ W.w ^ S.x ^ S.y;
+            if constexpr (Sl::kX) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    X[i][0] = make_uint4(0u, 0u, 0u, 0u);
+                    X[i][1] = X[i][0];
+                    // the phantom tile's lanes (c >= 2) keep zeros: that part of the slot is stale
+                    if (i < uq && (4 * q + i != phantom_u || c < 2)) {
+                        const uint32_t xa = slot + kQuad + 512 * xrow + 128 * i + 32 * c;
+                        X[i][0] = lds_slot4(xa);
+                        X[i][1] = lds_slot4(xa + 16);
+                    }
+                    dep ^= X[i][0].x ^ X[i][1].w;
+                }
+            }
+            // every lane waits for its slot reads to land before lane 0 reuses the slot
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dep ^= A[i].x ^ A[i].y ^ A[i].z ^ A[i].w;
+            asm volatile("" ::"r"(dep));
+            __syncwarp();
+            produce();
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
+
+            const uint16_t* xq = xp + 256 * q;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (i < uq) {
+                    uint4 xa, xb;
+                    if constexpr (Sl::kX) {
+                        xa = X[i][0];
+                        xb = X[i][1];
+                    } else {
+                        load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
+                    }
+                    if (i == 0) unit_mma<NS, 0>(A[0], W.x, S.x, xa, xb, lane_base, sig_base, d);
+                    if (i == 1) unit_mma<NS, 16>(A[1], W.y, S.x, xa, xb, lane_base, sig_base, d);
+                    if (i == 2) unit_mma<NS, 0>(A[2], W.z, S.y, xa, xb, lane_base, sig_base, d);
+                    if (i == 3) unit_mma<NS, 16>(A[3], W.w, S.y, xa, xb, lane_base, sig_base, d);
+                }
             }
         }
+        if (failed) break;
+        // this group's partial sums of rows g and g + 8 (batch columns 2c, 2c + 1)
+        const int64_t rpad = (int64_t)J.r16 * 16;
+        const int n0 = 2 * c;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t row = I.b16 * 16 + g + 8 * h;
+            if (n0 < M) J.partial[((int64_t)n0 * J.kg + I.grp) * rpad + row] = d[2 * h];
+            if (n0 + 1 < M) J.partial[((int64_t)(n0 + 1) * J.kg + I.grp) * rpad + row] = d[2 * h + 1];
+        }
+    }
+    if (failed) {
+        // a copy that never landed: record it, give the copies still in
+        // flight a bounded chance to land, and leave
+        if (lane == 0) atomicExch(&g_gemv_error, 2);
+        for (int k = 0; k < kSlots; ++k) {
+            (void)mbar_wait(bars + 8 * c_slot, c_phase);
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
+        }
+    }
+}
+
+// Fix-up pass: y[m, row] = sum over residual groups g, in group order, of
+// (partial sum of group g + the row's residual entries of group g, bf16 value
+// x activation in fp32, in entry order) + bias, rounded once to bf16 (or
+// stored as float32). One thread per (row, group) with all of its entries in
+// flight at once (the pass is a few dependent memory round trips per thread,
+// so the work per thread is sized for memory-level parallelism); the groups
+// of a row meet in shared memory. A block covers kFixThreads / kg rows of one
+// job; the job's activations are staged in shared memory when they fit.
+constexpr int kFixThreads = 256;
+constexpr uint32_t kFixStageMax = 64u << 10;  // activations staged in shared memory up to this size
+
+template <int M, int MAXJ, bool kStaged>
+__global__ void __launch_bounds__(kFixThreads, 4)
+fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    constexpr int kFixBatch = M <= 2 ? 16 : 4;
+    __shared__ float red[kFixThreads][M];
+    extern __shared__ __align__(16) uint16_t xs[];
+    // block -> (job, block of the job): rb_begin holds each job's first block
+    int j = 0;
+    if constexpr (MAXJ > 1) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (batch.jobs[mid].rb_begin <= (int)blockIdx.x) lo = mid; else hi = mid - 1;
+        }
+        j = lo;
+    }
+    const GemvJob& J = batch.jobs[j];
+    const int kg = J.kg, cols = J.cols, rows = J.rows;
+    const int rpb = kFixThreads / kg;  // rows per block
+    const int row0 = ((int)blockIdx.x - J.rb_begin) * rpb;
+    const uint16_t* x = J.x;
+    if constexpr (kStaged) {
+        // the job's activations, read coalesced once per block; the residual
+        // gathers then hit shared memory instead of one L1 sector per lane
+        const int words = M * cols / 8;
+        const uint4* src = reinterpret_cast<const uint4*>(J.x);
+        uint4* dst = reinterpret_cast<uint4*>(xs);
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = __ldg(src + i);
+        x = xs;
+    }
+    const int rl = (int)threadIdx.x / kg, grp = (int)threadIdx.x - rl * kg;
+    const int row = row0 + rl;
+    const bool live = rl < rpb && row < rows;
+    float val[M];
+#pragma unroll
+    for (int n = 0; n < M; ++n) val[n] = 0.f;
+    uint32_t eb = 0, ee = 0;
+    if (live) {
+        const int64_t rpad = (int64_t)J.r16 * 16;
+        const int64_t bk = ((int64_t)(row >> 4) * kg + grp) * 16 + (row & 15);
+        eb = __ldg(J.res_ptr + bk);
+        ee = min(__ldg(J.res_ptr + bk + 1), J.n_res);
+#pragma unroll
+        for (int n = 0; n < M; ++n) val[n] = __ldcg(J.partial + ((int64_t)n * kg + grp) * rpad + row);
+    }
+    if constexpr (kStaged) __syncthreads();
+    float acc[M];
+#pragma unroll
+    for (int n = 0; n < M; ++n) acc[n] = 0.f;
+    for (uint32_t e0 = eb; e0 < ee; e0 += kFixBatch) {
+        uint32_t en[kFixBatch];
+#pragma unroll
+        for (int t = 0; t < kFixBatch; ++t) en[t] = e0 + t < ee ? __ldg(J.res_ent + e0 + t) : 0u;
+#pragma unroll
+        for (int t = 0; t < kFixBatch; ++t) {
+            const uint32_t col = en[t] >> 16;
+            if (e0 + t < ee && col < (uint32_t)cols) {
+                const float v = __uint_as_float(en[t] << 16);
+#pragma unroll
+                for (int n = 0; n < M; ++n)
+                    acc[n] = fmaf(v, bf16_to_f32(kStaged ? x[n * cols + col] : __ldg(x + (int64_t)n * cols + col)),
+                                  acc[n]);
+            }
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < M; ++n) red[threadIdx.x][n] = val[n] + acc[n];
+    __syncthreads();
+    if (!live || grp != 0) return;
+#pragma unroll
+    for (int n = 0; n < M; ++n) {
+        float s = 0.f;
+        for (int g2 = 0; g2 < kg; ++g2) s += red[threadIdx.x + g2][n];
+        store_out(J, n, row, s);
     }
 }
 
 template <int NS, int M, int MAXJ>
 cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
-    using T = PackTraits<NS>;
-    const size_t smem = (size_t)T::kPairs * 32 * 4 + 256 * 4;
     auto kern = gemv_kernel<NS, M, MAXJ>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) return e;
-    const int per_sm = NS == 26 ? 2 : 3;
-    int64_t want = (b.total_items + kWarps - 1) / kWarps;
-    int grid = (int)std::min<int64_t>(want, (int64_t)num_sms * per_sm);
-    if (grid < 1) grid = 1;
-    kern<<<grid, kThreads, smem, stream>>>(b);
+    const int64_t want = (b.total_items + kWarps - 1) / kWarps;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, num_sms));
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(b);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    // the fix-up grid: each job's rows in blocks of kFixThreads / kg rows, jobs back to back
+    GemvBatch<MAXJ> fb = b;
+    int blocks = 0, max_cols = 32;
+    for (int j = 0; j < fb.n; ++j) {
+        const int rpb = kFixThreads / fb.jobs[j].kg;
+        fb.jobs[j].rb_begin = blocks;
+        blocks += (fb.jobs[j].rows + rpb - 1) / rpb;
+        max_cols = std::max(max_cols, fb.jobs[j].cols);
+    }
+    const unsigned fix_grid = (unsigned)std::max(blocks, 1);
+    const uint32_t xbytes = (uint32_t)M * (uint32_t)max_cols * 2u;
+    if (xbytes <= kFixStageMax) {
+        auto fk = fixup_kernel<M, MAXJ, true>;
+        e = cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFixStageMax);
+        if (e != cudaSuccess) return e;
+        fk<<<fix_grid, kFixThreads, xbytes, stream>>>(fb);
+    } else {
+        fixup_kernel<M, MAXJ, false><<<fix_grid, kFixThreads, 0, stream>>>(fb);
+    }
     return cudaGetLastError();
 }
 
@@ -343,6 +689,14 @@ cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_
 cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cudaStream_t s,
                                 int sms) {
     return dispatch<kMaxJobs>(b, ns, m, s, sms);
+}
+
+cudaError_t gemv_read_error(int* out) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof v);
+    if (e != cudaSuccess) return e;
+    *out = v;
+    return cudaSuccess;
 }
 
 }  // namespace cdq
@@ -391,8 +745,6 @@ cdq_status noalloc_setup(void** scratch, int* sms) {
     return CDQ_OK;
 }
 
-inline int64_t al256(int64_t b) { return (b + 255) / 256 * 256; }
-
 }  // namespace
 }  // namespace cdq
 
@@ -402,15 +754,13 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     if (!w) return CDQ_ERR_ARG;
     if (w->n_states != 26 && w->n_states != 16) return CDQ_ERR_STATES;
     if (w->rows <= 0 || w->cols <= 0 || w->cols % 32 || w->cols > CDQ_MAX_COLS) return CDQ_ERR_SHAPE;
-    if (!w->codes || !w->scales || !w->res_ptr || (w->n_res > 0 && !w->res_ent)) return CDQ_ERR_ARG;
+    if (!w->units || !w->res_ptr || (w->n_res > 0 && !w->res_ent)) return CDQ_ERR_ARG;
     if (m < 1 || m > CDQ_MAX_BATCH || !x || !y) return CDQ_ERR_ARG;
-    if ((uintptr_t)w->codes % 16 || (uintptr_t)w->scales % 4 || (uintptr_t)w->res_ptr % 4 ||
-        (uintptr_t)x % 16 || (uintptr_t)y % 2 || (bias && (uintptr_t)bias % 2))
+    if ((uintptr_t)w->units % 16 || (uintptr_t)w->res_ptr % 4 || (uintptr_t)x % 16 ||
+        (uintptr_t)y % 2 || (bias && (uintptr_t)bias % 2))
         return CDQ_ERR_ARG;
     const Geometry g = geometry(w->rows, w->cols, w->n_states);
-    const int64_t slots = al256(m * g.kg * g.rb * 32 * 4);
-    const int64_t need = slots + al256(g.rb * 4);
-    if (g.kg > 1 && need > (int64_t)kNoAllocScratchBytes) return CDQ_ERR_WORKSPACE;
+    if (linear_workspace_need(g, m) > (int64_t)kNoAllocScratchBytes) return CDQ_ERR_WORKSPACE;
 
     void* scratch = nullptr;
     int sms = 0;
@@ -419,10 +769,8 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
 
     GemvBatch<1> b;
     b.n = 1;
-    b.pad_ = 0;
     GemvJob& J = b.jobs[0];
-    J.codes = w->codes;
-    J.scales = w->scales;
+    J.units = w->units;
     J.res_ptr = w->res_ptr;
     J.res_ent = w->res_ent;
     J.x = x;
@@ -430,24 +778,22 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     J.bias = bias;
     J.rows = w->rows;
     J.cols = w->cols;
-    J.rb = (int32_t)g.rb;
+    J.r16 = (int32_t)g.r16;
     J.kt = (int32_t)g.kt;
-    J.kt4 = (int32_t)g.kt4;
+    J.kp = (int32_t)g.kp;
     J.kg = (int32_t)g.kg;
     J.out_f32 = 0;
-    J.pad_ = 0;
+    J.n_res = (uint32_t)w->n_res;
     J.item_begin = 0;
-    J.partial = nullptr;
-    J.counters = nullptr;
-    cudaStream_t s = (cudaStream_t)stream;
-    if (g.kg > 1) {
-        unsigned char* base = static_cast<unsigned char*>(scratch);
-        J.partial = reinterpret_cast<float*>(base);
-        J.counters = reinterpret_cast<uint32_t*>(base + slots);
-        // the array keeps the previous call's contents: the arrival counters
-        // must start at zero (the partial slots are written before they are read)
-        if (cudaMemsetAsync(J.counters, 0, (size_t)g.rb * 4, s) != cudaSuccess) return CDQ_ERR_CUDA;
-    }
-    b.total_items = (int64_t)J.rb * J.kg;
-    return gemv_launch_single(b, w->n_states, (int)m, s, sms) == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    J.rb_begin = 0;
+    J.reserved0 = 0;
+    J.reserved_ptr = nullptr;
+    // the streaming pass writes every partial slot before the fix-up pass
+    // reads it, so the array's previous contents never matter
+    J.partial = static_cast<float*>(scratch);
+    b.total_items = (int64_t)J.r16 * J.kg;
+    b.total_row_blocks = J.r16;
+    return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
 }

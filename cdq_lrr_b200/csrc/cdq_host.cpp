@@ -35,47 +35,36 @@ cdq_status check_shape(int32_t rows, int32_t cols, int32_t n_states) {
     return CDQ_OK;
 }
 
-// Symbols of one tile -> its code words (device layout encoding).
-void encode_tile(const uint8_t* sym, int n_states, uint32_t* w) {
+// Slot code of two symbols, and its inverse.
+inline uint32_t pair_code(int n_states, uint32_t a, uint32_t b) {
+    return n_states == 26 ? a * 27u + b : (a & 0xFu) | ((b & 0xFu) << 4);
+}
+inline void pair_syms(int n_states, uint32_t code, uint8_t* a, uint8_t* b) {
     if (n_states == 26) {
-        uint32_t acc[5] = {0, 0, 0, 0, 0};
-        for (int j = 0; j < 16; ++j) {
-            uint32_t code = (uint32_t)sym[2 * j] * 27u + sym[2 * j + 1];
-            int bit = 10 * j;
-            int wd = bit >> 5, off = bit & 31;
-            acc[wd] |= code << off;
-            if (off > 22) acc[wd + 1] |= code >> (32 - off);
-        }
-        memcpy(w, acc, sizeof acc);
+        *a = (uint8_t)(code / 27u);
+        *b = (uint8_t)(code % 27u);
     } else {
-        for (int wd = 0; wd < 4; ++wd) {
-            uint32_t v = 0;
-            for (int b = 0; b < 4; ++b) {
-                int j = wd * 4 + b;
-                v |= (uint32_t)((sym[2 * j] & 0xF) | ((sym[2 * j + 1] & 0xF) << 4)) << (8 * b);
-            }
-            w[wd] = v;
-        }
+        *a = (uint8_t)(code & 0xFu);
+        *b = (uint8_t)(code >> 4);
     }
 }
-
-void decode_tile(const uint32_t* w, int n_states, uint8_t* sym) {
+// Place / read slot q of a lane's word stream.
+inline void put_slot(int n_states, uint32_t* w, int q, uint32_t code) {
     if (n_states == 26) {
-        for (int j = 0; j < 16; ++j) {
-            int bit = 10 * j;
-            int wd = bit >> 5, off = bit & 31;
-            uint64_t win = w[wd] | (wd + 1 < 5 ? (uint64_t)w[wd + 1] << 32 : 0);
-            uint32_t code = (uint32_t)(win >> off) & 0x3FFu;
-            sym[2 * j] = (uint8_t)(code / 27u);
-            sym[2 * j + 1] = (uint8_t)(code % 27u);
-        }
+        const int bit = 10 * q, wd = bit >> 5, off = bit & 31;
+        w[wd] |= code << off;
+        if (off > 22) w[wd + 1] |= code >> (32 - off);
     } else {
-        for (int j = 0; j < 16; ++j) {
-            uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-            sym[2 * j] = (uint8_t)(byte & 0xF);
-            sym[2 * j + 1] = (uint8_t)(byte >> 4);
-        }
+        w[q >> 2] |= (code & 0xFFu) << (8 * (q & 3));
     }
+}
+inline uint32_t get_slot(int n_states, const uint32_t* w, int q) {
+    if (n_states == 26) {
+        const int bit = 10 * q, wd = bit >> 5, off = bit & 31;
+        uint64_t win = w[wd] | (wd + 1 < 5 ? (uint64_t)w[wd + 1] << 32 : 0);
+        return (uint32_t)(win >> off) & 0x3FFu;
+    }
+    return (w[q >> 2] >> (8 * (q & 3))) & 0xFFu;
 }
 
 // ---- little-endian byte stream helpers for the .cdq codec ----
@@ -154,23 +143,21 @@ cdq_status cdq_get_sizes(int32_t rows, int32_t cols, int32_t n_states, double st
     Geometry g = geometry(rows, cols, n_states);
     int64_t numel = (int64_t)rows * cols;
     int64_t n_tiles = numel / 32;
-    out->row_blocks = g.rb;
-    out->tile_cols = g.kt;
+    out->row_blocks = g.r16;
+    out->tile_pairs = g.kp;
     out->res_groups = g.kg;
-    out->codes_bytes = g.rb * g.kt * g.words * 128;
-    out->scales_bytes = g.rb * g.kt4 * 128;
-    out->res_ptr_count = g.rb * g.kg * 32 + 1;
+    out->units_bytes = g.r16 * g.kp * g.unit;
+    out->res_ptr_count = g.r16 * g.kg * 16 + 1;
     out->max_res = residual_budget(numel, stc_frac);
-    // split-K partial slots [max_batch][kg][rb*32] f32 + one arrival counter per row block
-    out->linear_workspace_bytes =
-        align256((int64_t)max_batch * g.kg * g.rb * 32 * 4) + align256(g.rb * 4);
+    // per-group partial sums [max_batch][kg][r16*16] f32 of the streaming pass
+    out->linear_workspace_bytes = align256((int64_t)max_batch * g.kg * g.r16 * 16 * 4);
     // tile variance f32, tie counts u32 (n_tiles + 1), histograms, scalars
     out->quantize_workspace_bytes = align256(n_tiles * 4) + align256((n_tiles + 1) * 4) +
                                     align256(4 * 2048 * 4) + align256(1024);
     return CDQ_OK;
 }
 
-const char* cdq_version(void) { return "cdq-b200 1.0 (sm_100a)"; }
+const char* cdq_version(void) { return "cdq-b200 1.1 (sm_100a)"; }
 
 cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
                                    const uint8_t* q, const uint8_t* scales_f8,
@@ -178,7 +165,7 @@ cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
                                    cdq_packed* out) {
     cdq_status st = check_shape(rows, cols, n_states);
     if (st) return st;
-    if (!q || !scales_f8 || !out || !out->codes || !out->scales || !out->res_ptr ||
+    if (!q || !scales_f8 || !out || !out->units || !out->res_ptr ||
         (n_res > 0 && (!ridx || !rval || !out->res_ent || !out->res_q)) || n_res < 0)
         return CDQ_ERR_ARG;
     Geometry g = geometry(rows, cols, n_states);
@@ -192,38 +179,42 @@ cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
         if (f < 0 || f >= numel || (i && f <= ridx[i - 1])) return CDQ_ERR_ARG;
         mask[f / 32] |= 1u << (f % 32);
     }
-    uint8_t sym[32];
-    uint32_t w[5];
-    for (int64_t rb = 0; rb < g.rb; ++rb) {
-        for (int lane = 0; lane < 32; ++lane) {
-            int64_t row = rb * 32 + lane;
-            for (int64_t c = 0; c < g.kt; ++c) {
-                uint8_t sc = 0;
-                if (row < rows) {
-                    int64_t t = row * g.kt + c;
-                    for (int e = 0; e < 32; ++e) {
-                        uint8_t v = q[t * 32 + e];
-                        if (v >= n_states) return CDQ_ERR_ARG;
-                        sym[e] = ((mask[t] >> e) & 1u) ? res_sym : v;
-                    }
-                    sc = scales_f8[t];
-                } else {
-                    memset(sym, res_sym, 32);
+    for (int64_t t = 0; t < n_tiles; ++t)
+        for (int e = 0; e < 32; ++e)
+            if (q[t * 32 + e] >= n_states) return CDQ_ERR_ARG;
+    auto sym = [&](int64_t t, int e) -> uint32_t {
+        return ((mask[t] >> e) & 1u) ? res_sym : q[t * 32 + e];
+    };
+    memset(out->units, 0, (size_t)(g.r16 * g.kp * g.unit));
+    for (int64_t b16 = 0; b16 < g.r16; ++b16) {
+        for (int64_t cp = 0; cp < g.kp; ++cp) {
+            for (int lane = 0; lane < 32; ++lane) {
+                uint32_t w[5] = {0, 0, 0, 0, 0};
+                for (int s = 0; s < 16; ++s) {
+                    int ri, t, p;
+                    slot_pos(lane, s, &ri, &t, &p);
+                    const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+                    if (row >= rows || c >= g.kt) continue;
+                    const int64_t tile = row * g.kt + c;
+                    put_slot(n_states, w, s, pair_code(n_states, sym(tile, 2 * p), sym(tile, 2 * p + 1)));
                 }
-                encode_tile(sym, n_states, w);
-                for (int wd = 0; wd < g.words; ++wd) out->codes[code_word_index(g, rb, c, lane, wd)] = w[wd];
-                out->scales[scale_index(g, rb, c, lane)] = sc;
+                for (int wd = 0; wd < g.words; ++wd) memcpy(out->units + word_offset(g, b16, cp, lane, wd), &w[wd], 4);
             }
-            for (int64_t c = g.kt; c < g.kt4 * 4; ++c) out->scales[scale_index(g, rb, c, lane)] = 0;
+            for (int ri = 0; ri < 16; ++ri)
+                for (int t = 0; t < 2; ++t) {
+                    const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+                    if (row < rows && c < g.kt) out->units[scale_offset(g, b16, cp, ri, t)] = scales_f8[row * g.kt + c];
+                }
         }
     }
-    // residual CSR: bucket (rb, group, lane)
-    const int64_t nb = g.rb * g.kg * 32;
+    // residual CSR: bucket (b16, group, row in block)
+    const int64_t nb = g.r16 * g.kg * 16;
     std::vector<int64_t> cnt(nb + 1, 0);
-    for (int64_t i = 0; i < n_res; ++i) {
-        int64_t row = ridx[i] / cols, col = ridx[i] % cols;
-        cnt[bucket_index(g, row / 32, (col / 32) / kGroupTiles, (int)(row % 32))]++;
-    }
+    auto bucket_of = [&](int64_t f) {
+        const int64_t row = f / cols, col = f % cols;
+        return bucket_index(g, row / 16, (col / 32) / kGroupTiles, (int)(row % 16));
+    };
+    for (int64_t i = 0; i < n_res; ++i) cnt[bucket_of(ridx[i])]++;
     int64_t run = 0;
     for (int64_t b = 0; b < nb; ++b) {
         out->res_ptr[b] = (uint32_t)run;
@@ -233,10 +224,8 @@ cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
     }
     out->res_ptr[nb] = (uint32_t)run;
     for (int64_t i = 0; i < n_res; ++i) {
-        int64_t row = ridx[i] / cols, col = ridx[i] % cols;
-        int64_t b = bucket_index(g, row / 32, (col / 32) / kGroupTiles, (int)(row % 32));
-        int64_t pos = cnt[b]++;
-        out->res_ent[pos] = ((uint32_t)col << 16) | rval[i];
+        const int64_t pos = cnt[bucket_of(ridx[i])]++;
+        out->res_ent[pos] = ((uint32_t)(ridx[i] % cols) << 16) | rval[i];
         out->res_q[pos] = q[ridx[i]];
     }
     out->rows = rows;
@@ -248,43 +237,44 @@ cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
 
 cdq_status cdq_host_to_reference(const cdq_packed* in, uint8_t* q, uint8_t* scales_f8,
                                  int64_t* ridx, uint16_t* rval) {
-    if (!in || !q || !scales_f8) return CDQ_ERR_ARG;
+    if (!in || !q || !scales_f8 || !in->units || !in->res_ptr) return CDQ_ERR_ARG;
     cdq_status st = check_shape(in->rows, in->cols, in->n_states);
     if (st) return st;
     if (in->n_res > 0 && (!ridx || !rval || !in->res_ent || !in->res_q)) return CDQ_ERR_ARG;
-    Geometry g = geometry(in->rows, in->cols, in->n_states);
-    uint32_t w[5] = {0, 0, 0, 0, 0};
-    for (int64_t row = 0; row < in->rows; ++row) {
-        int64_t rb = row / 32;
-        int lane = (int)(row % 32);
-        for (int64_t c = 0; c < g.kt; ++c) {
-            int64_t t = row * g.kt + c;
-            for (int wd = 0; wd < g.words; ++wd) w[wd] = in->codes[code_word_index(g, rb, c, lane, wd)];
-            decode_tile(w, in->n_states, q + t * 32);
-            scales_f8[t] = in->scales[scale_index(g, rb, c, lane)];
-        }
-        // residuals of this row in flat order: groups ascending, cols ascending
-        int64_t k = 0;
-        for (int64_t gr = 0; gr < g.kg; ++gr) {
-            int64_t b = bucket_index(g, rb, gr, lane);
-            for (uint32_t e = in->res_ptr[b]; e < in->res_ptr[b + 1]; ++e) {
-                uint32_t col = in->res_ent[e] >> 16;
-                int64_t f = row * in->cols + col;
-                q[f] = in->res_q[e];
-                (void)k;
+    const int ns = in->n_states;
+    Geometry g = geometry(in->rows, in->cols, ns);
+    for (int64_t b16 = 0; b16 < g.r16; ++b16) {
+        for (int64_t cp = 0; cp < g.kp; ++cp) {
+            for (int lane = 0; lane < 32; ++lane) {
+                uint32_t w[5] = {0, 0, 0, 0, 0};
+                for (int wd = 0; wd < g.words; ++wd) memcpy(&w[wd], in->units + word_offset(g, b16, cp, lane, wd), 4);
+                for (int s = 0; s < 16; ++s) {
+                    int ri, t, p;
+                    slot_pos(lane, s, &ri, &t, &p);
+                    const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+                    if (row >= in->rows || c >= g.kt) continue;
+                    const int64_t tile = row * g.kt + c;
+                    pair_syms(ns, get_slot(ns, w, s), &q[tile * 32 + 2 * p], &q[tile * 32 + 2 * p + 1]);
+                }
             }
+            for (int ri = 0; ri < 16; ++ri)
+                for (int t = 0; t < 2; ++t) {
+                    const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+                    if (row < in->rows && c < g.kt) scales_f8[row * g.kt + c] = in->units[scale_offset(g, b16, cp, ri, t)];
+                }
         }
     }
-    // flat residual list: rows ascending, then groups, then cols
+    // residual positions: the quantizer's index, and the flat residual list in
+    // row-major order (rows ascending, then groups, then columns)
     int64_t n = 0;
     for (int64_t row = 0; row < in->rows; ++row) {
-        int64_t rb = row / 32;
-        int lane = (int)(row % 32);
         for (int64_t gr = 0; gr < g.kg; ++gr) {
-            int64_t b = bucket_index(g, rb, gr, lane);
+            const int64_t b = bucket_index(g, row / 16, gr, (int)(row % 16));
             for (uint32_t e = in->res_ptr[b]; e < in->res_ptr[b + 1]; ++e) {
                 if (n >= in->n_res) return CDQ_ERR_FORMAT;
-                ridx[n] = row * in->cols + (in->res_ent[e] >> 16);
+                const int64_t f = row * in->cols + (in->res_ent[e] >> 16);
+                q[f] = in->res_q[e];
+                ridx[n] = f;
                 rval[n] = (uint16_t)(in->res_ent[e] & 0xFFFFu);
                 ++n;
             }
@@ -362,7 +352,6 @@ cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
         pos += 2 + ib;
         int64_t bb = blob_bytes(tc);
         if (pos + bb > len || n + tc > t->n_res) return CDQ_ERR_FORMAT;
-        int off_prev = -1;
         int64_t first = n;
         for (int j = 0; j < tc; ++j) {
             int off = (int)get_bits(data + pos, bb, 21LL * j, 5);
@@ -370,7 +359,6 @@ cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
             ridx[n] = k * 32 + off;
             rval[n] = v;
             ++n;
-            (void)off_prev;
         }
         // offsets inside a tile are written in ascending order by the packer;
         // accept any order of distinct offsets, reject duplicates

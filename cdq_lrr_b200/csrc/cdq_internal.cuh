@@ -5,40 +5,50 @@
 #include <stdint.h>
 
 #include "cdq.h"
+#include "cdq_common.cuh"
 
 namespace cdq {
 
 // One GEMV of a launch, with geometry precomputed on the host.
 struct GemvJob {
-    const uint32_t* codes;
-    const uint8_t* scales;
+    const uint8_t* units;
     const uint32_t* res_ptr;
     const uint32_t* res_ent;
     const uint16_t* x;
     void* y;
     const uint16_t* bias;
-    float* partial;       // split-K slots [m][kg][rb*32]
-    uint32_t* counters;   // [rb], zero between calls
-    int64_t item_begin;   // first work item of this job in the launch
-    int32_t rows, cols, rb, kt, kt4, kg;
+    float* partial;       // per-group partial sums [m][kg][r16*16] (workspace)
+    void* reserved_ptr;
+    int64_t item_begin;   // first work item (row block x residual group) of this job
+    int32_t rows, cols, r16, kt, kp, kg;
     int32_t out_f32;
-    int32_t pad_;
+    uint32_t n_res;       // residual entries; bucket pointers are clamped to it
+    int32_t rb_begin;     // first fix-up block of this job (set by the launcher)
+    int32_t reserved0;
 };
+static_assert(sizeof(GemvJob) == 112, "GemvJob layout");
 
-constexpr int kMaxJobs = 192;  // 192 x 104-byte jobs fit the 32 KB kernel-parameter space
+constexpr int kMaxJobs = 192;  // 192 x 112-byte jobs fit the 32 KB kernel-parameter space
 
 template <int MAXJ>
 struct GemvBatch {
     int64_t total_items;
     int32_t n;
-    int32_t pad_;
+    int32_t total_row_blocks;  // fix-up pass work
     GemvJob jobs[MAXJ];
 };
+
+// Workspace of one linear call: float32 partial sums per (batch column,
+// residual group, padded row), 256-byte aligned size.
+inline int64_t linear_workspace_need(const Geometry& g, int64_t m) {
+    return (m * g.kg * g.r16 * 16 * 4 + 255) / 256 * 256;
+}
 
 cudaError_t upload_lattices();
 cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_t s, int sms);
 cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cudaStream_t s,
                                 int sms);
+cudaError_t gemv_read_error(int* out);
 
 cudaError_t dequant_setup();
 cudaError_t quantize_setup();

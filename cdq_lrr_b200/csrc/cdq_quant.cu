@@ -88,7 +88,7 @@ __device__ __forceinline__ void load_tile(const uint16_t* w, int64_t t, float (&
 
 // 1. per-tile sigma code and variance
 __global__ void k_stats(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, int ns,
-                        uint8_t* __restrict__ scales, WS ws) {
+                        uint8_t* __restrict__ units, WS ws) {
     const Geometry g = geometry(rows, cols, ns);
     const int64_t n_tiles = (int64_t)rows * g.kt;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tiles;
@@ -106,7 +106,7 @@ __global__ void k_stats(const uint16_t* __restrict__ w, int32_t rows, int32_t co
         if (nan) sig = __uint_as_float(0x7FC00000u);
         else if (sig < 1e-8f) sig = __uint_as_float(0x322C0000u);  // bf16(1e-8): clamp(min=1e-8)
         const int64_t row = t / g.kt, c = t % g.kt;
-        scales[scale_index(g, row / 32, c, (int)(row % 32))] = fp8_encode(sig);
+        units[scale_offset(g, row / 16, c / 2, (int)(row % 16), (int)(c % 2))] = fp8_encode(sig);
         double mean = 0.0, m2 = 0.0;
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
@@ -236,19 +236,63 @@ __device__ __forceinline__ Rule make_rule(const QState* st) {
     return r;
 }
 
-// 3/4b. residual count of every bucket (row, residual group)
+// Residual mask of one tile (bit e set: element e becomes a residual).
+// Normal rule: saliency >= threshold (code/cdq_lrr_qwen05.py:91). Top-k
+// fallback (:93-96): saliency > v_k, or == v_k among the first `need` equal
+// saliencies in flat order (tie_base = equal saliencies before this tile).
+__device__ __forceinline__ uint32_t tile_mask(const float (&x)[32], float var, const Rule& rule,
+                                              uint32_t tie_base) {
+    uint32_t m = 0, tie = tie_base;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const float sl = sal_of(x[e], var);
+        bool inc;
+        if (rule.fallback) {
+            inc = sl > rule.vk;
+            if (sl == rule.vk) {
+                inc = tie < rule.need;
+                ++tie;
+            }
+        } else {
+            inc = sl >= rule.thr;
+        }
+        m |= (uint32_t)inc << e;
+    }
+    return m;
+}
+
+// Nearest lattice centroid of x / sigma_q: float32 division, |d| per centroid,
+// first index of the minimum, NaN counts as the minimum (:104-110).
+template <int NS>
+__device__ __forceinline__ uint32_t snap(float x, float sq) {
+    const float nrm = __fdiv_rn(x, sq);
+    uint32_t q = 0;
+    float best = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[0] : q_lat16[0]));
+    if (isnan(best)) return 0;
+    for (int j = 1; j < NS; ++j) {
+        const float d = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[j] : q_lat16[j]));
+        if (isnan(d)) return (uint32_t)j;
+        if (d < best) {
+            best = d;
+            q = j;
+        }
+    }
+    return q;
+}
+
+// 3/4b. residual count of every bucket (16-row block, residual group, row)
 __global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, int ns,
                         uint32_t* __restrict__ counts, WS ws, int fallback_pass) {
     const QState* st = ws.st;
     if (fallback_pass && !st->fallback) return;
     const Geometry g = geometry(rows, cols, ns);
-    const int64_t nb = g.rb * g.kg * 32;
+    const int64_t nb = g.r16 * g.kg * 16;
     const Rule rule = make_rule(st);
     unsigned long long total = 0;
     for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
          b += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t rb = b / (g.kg * 32), grp = (b / 32) % g.kg;
-        const int64_t row = rb * 32 + (b & 31);
+        const int64_t b16 = b / (g.kg * 16), grp = (b / 16) % g.kg;
+        const int64_t row = b16 * 16 + (b & 15);
         uint32_t cnt = 0;
         if (row < rows) {
             const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
@@ -256,23 +300,7 @@ __global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t co
                 const int64_t t = row * g.kt + c;
                 float x[32];
                 load_tile(w, t, x);
-                const float var = ws.var[t];
-                uint32_t tie = fallback_pass ? ws.tie[t] : 0u;
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float s = sal_of(x[e], var);
-                    bool inc;
-                    if (fallback_pass) {
-                        inc = s > rule.vk;
-                        if (s == rule.vk) {
-                            inc = tie < rule.need;
-                            ++tie;
-                        }
-                    } else {
-                        inc = s >= rule.thr;
-                    }
-                    cnt += inc;
-                }
+                cnt += __popc(tile_mask(x, ws.var[t], rule, rule.fallback ? ws.tie[t] : 0u));
             }
         }
         counts[b] = cnt;
@@ -361,97 +389,84 @@ __global__ void __launch_bounds__(1024) k_scan(uint32_t* data, int64_t n, const 
     }
 }
 
-// 6. per bucket: lattice snap, residual substitution, codes and residual entries
+// 6a. codes: one thread per (unit, lane), its 16 slots (rows g, g+8 of the
+// 16-row block, both tiles of the pair): lattice snap with the residual
+// positions replaced by the zero-valued residual symbol.
 template <int NS>
-__global__ void k_pack(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, cdq_packed out,
-                       WS ws) {
+__global__ void k_pack_codes(const uint16_t* __restrict__ w, int32_t rows, int32_t cols,
+                             cdq_packed out, WS ws) {
     const Geometry g = geometry(rows, cols, NS);
-    const int64_t nb = g.rb * g.kg * 32;
     const Rule rule = make_rule(ws.st);
-    constexpr int kStates = NS;
     constexpr uint32_t kRes = NS == 26 ? kResidualSym26 : kResidualSym16;
+    const int64_t total = g.r16 * g.kp * 32;
+    for (int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tid < total;
+         tid += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(tid & 31);
+        const int64_t un = tid >> 5, b16 = un / g.kp, cp = un % g.kp;
+        uint32_t wd[5] = {0, 0, 0, 0, 0};
+        const int t = (lane & 3) >> 1;  // every slot of the lane lies in one tile
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {  // rows g and g + 8
+            const int ri = (lane >> 2) + 8 * h;
+            const int64_t row = b16 * 16 + ri, c = cp * 2 + t;
+            if (row >= rows || c >= g.kt) continue;
+            const int64_t tl = row * g.kt + c;
+            float x[32];
+            load_tile(w, tl, x);
+            const uint32_t m = tile_mask(x, ws.var[tl], rule, rule.fallback ? ws.tie[tl] : 0u);
+            const float sq = bf16_to_f32(fp8_to_bf16(out.units[scale_offset(g, b16, cp, ri, t)]));
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {  // pair p = 8(c&1) + 2s + j -> slot q = 4s + h + 2j
+                const int sl = k >> 1, j = k & 1;
+                const int p = 8 * (lane & 1) + 2 * sl + j;
+                const int q = 4 * sl + (h | (j << 1));
+                const uint32_t a = ((m >> (2 * p)) & 1u) ? kRes : snap<NS>(x[2 * p], sq);
+                const uint32_t bb = ((m >> (2 * p + 1)) & 1u) ? kRes : snap<NS>(x[2 * p + 1], sq);
+                if (NS == 26) {
+                    const uint32_t code = a * 27u + bb;
+                    const int bit = 10 * q, w0 = bit >> 5, off = bit & 31;
+                    wd[w0] |= code << off;
+                    if (off > 22) wd[w0 + 1] |= code >> (32 - off);
+                } else {
+                    wd[q >> 2] |= (a | (bb << 4)) << (8 * (q & 3));
+                }
+            }
+        }
+        for (int k = 0; k < g.words; ++k)
+            *reinterpret_cast<uint32_t*>(out.units + word_offset(g, b16, cp, lane, k)) = wd[k];
+    }
+}
+
+// 6b. residual entries: one thread per bucket, columns in ascending order.
+template <int NS>
+__global__ void k_pack_res(const uint16_t* __restrict__ w, int32_t rows, int32_t cols,
+                           cdq_packed out, WS ws) {
+    const Geometry g = geometry(rows, cols, NS);
+    const int64_t nb = g.r16 * g.kg * 16;
+    const Rule rule = make_rule(ws.st);
     for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
          b += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t rb = b / (g.kg * 32), grp = (b / 32) % g.kg;
-        const int lane = (int)(b & 31);
-        const int64_t row = rb * 32 + lane;
-        const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
+        const int64_t b16 = b / (g.kg * 16), grp = (b / 16) % g.kg;
+        const int ri = (int)(b & 15);
+        const int64_t row = b16 * 16 + ri;
+        if (row >= rows) continue;
         uint32_t pos = out.res_ptr[b];
+        const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
         for (int64_t c = c0; c < c1; ++c) {
-            uint8_t sym[32];
-            if (row < rows) {
-                const int64_t t = row * g.kt + c;
-                float x[32];
-                load_tile(w, t, x);
-                const float var = ws.var[t];
-                const float sq = bf16_to_f32(fp8_to_bf16(out.scales[scale_index(g, rb, c, lane)]));
-                uint32_t tie = rule.fallback ? ws.tie[t] : 0u;
-                const uint16_t* wt = w + t * 32;
-#pragma unroll 1
-                for (int e = 0; e < 32; ++e) {
-                    const float nrm = __fdiv_rn(x[e], sq);
-                    uint32_t q = 0;
-                    float best = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[0] : q_lat16[0]));
-                    if (!isnan(best)) {
-                        for (int j = 1; j < kStates; ++j) {
-                            const float d = fabsf(__fsub_rn(nrm, NS == 26 ? q_lat26[j] : q_lat16[j]));
-                            if (isnan(d)) {
-                                q = j;
-                                break;
-                            }
-                            if (d < best) {
-                                best = d;
-                                q = j;
-                            }
-                        }
-                    }
-                    const float s = sal_of(x[e], var);
-                    bool inc;
-                    if (rule.fallback) {
-                        inc = s > rule.vk;
-                        if (s == rule.vk) {
-                            inc = tie < rule.need;
-                            ++tie;
-                        }
-                    } else {
-                        inc = s >= rule.thr;
-                    }
-                    if (inc) {
-                        out.res_ent[pos] = ((uint32_t)(c * 32 + e) << 16) | wt[e];
-                        out.res_q[pos] = (uint8_t)q;
-                        ++pos;
-                        sym[e] = (uint8_t)kRes;
-                    } else {
-                        sym[e] = (uint8_t)q;
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) sym[e] = (uint8_t)kRes;
-            }
-            // pair codes
-            if (NS == 26) {
-                uint32_t acc[5] = {0, 0, 0, 0, 0};
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint32_t code = (uint32_t)sym[2 * j] * 27u + sym[2 * j + 1];
-                    const int bit = 10 * j, wd = bit >> 5, off = bit & 31;
-                    acc[wd] |= code << off;
-                    if (off > 22) acc[wd + 1] |= code >> (32 - off);
-                }
-#pragma unroll
-                for (int wd = 0; wd < 5; ++wd) out.codes[code_word_index(g, rb, c, lane, wd)] = acc[wd];
-            } else {
-#pragma unroll
-                for (int wd = 0; wd < 4; ++wd) {
-                    uint32_t v = 0;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int j = wd * 4 + k;
-                        v |= (uint32_t)(sym[2 * j] | (sym[2 * j + 1] << 4)) << (8 * k);
-                    }
-                    out.codes[code_word_index(g, rb, c, lane, wd)] = v;
-                }
+            const int64_t tl = row * g.kt + c;
+            float x[32];
+            load_tile(w, tl, x);
+            uint32_t m = tile_mask(x, ws.var[tl], rule, rule.fallback ? ws.tie[tl] : 0u);
+            if (!m) continue;
+            const float sq = bf16_to_f32(fp8_to_bf16(
+                out.units[scale_offset(g, b16, c / 2, ri, (int)(c % 2))]));
+            const uint16_t* wt = w + tl * 32;
+            while (m) {
+                const int e = __ffs(m) - 1;
+                m &= m - 1;
+                out.res_ent[pos] = ((uint32_t)(c * 32 + e) << 16) | wt[e];
+                out.res_q[pos] = (uint8_t)snap<NS>(x[e], sq);
+                ++pos;
             }
         }
     }
@@ -483,7 +498,7 @@ cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
     cudaError_t e;
     const Geometry g = geometry(a.rows, a.cols, a.n_states);
     const int64_t numel = (int64_t)a.rows * a.cols, n_tiles = numel / 32;
-    const int64_t nb = g.rb * g.kg * 32;
+    const int64_t nb = g.r16 * g.kg * 16;
     WS ws = carve(a.ws, n_tiles);
 
     // torch.quantile's rank rule in float32, evaluated here once
@@ -499,11 +514,11 @@ cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
     const int tile_blocks = (int)std::min<int64_t>((n_tiles + threads - 1) / threads, (int64_t)sms * 8);
     const int bucket_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((nb + threads - 1) / threads, (int64_t)sms * 8));
 
-    if ((e = cudaMemsetAsync(a.out.scales, 0, (size_t)(g.rb * g.kt4 * 128), s)) != cudaSuccess) return e;
+    if ((e = cudaMemsetAsync(a.out.units, 0, (size_t)(g.r16 * g.kp * g.unit), s)) != cudaSuccess) return e;
     if ((e = cudaMemsetAsync(ws.hist, 0, (size_t)kSel * kHistBins * 4, s)) != cudaSuccess) return e;
     if ((e = cudaMemsetAsync(a.out.res_ptr + nb, 0, 4, s)) != cudaSuccess) return e;
     k_init<<<1, 1, 0, s>>>(ws, r_lo, r_hi);
-    k_stats<<<tile_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.scales, ws);
+    k_stats<<<tile_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.units, ws);
     k_hist<0><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 3u, 0, ws);
     k_find<0><<<1, 256, 0, s>>>(3u, 0, ws);
     k_hist<1><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 3u, 0, ws);
@@ -526,10 +541,15 @@ cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
     k_count<<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.res_ptr, ws, 1);
     // residual CSR offsets
     k_scan<<<1, 1024, 0, s>>>(a.out.res_ptr, nb + 1, nullptr);
-    if (a.n_states == 26)
-        k_pack<26><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
-    else
-        k_pack<16><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+    const int64_t lanes = g.r16 * g.kp * 32;
+    const int code_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((lanes + threads - 1) / threads, (int64_t)sms * 16));
+    if (a.n_states == 26) {
+        k_pack_codes<26><<<code_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+        k_pack_res<26><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+    } else {
+        k_pack_codes<16><<<code_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+        k_pack_res<16><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+    }
     k_info<<<1, 1, 0, s>>>(ws, a.out.res_ptr, nb, a.info, k);
     return cudaGetLastError();
 }

@@ -57,7 +57,7 @@ class CDQLinear(nn.Module):
     @property
     def device_pack(self) -> ops.DevicePack:
         return ops.DevicePack(self.shape[0], self.shape[1], self.n_states, self._n_res,
-                              self.codes, self.scales, self.res_ptr, self.res_ent, self.res_q,
+                              self.units, self.res_ptr, self.res_ent, self.res_q,
                               _ws=self._ws)
 
     def _ref(self):

@@ -34,13 +34,13 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
 class DevicePack:
     """One packed weight in the device layout of include/cdq.h.
 
-    uint32 buffers are held as int32 tensors (bit patterns)."""
+    The units are a uint8 tensor; uint32 buffers are held as int32 tensors
+    (bit patterns)."""
     rows: int
     cols: int
     n_states: int
     n_res: int
-    codes: torch.Tensor
-    scales: torch.Tensor
+    units: torch.Tensor
     res_ptr: torch.Tensor
     res_ent: torch.Tensor
     res_q: torch.Tensor
@@ -48,7 +48,7 @@ class DevicePack:
 
     @property
     def device(self) -> torch.device:
-        return self.codes.device
+        return self.units.device
 
     @property
     def n_tiles(self) -> int:
@@ -58,15 +58,14 @@ class DevicePack:
         p = L.cdq_packed()
         p.rows, p.cols, p.n_states, p.reserved0 = self.rows, self.cols, self.n_states, 0
         p.n_res = self.n_res
-        p.codes = self.codes.data_ptr()
-        p.scales = self.scales.data_ptr()
+        p.units = self.units.data_ptr()
         p.res_ptr = self.res_ptr.data_ptr()
         p.res_ent = self.res_ent.data_ptr() if self.res_ent.numel() else None
         p.res_q = self.res_q.data_ptr() if self.res_q.numel() else None
         return p
 
     def tensors(self) -> dict[str, torch.Tensor]:
-        return {"codes": self.codes, "scales": self.scales, "res_ptr": self.res_ptr,
+        return {"units": self.units, "res_ptr": self.res_ptr,
                 "res_ent": self.res_ent, "res_q": self.res_q}
 
     @classmethod
@@ -75,8 +74,7 @@ class DevicePack:
         s = L.sizes(rows, cols, n_states)
         dev = torch.device(device)
         return cls(rows, cols, n_states, 0,
-                   torch.empty(s.codes_bytes // 4, dtype=torch.int32, device=dev),
-                   torch.empty(s.scales_bytes, dtype=torch.uint8, device=dev),
+                   torch.empty(s.units_bytes, dtype=torch.uint8, device=dev),
                    torch.empty(s.res_ptr_count, dtype=torch.int32, device=dev),
                    torch.empty(max(res_capacity, 0), dtype=torch.int32, device=dev),
                    torch.empty(max(res_capacity, 0), dtype=torch.uint8, device=dev))
@@ -136,14 +134,14 @@ class DevicePack:
         counts = (rp[1:] - rp[:-1])
         kg = (kt + 31) // 32
         b = torch.arange(counts.numel())
-        rows = (b // (kg * 32)) * 32 + (b % 32)
+        rows = (b // (kg * 16)) * 16 + (b % 16)
         row_of = torch.repeat_interleave(rows, counts)
         col = (ent >> 16) & 0xFFFF
         tile = row_of * kt + col // TILE
         tc = torch.bincount(tile, minlength=self.n_tiles)
         return int(self.n_tiles * (2 + ib) + ((tc * 21 + 7) // 8).sum().item())
 
-    # ---- workspace of cdq_linear (zero-filled once, kept by the pack) ----
+    # ---- workspace of cdq_linear (float32 group sums, kept by the pack) ----
     def linear_workspace(self, m: int) -> torch.Tensor:
         dev = self.device
         key = (dev, m)
@@ -249,7 +247,11 @@ class GroupedLinear:
             j.workspace_bytes = ws.numel()
             j.out_f32 = 1 if t.y.dtype == torch.float32 else 0
         self.device = self.tasks[0].x.device if self.tasks else None
-        self.launches = len({t.pack.n_states for t in self.tasks}) if self.tasks else 0
+        # per lattice size, per batch of at most L.MAX_JOBS jobs: a streaming pass and a fix-up pass
+        per_ns = {}
+        for t in self.tasks:
+            per_ns[t.pack.n_states] = per_ns.get(t.pack.n_states, 0) + 1
+        self.launches = sum(2 * -(-n // L.MAX_JOBS) for n in per_ns.values())
 
     def __call__(self) -> None:
         if self.tasks:

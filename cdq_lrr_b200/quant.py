@@ -20,7 +20,7 @@ materialises w_hat. Differences from the reference, all deliberate:
   tables); any other ``lattice`` raises ValueError;
 * the returned dict also carries ``"device_pack"``, the packed weight in the
   device layout, so CDQLinear does not repack it;
-* CDQLinear stores the device pack as its buffers (``codes``, ``scales``,
+* CDQLinear stores the device pack as its buffers (``units``,
   ``res_ptr``, ``res_ent``, ``res_q``); the reference buffer names
   (``quant_indices``, ``scales_f8``, ``scales_bf16``, ``residual_indices``,
   ``residual_values``, ``lattice``) are read-only properties rebuilt from it,
@@ -179,7 +179,7 @@ class CDQLinear(nn.Module):
     @property
     def device_pack(self) -> ops.DevicePack:
         dp = ops.DevicePack(self.orig_shape[0], self.orig_shape[1], self.n_states, self._n_res,
-                            self.codes, self.scales, self.res_ptr, self.res_ent, self.res_q,
+                            self.units, self.res_ptr, self.res_ent, self.res_q,
                             _ws=self._ws)
         return dp
 
@@ -240,7 +240,7 @@ class CDQLinear(nn.Module):
             dp = ops.DevicePack.from_reference(
                 state_dict[prefix + "quant_indices"], state_dict[prefix + "scales_f8"],
                 state_dict[prefix + "residual_indices"], state_dict[prefix + "residual_values"],
-                rows, cols, n_states, device=self.codes.device)
+                rows, cols, n_states, device=self.units.device)
             self.n_states = n_states
             self._n_res = dp.n_res
             self._ws.clear()
@@ -253,9 +253,9 @@ class CDQLinear(nn.Module):
                     self.bias.copy_(state_dict.pop(prefix + "bias"))
             return
         # own format: buffers may change length (residual count)
-        for k in ("codes", "scales", "res_ptr", "res_ent", "res_q"):
+        for k in ("units", "res_ptr", "res_ent", "res_q"):
             if prefix + k in state_dict:
-                setattr(self, k, state_dict[prefix + k].to(self.codes.device))
+                setattr(self, k, state_dict[prefix + k].to(self.units.device))
         self._n_res = int(self.res_ent.numel())
         self._ws.clear()
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,

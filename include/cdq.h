@@ -51,27 +51,34 @@ typedef enum cdq_status {
 #define CDQ_MAX_BATCH 8         /* cdq_linear serves M <= CDQ_MAX_BATCH      */
 
 /*
- * Device layout of one packed weight ("device pack").
+ * Device layout of one packed weight ("device pack"), built so that one
+ * 128-bit (+32-bit) load per lane gives each lane of a warp exactly the pair
+ * codes of its m16n8k16 tensor-core A fragment.
  *
- * Rows are grouped in row blocks of 32 (RB = ceil(rows/32)); a row block's
- * tile column c (KT = cols/32 columns) holds the 32 tiles of its rows at c.
- *   codes   : per (row block, tile column) 32 lanes x W words, W = 5 (26-state)
- *             or 4 (16-state). Lane l is row 32*rb + l. Words 0..3 of all
- *             lanes come first as 16-byte groups (lane l at byte 16*l), then
- *             word 4 of all lanes (26-state only).
- *             26-state: element pair j (weights 2j, 2j+1) has the code
- *             s[2j]*27 + s[2j+1] in bits [10j, 10j+10) of the tile's 160-bit
- *             little-endian word stream, with s = lattice index 0..25, or 26
- *             at a residual position (contributes zero).
- *             16-state: byte j = s[2j] | s[2j+1] << 4, residual positions
- *             hold 7 (the lattice's exact zero).
- *   scales  : float8 e4m3fn sigma codes, [RB][ceil(KT/4)][32 lanes][4 tiles].
- *   res_ptr : residual CSR offsets, RB*KG*32 + 1 entries (KG = ceil(KT/32));
- *             bucket (rb, g, l) lists row 32*rb+l, tile columns [32g, 32g+32).
+ * Rows form blocks of 16 (R16 = ceil(rows/16)), tile columns (32 weights of
+ * a row) form pairs (KP = ceil(KT/2), KT = cols/32). A unit = one 16-row block
+ * x one tile-column pair = 32 tiles, stored as 672 bytes (26 states) or 544
+ * bytes (16 states), units ordered [R16][KP]:
+ *   bytes [0, 512)   lane l's code words 0..3 (16 bytes at 16*l);
+ *   bytes [512, 640) lane l's code word 4 (26 states only);
+ *   then 32 bytes of fp8 e4m3fn scales: word g holds the scales of
+ *   (row g, tile 0), (row g, tile 1), (row g+8, tile 0), (row g+8, tile 1).
+ * Lane l = 4g + c carries 16 slots q = 8t + 4s + i (t: tile of the pair, s:
+ * 16-element half of the tile, i = h + 2j): slot q is the element pair
+ * p = 8s + c + 4j (weights 2p, 2p+1) of row g + 8h of tile t.
+ *   26 states: slot q is the 10-bit code s[2p]*27 + s[2p+1] at bits
+ *   [10q, 10q+10) of the lane's 160-bit word stream, s = lattice index 0..25,
+ *   or 26 at a residual position (contributes zero);
+ *   16 states: byte q = s[2p] | s[2p+1] << 4, residual positions hold index 7
+ *   (the lattice's exact zero).
+ * Rows beyond `rows` and the missing tile of an odd KT hold zero codes and
+ * scale 0.
+ *   res_ptr : residual CSR offsets, R16*KG*16 + 1 entries (KG = ceil(KT/32));
+ *             bucket (b16, g, r) lists row 16*b16 + r, tile columns
+ *             [32g, 32g + 32).
  *   res_ent : n_res words (col << 16) | bf16 bits, sorted by bucket then col.
  *   res_q   : n_res lattice indices the quantizer chose at the residual
  *             positions (read only by format conversion, never by cdq_linear).
- * Padding rows of the last row block hold residual-slot codes and sigma 0.
  */
 typedef struct cdq_packed {
     int32_t rows;
@@ -79,8 +86,7 @@ typedef struct cdq_packed {
     int32_t n_states;      /* 26 or 16 */
     int32_t reserved0;
     int64_t n_res;         /* residual entries in res_ent / res_q */
-    uint32_t* codes;
-    uint8_t* scales;
+    uint8_t* units;        /* R16 * KP units of 672 or 544 bytes */
     uint32_t* res_ptr;
     uint32_t* res_ent;
     uint8_t* res_q;
@@ -88,55 +94,56 @@ typedef struct cdq_packed {
 
 /* Byte and element counts of a device pack and of the workspaces. */
 typedef struct cdq_sizes {
-    int64_t row_blocks;        /* RB */
-    int64_t tile_cols;         /* KT */
+    int64_t row_blocks;        /* R16 */
+    int64_t tile_pairs;        /* KP */
     int64_t res_groups;        /* KG */
-    int64_t codes_bytes;
-    int64_t scales_bytes;
+    int64_t units_bytes;
     int64_t res_ptr_count;     /* uint32 entries */
     int64_t max_res;           /* upper bound on n_res from cdq_quantize: 2k */
-    int64_t linear_workspace_bytes;    /* per call of cdq_linear (zeroed once) */
+    int64_t linear_workspace_bytes;    /* per call of cdq_linear (float32 group sums) */
     int64_t quantize_workspace_bytes;
 } cdq_sizes;
 
 /* Sizes for a [rows, cols] weight, the given lattice and residual fraction
- * (stc_frac only affects max_res). No CUDA calls. */
+ * (stc_frac only affects max_res) and largest batch. No CUDA calls. */
 CDQ_API cdq_status cdq_get_sizes(int32_t rows, int32_t cols, int32_t n_states, double stc_frac,
-                         int32_t max_batch, cdq_sizes* out);
+                                 int32_t max_batch, cdq_sizes* out);
 
 /* Library version string and the compiled device architecture. */
 CDQ_API const char* cdq_version(void);
 
 /*
  * y[M, rows] = x[M, cols] * w_hat^T (+ bias), fused: the packed weight is
- * streamed from HBM and dequantized in registers (bit-exact w_hat), FP32
- * accumulation, result rounded once to bf16. M <= CDQ_MAX_BATCH.
- * workspace: linear_workspace_bytes of device memory, zero-filled before the
- * first call and left zero-filled by every call (split-K accumulators); calls
- * that share one workspace must not overlap on the GPU.
+ * streamed from HBM and dequantized in registers (bit-exact w_hat pairs fed
+ * to the tensor cores), FP32 accumulation, result rounded once to bf16.
+ * M <= CDQ_MAX_BATCH.
+ * workspace: linear_workspace_bytes of device memory (float32 partial sums per
+ * residual group; no zeroing needed, every call writes the slots it reads).
+ * Two launches per call: the streaming pass, then a fix-up pass that adds the
+ * groups, the residual entries and the bias. Calls that share one workspace
+ * must not overlap on the GPU.
  * bias may be NULL. x, y, bias: bf16 bit patterns, row-major.
  * Replaces CDQLinear.forward, code/cdq_lrr_qwen05.py:196-198, and the
  * loader's CDQLinear.forward, code/cdq_loader.py:53-58.
  */
 CDQ_API cdq_status cdq_linear(const cdq_packed* w, const uint16_t* x, int64_t m, uint16_t* y,
-                      const uint16_t* bias, void* workspace, size_t workspace_bytes,
-                      void* stream);
+                              const uint16_t* bias, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 /* As cdq_linear, output in float32 (no final bf16 rounding). */
 CDQ_API cdq_status cdq_linear_f32(const cdq_packed* w, const uint16_t* x, int64_t m, float* y,
-                          const uint16_t* bias, void* workspace, size_t workspace_bytes,
-                          void* stream);
+                                  const uint16_t* bias, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 /*
  * As cdq_linear (bf16 output), for callers that cannot allocate device
  * memory: a plugin whose host process owns all device memory through its own
  * pool, or a path where a cudaMalloc, which may synchronise the device, is
- * not allowed. It allocates nothing and takes no workspace: its split-K
+ * not allowed. It allocates nothing and takes no workspace: its partial-sum
  * scratch is a 4 MiB array that the library holds on every GPU that loads it,
  * until the process exits. Weights whose scratch would exceed 4 MiB
- * (m * ceil(cols/1024) * ceil(rows/32) * 128 bytes, plus 4 bytes per 32 rows;
- * only weights with cols > 1024 use scratch) are rejected with
- * CDQ_ERR_WORKSPACE. All calls share the one array: calls that overlap on the
+ * (m * ceil(cols/1024) * ceil(rows/16) * 64 bytes, rounded up to 256) are
+ * rejected with CDQ_ERR_WORKSPACE. All calls share the one array: calls that overlap on the
  * GPU race, so issue them on one stream. The first call on a device sets up
  * the scratch address and lattice tables (host-side runtime calls); make it
  * before any stream capture.
@@ -195,8 +202,8 @@ typedef struct cdq_quant_info {
  * workspace: quantize_workspace_bytes of device memory (no zeroing needed).
  */
 CDQ_API cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
-                        double stc_frac, cdq_packed* out, cdq_quant_info* info,
-                        void* workspace, size_t workspace_bytes, void* stream);
+                                double stc_frac, cdq_packed* out, cdq_quant_info* info,
+                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Host-side conversions between the reference's pack tensors and the device
@@ -209,14 +216,14 @@ CDQ_API cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, i
  * decoded scales, offs (= residual_indices) and vals.
  */
 CDQ_API cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
-                                   const uint8_t* quant_indices, const uint8_t* scales_f8,
-                                   const int64_t* residual_indices,
-                                   const uint16_t* residual_values, int64_t n_res,
-                                   cdq_packed* out_host);
+                                           const uint8_t* quant_indices, const uint8_t* scales_f8,
+                                           const int64_t* residual_indices,
+                                           const uint16_t* residual_values, int64_t n_res,
+                                           cdq_packed* out_host);
 
 CDQ_API cdq_status cdq_host_to_reference(const cdq_packed* in_host, uint8_t* quant_indices,
-                                 uint8_t* scales_f8, int64_t* residual_indices,
-                                 uint16_t* residual_values);
+                                         uint8_t* scales_f8, int64_t* residual_indices,
+                                         uint16_t* residual_values);
 
 /*
  * .cdq file codec (host memory, synchronous), byte-exact with write_cdq /
@@ -239,26 +246,27 @@ typedef struct cdq_file_tensor {
 /* Parses the header and tensor table. *n_states gets 26 or 16. At most
  * max_tensors entries are written; *n_tensors gets the file's count. */
 CDQ_API cdq_status cdq_file_scan(const uint8_t* data, int64_t len, int32_t* n_states,
-                         cdq_file_tensor* tensors, int32_t max_tensors, int32_t* n_tensors);
+                                 cdq_file_tensor* tensors, int32_t max_tensors, int32_t* n_tensors);
 
 /* Decodes one scanned tensor into reference pack tensors (sizes from t). */
 CDQ_API cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
-                           const cdq_file_tensor* t, uint8_t* quant_indices,
-                           uint8_t* scales_f8, int64_t* residual_indices,
-                           uint16_t* residual_values);
+                                   const cdq_file_tensor* t, uint8_t* quant_indices,
+                                   uint8_t* scales_f8, int64_t* residual_indices,
+                                   uint16_t* residual_values);
 
 /* Encodes the header (magic, version, count, lattice) into out (capacity
  * cap); *written gets the byte count (8 + 52 or 8 + 32). */
 CDQ_API cdq_status cdq_file_encode_header(int32_t n_states, int32_t n_tensors, uint8_t* out,
-                                  int64_t cap, int64_t* written);
+                                          int64_t cap, int64_t* written);
 
 /* Encodes one tensor (name, dims, tile records) from reference pack tensors.
  * With out == NULL only *written (the required bytes) is computed. */
 CDQ_API cdq_status cdq_file_encode_tensor(const char* name, int32_t rows, int32_t cols,
-                                  int32_t n_states, const uint8_t* quant_indices,
-                                  const uint8_t* scales_f8, const int64_t* residual_indices,
-                                  const uint16_t* residual_values, int64_t n_res,
-                                  uint8_t* out, int64_t cap, int64_t* written);
+                                          int32_t n_states, const uint8_t* quant_indices,
+                                          const uint8_t* scales_f8,
+                                          const int64_t* residual_indices,
+                                          const uint16_t* residual_values, int64_t n_res,
+                                          uint8_t* out, int64_t cap, int64_t* written);
 
 #ifdef __cplusplus
 }

@@ -38,8 +38,9 @@ def test_version(L):
 
 def test_sizes_and_errors(L):
     s = L.sizes(4864, 896, 26)
-    assert s.row_blocks == 152 and s.tile_cols == 28 and s.res_groups == 1
-    assert s.codes_bytes == 152 * 28 * 5 * 128
+    assert s.row_blocks == 304 and s.tile_pairs == 14 and s.res_groups == 1
+    assert s.units_bytes == 304 * 14 * 672
+    assert L.sizes(896, 4864, 16).units_bytes == 56 * 76 * 544
     assert s.max_res == 2 * round(4864 * 896 * 0.0156)
     out = L.cdq_sizes()
     lib = L.lib()

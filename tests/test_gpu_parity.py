@@ -200,7 +200,7 @@ def test_large_projection_properties():
     counts = rp[1:] - rp[:-1]
     kg = (cols // 32 + 31) // 32
     b = torch.arange(counts.numel(), device="cuda")
-    row_of = torch.repeat_interleave((b // (kg * 32)) * 32 + (b % 32), counts)
+    row_of = torch.repeat_interleave((b // (kg * 16)) * 16 + (b % 16), counts)
     col = ent >> 16
     assert torch.equal(w_hat[row_of, col], w[row_of, col])
     # every non-residual weight is within half a lattice gap of sigma-scaled value
@@ -208,3 +208,24 @@ def test_large_projection_properties():
     y = ops.linear(pack, x, out_f32=True)
     y64 = (x.double() @ w_hat.double().T).cpu().numpy()
     _check_gemv(y, y64)
+
+
+@pytest.mark.parametrize("shape,ns,m", [((896, 896), 26, 1), ((4864, 896), 26, 8),
+                                        ((896, 4864), 16, 3), ((45, 1088), 26, 5),
+                                        ((300, 2080), 26, 2), ((17, 96), 16, 7),
+                                        ((130, 1056), 16, 1)])
+def test_linear_shapes_batches_bias(shape, ns, m):
+    """Odd tile counts (a phantom tile in the last pair), rows not a multiple
+    of 16, every batch size, bias, both lattices."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    rows, cols = shape
+    w = synth_weight(rows, cols, seed=rows + 3 * cols)
+    p = O.quantize(_bits(w), n_states=ns)
+    dp = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                       p["residual_values"], rows, cols, ns, device="cuda")
+    x = synth_activation(m, cols, seed=9).cuda()
+    bias = synth_activation(1, rows, seed=10)[0]
+    y = ops.linear(dp, x, bias.cuda(), out_f32=True)
+    torch.cuda.synchronize()
+    _check_gemv(y, O.linear_f64(O.dequantize(p), _bits(x), _bits(bias)))
