@@ -532,91 +532,99 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     }
 }
 
-// Fix-up pass: y[m, row] = sum over residual groups g, in group order, of
-// (partial sum of group g + the row's residual entries of group g, bf16 value
-// x activation in fp32, in entry order) + bias, rounded once to bf16 (or
-// stored as float32). One thread per (row, group) with all of its entries in
-// flight at once (the pass is a few dependent memory round trips per thread,
-// so the work per thread is sized for memory-level parallelism); the groups
-// of a row meet in shared memory. A block covers kFixThreads / kg rows of one
-// job; the job's activations are staged in shared memory when they fit.
+// Fix-up pass: y[m, row] = sum over groups (in group order) of the partial
+// sums + the residual entries of the row (bf16 value x activation, fp32) +
+// bias, rounded once to bf16 (or stored as float32). One warp per (job,
+// 16-row block); lane l = 2 * (row in block) + half, the two halves of a row
+// taking alternate residual entries and meeting in one shuffle. Grid row y
+// is job y; the job's fields are uniform reads of the launch record.
 constexpr int kFixThreads = 256;
-constexpr uint32_t kFixStageMax = 64u << 10;  // activations staged in shared memory up to this size
+constexpr int kFixGroups = 4;  // residual groups whose bucket bounds are fetched together
 
-template <int M, int MAXJ, bool kStaged>
-__global__ void __launch_bounds__(kFixThreads, 4)
+template <int M, int MAXJ>
+__global__ void __launch_bounds__(kFixThreads)
 fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
-    constexpr int kFixBatch = M <= 2 ? 16 : 4;
-    __shared__ float red[kFixThreads][M];
-    extern __shared__ __align__(16) uint16_t xs[];
-    // block -> (job, block of the job): rb_begin holds each job's first block
-    int j = 0;
-    if constexpr (MAXJ > 1) {
-        int lo = 0, hi = batch.n - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (batch.jobs[mid].rb_begin <= (int)blockIdx.x) lo = mid; else hi = mid - 1;
-        }
-        j = lo;
-    }
-    const GemvJob& J = batch.jobs[j];
+    const GemvJob& J = batch.jobs[blockIdx.y];  // one grid row per job
+    const int b16 = (int)(blockIdx.x * (kFixThreads / 32) + (threadIdx.x >> 5));
+    if (b16 >= J.r16) return;
+    const uint32_t* const res_ptr = J.res_ptr;
+    const uint32_t* const res_ent = J.res_ent;
+    const uint16_t* const x = J.x;
+    const float* const partial = J.partial;
     const int kg = J.kg, cols = J.cols, rows = J.rows;
-    const int rpb = kFixThreads / kg;  // rows per block
-    const int row0 = ((int)blockIdx.x - J.rb_begin) * rpb;
-    const uint16_t* x = J.x;
-    if constexpr (kStaged) {
-        // the job's activations, read coalesced once per block; the residual
-        // gathers then hit shared memory instead of one L1 sector per lane
-        const int words = M * cols / 8;
-        const uint4* src = reinterpret_cast<const uint4*>(J.x);
-        uint4* dst = reinterpret_cast<uint4*>(xs);
-        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = __ldg(src + i);
-        x = xs;
-    }
-    const int rl = (int)threadIdx.x / kg, grp = (int)threadIdx.x - rl * kg;
-    const int row = row0 + rl;
-    const bool live = rl < rpb && row < rows;
-    float val[M];
+    const uint32_t n_res = J.n_res;
+    const int64_t rpad = (int64_t)J.r16 * 16;
+    const int lane = threadIdx.x & 31, ri = lane >> 1, half = lane & 1;
+    const int row = b16 * 16 + ri;
+
+    // the group partial sums do not depend on the residuals: fetch them first
+    // (half 0 holds even batch columns, half 1 odd ones; kFixGroups groups at a time)
+    constexpr int kMH = (M + 1) / 2;
+    float psum[kMH];
 #pragma unroll
-    for (int n = 0; n < M; ++n) val[n] = 0.f;
-    uint32_t eb = 0, ee = 0;
-    if (live) {
-        const int64_t rpad = (int64_t)J.r16 * 16;
-        const int64_t bk = ((int64_t)(row >> 4) * kg + grp) * 16 + (row & 15);
-        eb = __ldg(J.res_ptr + bk);
-        ee = min(__ldg(J.res_ptr + bk + 1), J.n_res);
-#pragma unroll
-        for (int n = 0; n < M; ++n) val[n] = __ldcg(J.partial + ((int64_t)n * kg + grp) * rpad + row);
-    }
-    if constexpr (kStaged) __syncthreads();
+    for (int k = 0; k < kMH; ++k) psum[k] = 0.f;
+    const bool live = row < rows;
     float acc[M];
 #pragma unroll
     for (int n = 0; n < M; ++n) acc[n] = 0.f;
-    for (uint32_t e0 = eb; e0 < ee; e0 += kFixBatch) {
-        uint32_t en[kFixBatch];
+    for (int g0 = 0; g0 < kg; g0 += kFixGroups) {
+        float pv[kMH][kFixGroups];
+        uint32_t eb[kFixGroups], ee[kFixGroups];
 #pragma unroll
-        for (int t = 0; t < kFixBatch; ++t) en[t] = e0 + t < ee ? __ldg(J.res_ent + e0 + t) : 0u;
+        for (int k = 0; k < kFixGroups; ++k) {
+            eb[k] = ee[k] = 0;
 #pragma unroll
-        for (int t = 0; t < kFixBatch; ++t) {
-            const uint32_t col = en[t] >> 16;
-            if (e0 + t < ee && col < (uint32_t)cols) {
-                const float v = __uint_as_float(en[t] << 16);
+            for (int t = 0; t < kMH; ++t) pv[t][k] = 0.f;
+            if (g0 + k < kg) {
+                const int64_t b = ((int64_t)b16 * kg + g0 + k) * 16 + ri;
+                eb[k] = __ldg(res_ptr + b) + half;
+                ee[k] = min(__ldg(res_ptr + b + 1), n_res);
 #pragma unroll
-                for (int n = 0; n < M; ++n)
-                    acc[n] = fmaf(v, bf16_to_f32(kStaged ? x[n * cols + col] : __ldg(x + (int64_t)n * cols + col)),
-                                  acc[n]);
+                for (int t = 0; t < kMH; ++t) {
+                    const int n = 2 * t + half;
+                    if (n < M && live) pv[t][k] = __ldcg(partial + ((int64_t)n * kg + g0 + k) * rpad + row);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kFixGroups; ++k)
+#pragma unroll
+            for (int t = 0; t < kMH; ++t) psum[t] += pv[t][k];  // group order
+#pragma unroll
+        for (int k = 0; k < kFixGroups; ++k) {
+            if (g0 + k >= kg) break;
+            constexpr int kBatch = M <= 2 ? 12 : 4;  // entries of this half in flight at once
+            for (uint32_t e0 = eb[k]; e0 < ee[k]; e0 += 2 * kBatch) {
+                uint32_t en[kBatch];
+#pragma unroll
+                for (int t = 0; t < kBatch; ++t) en[t] = e0 + 2 * t < ee[k] ? __ldg(res_ent + e0 + 2 * t) : 0u;
+                float xv[kBatch][M];
+#pragma unroll
+                for (int t = 0; t < kBatch; ++t) {
+                    const uint32_t col = en[t] >> 16;
+                    const bool ok = e0 + 2 * t < ee[k] && col < (uint32_t)cols;
+#pragma unroll
+                    for (int n = 0; n < M; ++n)
+                        xv[t][n] = ok ? bf16_to_f32(__ldg(x + (int64_t)n * cols + col)) : 0.f;
+                }
+#pragma unroll
+                for (int t = 0; t < kBatch; ++t) {
+                    const float v = __uint_as_float(en[t] << 16);
+                    if (e0 + 2 * t < ee[k] && (en[t] >> 16) < (uint32_t)cols) {
+#pragma unroll
+                        for (int n = 0; n < M; ++n) acc[n] = fmaf(v, xv[t][n], acc[n]);
+                    }
+                }
             }
         }
     }
 #pragma unroll
-    for (int n = 0; n < M; ++n) red[threadIdx.x][n] = val[n] + acc[n];
-    __syncthreads();
-    if (!live || grp != 0) return;
+    for (int n = 0; n < M; ++n) acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
+    if (!live) return;
 #pragma unroll
-    for (int n = 0; n < M; ++n) {
-        float s = 0.f;
-        for (int g2 = 0; g2 < kg; ++g2) s += red[threadIdx.x + g2][n];
-        store_out(J, n, row, s);
+    for (int t = 0; t < kMH; ++t) {
+        const int n = 2 * t + half;
+        if (n < M) store_out(J, n, row, psum[t] + acc[n]);
     }
 }
 
@@ -630,25 +638,10 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     kern<<<grid, kThreads, kSmemBytes, stream>>>(b);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    // the fix-up grid: each job's rows in blocks of kFixThreads / kg rows, jobs back to back
-    GemvBatch<MAXJ> fb = b;
-    int blocks = 0, max_cols = 32;
-    for (int j = 0; j < fb.n; ++j) {
-        const int rpb = kFixThreads / fb.jobs[j].kg;
-        fb.jobs[j].rb_begin = blocks;
-        blocks += (fb.jobs[j].rows + rpb - 1) / rpb;
-        max_cols = std::max(max_cols, fb.jobs[j].cols);
-    }
-    const unsigned fix_grid = (unsigned)std::max(blocks, 1);
-    const uint32_t xbytes = (uint32_t)M * (uint32_t)max_cols * 2u;
-    if (xbytes <= kFixStageMax) {
-        auto fk = fixup_kernel<M, MAXJ, true>;
-        e = cudaFuncSetAttribute(fk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFixStageMax);
-        if (e != cudaSuccess) return e;
-        fk<<<fix_grid, kFixThreads, xbytes, stream>>>(fb);
-    } else {
-        fixup_kernel<M, MAXJ, false><<<fix_grid, kFixThreads, 0, stream>>>(fb);
-    }
+    int max_r16 = 1;
+    for (int j = 0; j < b.n; ++j) max_r16 = std::max(max_r16, b.jobs[j].r16);
+    const dim3 fix_grid((unsigned)((max_r16 + kFixThreads / 32 - 1) / (kFixThreads / 32)), (unsigned)b.n);
+    fixup_kernel<M, MAXJ><<<fix_grid, kFixThreads, 0, stream>>>(b);
     return cudaGetLastError();
 }
 
