@@ -357,14 +357,16 @@ def run_ours(args) -> None:
     ok = torch.equal(ys_host.to(dev)[: tasks[0].y.numel()], tasks[0].y.view(-1))
 
     peak, peak_kind = measured_peak()
+    # DRAM bytes per step from the committed ncu summary of this workload (both passes)
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemv_qwen05_traffic.json")
-    if os.path.exists(tp):
-        try:
-            with open(tp) as f:
-                traffic = json.load(f).get("dram_bytes_per_launch")
-        except Exception:
-            traffic = None
+    tp = os.path.join(ROOT, "profiles", "gemv_streaming_and_fixup_qwen05_168proj.md")
+    try:
+        with open(tp) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_step:"):
+                    traffic = int(line.split(":", 1)[1])
+    except OSError:
+        traffic = None
 
     cpu = None
     if rank == 0 and ws_ == 1 and not args.no_cpu_baseline:
