@@ -1,0 +1,197 @@
+"""Batch-1 greedy decode of a Qwen2.5-0.5B-architecture model whose 168
+projections run through the fused CDQ-LRR dequant-GEMV.
+
+Mirrors the reference's model path: the reference quantizes every q/k/v/o/
+gate/up/down projection of a Qwen2 model and patches a CDQLinear into its
+place (code/cdq_lrr_qwen05.py:276-297), then runs the HF model unchanged
+(code/cdq_lrr_qwen05.py:300-330). Weights here are random-init of that
+architecture (no checkpoint is available): N(0, 0.02^2) with 1.5% of the
+projection entries scaled by U(8, 20), seeded.
+
+Decode runs with a static KV cache; the one-token step is captured in a CUDA
+graph when HF's forward allows it (no host synchronisation in the step), and
+replayed per token.
+"""
+from __future__ import annotations
+
+import time
+
+import torch
+import torch.nn as nn
+
+from .quant import CDQLinear
+from .synth import PROJ_NAMES, QWEN05, synth_weight
+
+
+def qwen05_config():
+    from transformers import Qwen2Config
+    c = QWEN05
+    return Qwen2Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                       num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                       num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"],
+                       tie_word_embeddings=True, max_position_embeddings=4096,
+                       torch_dtype=torch.bfloat16)
+
+
+def build_model(seed: int = 0, device="cuda", layers: int | None = None):
+    """Random-init Qwen2.5-0.5B-architecture model in bf16 with outlier-bearing projections."""
+    from transformers import Qwen2ForCausalLM
+    cfg = qwen05_config()
+    if layers is not None:
+        cfg.num_hidden_layers = layers
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen2ForCausalLM(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        for i, layer in enumerate(model.model.layers):
+            for j, name in enumerate(PROJ_NAMES):
+                mod = _proj(layer, name)
+                rows, cols = mod.weight.shape
+                mod.weight.copy_(synth_weight(rows, cols, std=0.02, seed=1000 + 7 * i + j,
+                                              device=mod.weight.device))
+    model.eval()
+    return model
+
+
+def _proj(layer, name: str) -> nn.Module:
+    return getattr(layer.self_attn if name.endswith(("q_proj", "k_proj", "v_proj", "o_proj"))
+                   else layer.mlp, name)
+
+
+def _set_proj(layer, name: str, mod: nn.Module) -> None:
+    parent = layer.self_attn if name in ("q_proj", "k_proj", "v_proj", "o_proj") else layer.mlp
+    setattr(parent, name, mod)
+
+
+def patch_cdq(model, lattice=None) -> dict:
+    """Quantize every projection on the GPU and swap in the fused CDQLinear
+    (the reference's quantize_model loop, code/cdq_lrr_qwen05.py:276-297).
+    Returns {module name: reference-format pack}."""
+    packs = {}
+    for i, layer in enumerate(model.model.layers):
+        for name in PROJ_NAMES:
+            lin = _proj(layer, name)
+            cdq, pack = CDQLinear.from_linear(lin, lattice=lattice)
+            _set_proj(layer, name, cdq)
+            packs[f"model.layers.{i}.{name}"] = pack
+    return packs
+
+
+def materialize_reference(model) -> None:
+    """Replace every CDQLinear by an nn.Linear holding its w_hat (bit-exact),
+    i.e. the reference CDQLinear.forward = F.linear(x, w_hat, bias)
+    (code/cdq_lrr_qwen05.py:196-198) with torch's own GEMM."""
+    for layer in model.model.layers:
+        for name in PROJ_NAMES:
+            cdq = _proj(layer, name)
+            w = cdq.dequant_weight()
+            lin = nn.Linear(cdq.in_features, cdq.out_features, bias=cdq.bias is not None,
+                            device=w.device, dtype=torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(w)
+                if cdq.bias is not None:
+                    lin.bias.copy_(cdq.bias)
+            _set_proj(layer, name, lin)
+
+
+class GreedyDecoder:
+    """Static-cache greedy decoder for batch 1; the per-token step replays a
+    CUDA graph when capture succeeds (`self.graphed`), else runs eagerly."""
+
+    def __init__(self, model, max_len: int, use_graph: bool = True):
+        from transformers import StaticCache
+        self.model = model
+        self.dev = next(model.parameters()).device
+        self.cache = StaticCache(config=model.config, max_cache_len=max_len)
+        self.ids = torch.zeros(1, 1, dtype=torch.long, device=self.dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=self.dev)
+        # explicit additive mask over the static cache: 0 for written positions,
+        # -inf elsewhere (so the captured step carries no host-side mask logic)
+        self.mask = torch.full((1, 1, 1, max_len), float("-inf"), dtype=torch.bfloat16, device=self.dev)
+        self.next_tok = None
+        self.graph = None
+        self.use_graph = use_graph
+        self.graphed = False
+
+    def _step(self) -> torch.Tensor:
+        out = self.model(input_ids=self.ids, attention_mask=self.mask, past_key_values=self.cache,
+                         cache_position=self.pos, position_ids=self.pos[None], use_cache=True)
+        return out.logits[:, -1].argmax(-1, keepdim=True)
+
+    @torch.no_grad()
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        n = prompt.shape[1]
+        pos = torch.arange(n, device=self.dev)
+        out = self.model(input_ids=prompt, past_key_values=self.cache, cache_position=pos,
+                         position_ids=pos[None], use_cache=True, logits_to_keep=1)
+        self.mask[..., :n] = 0
+        return out.logits[:, -1].argmax(-1, keepdim=True)
+
+    @torch.no_grad()
+    def capture(self, at: int) -> None:
+        """Warm up and capture the one-token step; the warm-up steps write the
+        cache at positions at, at+1, which decoding overwrites later."""
+        if not self.use_graph:
+            return
+        self.pos.fill_(at)
+        self.mask[..., at] = 0  # the warm-up steps attend to position `at` like the first real step
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.next_tok = self._step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.next_tok = self._step()
+            self.graph = g
+            self.graphed = True
+        except Exception:  # HF forward not capturable in this version: eager steps
+            self.graph = None
+            self.graphed = False
+            torch.cuda.synchronize(self.dev)
+        self._rewind(at)
+
+    def _rewind(self, at: int) -> None:
+        """The static cache writes each step at its own on-device counter (it
+        does not read cache_position), which the warm-up steps advanced: set
+        it back to the next real position."""
+        for layer in getattr(self.cache, "layers", []):
+            n = getattr(layer, "cumulative_length", None)
+            if torch.is_tensor(n):
+                n.fill_(at)
+
+    @torch.no_grad()
+    def step(self, tok: torch.Tensor, position: int) -> torch.Tensor:
+        self.ids.copy_(tok)
+        self.pos.fill_(position)
+        self.mask[..., position] = 0
+        if self.graph is not None:
+            self.graph.replay()
+            return self.next_tok
+        return self._step()
+
+
+@torch.no_grad()
+def greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True) -> dict:
+    """Prefill `prompt` (1, P) and decode `new_tokens` greedy tokens.
+    Returns the tokens and the device-timed prefill and per-token times."""
+    P = prompt.shape[1]
+    dec = GreedyDecoder(model, P + new_tokens + 2, use_graph=use_graph)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    tok = dec.prefill(prompt)
+    e[1].record()
+    dec.capture(P)
+    toks = [tok]
+    e[2].record()
+    for t in range(new_tokens - 1):
+        tok = dec.step(tok, P + t).clone()
+        toks.append(tok)
+    e[3].record()
+    torch.cuda.synchronize()
+    steps = max(new_tokens - 1, 1)
+    return {"tokens": torch.cat(toks, dim=1), "prefill_ms": e[0].elapsed_time(e[1]),
+            "decode_ms_per_token": e[2].elapsed_time(e[3]) / steps,
+            "tokens_per_s": 1e3 * steps / max(e[2].elapsed_time(e[3]), 1e-9), "graphed": dec.graphed}
