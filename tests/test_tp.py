@@ -1,0 +1,103 @@
+"""Tensor-parallel sharding: shards cut from the reference-format pack are
+bit-identical parts of the unsharded weight; row-parallel partial products
+summed across ranks (gloo, world size 2, CPU) equal the unsharded product; on
+one GPU, ranks emulated in turn reproduce the unsharded fused linear."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import cdq_oracle as O
+
+
+def _pack(rows, cols, seed, ns=26):
+    from cdq_lrr_b200.synth import synth_weight
+    w = synth_weight(rows, cols, seed=seed).view(torch.int16).numpy().view(np.uint16)
+    return O.quantize(w, n_states=ns)
+
+
+@pytest.mark.parametrize("rows,cols", [(96, 256), (45, 1088), (128, 96)])
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("kind", ["col", "row"])
+def test_shards_are_exact_parts(rows, cols, world, kind):
+    from cdq_lrr_b200 import tp
+    p = _pack(rows, cols, seed=rows + cols)
+    full = O.dequantize(p).reshape(rows, cols)
+    covered = 0
+    for r in range(world):
+        s, rs, cs, off = tp.shard_reference(p, rows, cols, kind, world, r)
+        sp = {**p, **s, "orig_shape": (rs, cs), "numel": rs * cs, "n_tiles": rs * cs // 32}
+        part = O.dequantize(sp).reshape(rs, cs) if rs * cs else np.zeros((rs, cs), np.uint16)
+        if kind == "col":
+            assert np.array_equal(part, full[off:off + rs])
+            covered += rs
+        else:
+            assert cs % 32 == 0
+            assert np.array_equal(part, full[:, off:off + cs])
+            covered += cs
+    assert covered == (rows if kind == "col" else cols)
+
+
+def _row_parallel_rank(rank, world, port, rows, cols, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from cdq_lrr_b200 import tp
+        from cdq_lrr_b200.synth import synth_activation
+        p = _pack(rows, cols, seed=11)
+        x = O.bf16_bits_to_f32(synth_activation(3, cols, seed=4).view(torch.int16).numpy().view(np.uint16))
+        s, rs, cs, off = tp.shard_reference(p, rows, cols, "row", world, rank)
+        sp = {**p, **s, "orig_shape": (rs, cs), "numel": rs * cs, "n_tiles": rs * cs // 32}
+        w = O.bf16_bits_to_f32(O.dequantize(sp).reshape(rs, cs)).astype(np.float64)
+        part = torch.from_numpy(x[:, off:off + cs].astype(np.float64) @ w.T)
+        dist.all_reduce(part)
+        full = O.bf16_bits_to_f32(O.dequantize(p).reshape(rows, cols)).astype(np.float64)
+        ref = x.astype(np.float64) @ full.T
+        q.put((rank, float(np.abs(part.numpy() - ref).max()), float(np.abs(ref).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_allreduce_gloo():
+    rows, cols, world = 64, 2048, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_row_parallel_rank, args=(r, world, port, rows, cols, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+        assert pr.exitcode == 0
+    res = [q.get(timeout=10) for _ in range(world)]
+    for rank, err, scale in res:
+        assert err <= 1e-9 * max(scale, 1.0), (rank, err, scale)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_emulated_on_one_gpu(world):
+    from cdq_lrr_b200 import ops, tp
+    from cdq_lrr_b200.synth import synth_activation
+    for kind, rows, cols in (("col", 896, 896), ("row", 896, 4864)):
+        p = _pack(rows, cols, seed=rows * 3 + cols)
+        full = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                             p["residual_values"], rows, cols, 26, device="cuda")
+        bias = synth_activation(1, rows, seed=8)[0].cuda()
+        x = synth_activation(2, cols, seed=6).cuda()
+        y_full32 = ops.linear(full, x, bias, out_f32=True)
+        shards = [tp.TPLinear.from_reference(p, rows, cols, 26, kind, world, r, bias=bias) for r in range(world)]
+        if kind == "col":
+            y = torch.cat([s(x) for s in shards], dim=-1)
+            # a row's computation does not depend on how rows are split: bit-identical
+            assert torch.equal(y, ops.linear(full, x, bias))
+        else:
+            parts = [ops.linear(s.pack, x[..., s.offset:s.offset + s.pack.cols].contiguous(), None, out_f32=True)
+                     for s in shards]
+            y32 = torch.stack(parts).sum(0) + bias.float()
+            err = (y32 - y_full32).abs().max().item()
+            assert err <= 1e-3 * (y_full32.abs().max().item() + 1e-6), err
