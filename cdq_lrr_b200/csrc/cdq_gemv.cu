@@ -434,6 +434,7 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const int n_units = I.n_units, nq = (n_units + 3) >> 2;
         // a phantom second tile (odd tile count) sits in the row's last unit
         const int phantom_u = (J.kt & 1) && I.cp0 + n_units == J.kp ? n_units - 1 : -1;
+        const bool phantom_item = phantom_u >= 0;
         const uint16_t* xp = J.x + (int64_t)xrow * J.cols + 64 * I.cp0 + 16 * c;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         for (int q = 0; q < nq; ++q) {
@@ -443,71 +444,107 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             }
             const uint32_t slot = ring + c_slot * Sl::kSlot;
             const int uq = min(4, n_units - 4 * q);
-            // the quad's words into registers, then the slot goes back to the copy engine
-            uint4 A[4], X[4][2];
-            uint4 W;
-            uint2 S;
-            if (uq == 4) {
+            const uint16_t* xq = xp + 256 * q;
+            if (uq == 4 && !phantom_item) {
+                // a full quad without a phantom tile: no per-unit checks
+                uint4 A[4], X[4][2];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
-                S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
-            } else {  // the short last quad of a row block (1..3 units, compact)
-                uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
+                const uint4 W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                const uint2 S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+                uint32_t dep = W.x ^ S.x;
+                if constexpr (Sl::kX) {
+                    const uint32_t xa = slot + kQuad + 512 * xrow + 32 * c;
 #pragma unroll
-                for (int i = 0; i < 3; ++i) {
-                    A[i] = make_uint4(0u, 0u, 0u, 0u);
-                    if (i < uq) {
-                        A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                        if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
-                        h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
+                    for (int i = 0; i < 4; ++i) {
+                        X[i][0] = lds_slot4(xa + 128 * i);
+                        X[i][1] = lds_slot4(xa + 128 * i + 16);
+                        dep ^= X[i][0].x ^ X[i][1].x;
                     }
                 }
-                A[3] = make_uint4(0u, 0u, 0u, 0u);
-                W = make_uint4(w4[0], w4[1], w4[2], 0u);
-                S = make_uint2(h[0] | (h[1] << 16), h[2]);
-            }
-            uint32_t dep = W.x ^ W.y ^ W.z ^ W.w ^ S.x ^ S.y;
-            if constexpr (Sl::kX) {
+                // one register of every slot read: each read has landed before the slot is reused
+                dep ^= A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+                asm volatile("" ::"r"(dep));
+                __syncwarp();
+                produce();
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    X[i][0] = make_uint4(0u, 0u, 0u, 0u);
-                    X[i][1] = X[i][0];
-                    // the phantom tile's lanes (c >= 2) keep zeros: that part of the slot is stale
-                    if (i < uq && (4 * q + i != phantom_u || c < 2)) {
-                        const uint32_t xa = slot + kQuad + 512 * xrow + 128 * i + 32 * c;
-                        X[i][0] = lds_slot4(xa);
-                        X[i][1] = lds_slot4(xa + 16);
-                    }
-                    dep ^= X[i][0].x ^ X[i][1].w;
-                }
-            }
-            // every lane waits for its slot reads to land before lane 0 reuses the slot
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dep ^= A[i].x ^ A[i].y ^ A[i].z ^ A[i].w;
-            asm volatile("" ::"r"(dep));
-            __syncwarp();
-            produce();
-            c_slot ^= 1u;
-            c_phase ^= c_slot == 0 ? 1u : 0u;
-
-            const uint16_t* xq = xp + 256 * q;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (i < uq) {
                     uint4 xa, xb;
                     if constexpr (Sl::kX) {
                         xa = X[i][0];
                         xb = X[i][1];
                     } else {
-                        load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
+                        xa = ldg_x4(xq + 64 * i);
+                        xb = ldg_x4(xq + 64 * i + 8);
                     }
                     if (i == 0) unit_mma<NS, 0>(A[0], W.x, S.x, xa, xb, lane_base, sig_base, d);
                     if (i == 1) unit_mma<NS, 16>(A[1], W.y, S.x, xa, xb, lane_base, sig_base, d);
                     if (i == 2) unit_mma<NS, 0>(A[2], W.z, S.y, xa, xb, lane_base, sig_base, d);
                     if (i == 3) unit_mma<NS, 16>(A[3], W.w, S.y, xa, xb, lane_base, sig_base, d);
                 }
+            } else {
+                // a short last quad (1..3 units, compact) or the quad holding a phantom tile
+                uint4 A[4], X[4][2];
+                uint4 W;
+                uint2 S;
+                if (uq == 4) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                    W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                    S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+                } else {
+                    uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) {
+                        A[i] = make_uint4(0u, 0u, 0u, 0u);
+                        if (i < uq) {
+                            A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                            if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
+                            h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
+                        }
+                    }
+                    A[3] = make_uint4(0u, 0u, 0u, 0u);
+                    W = make_uint4(w4[0], w4[1], w4[2], 0u);
+                    S = make_uint2(h[0] | (h[1] << 16), h[2]);
+                }
+                uint32_t dep = W.x ^ W.y ^ W.z ^ S.x ^ S.y;
+                if constexpr (Sl::kX) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        X[i][0] = make_uint4(0u, 0u, 0u, 0u);
+                        X[i][1] = X[i][0];
+                        // the phantom tile's lanes (c >= 2) keep zeros: that part of the slot is stale
+                        if (i < uq && (4 * q + i != phantom_u || c < 2)) {
+                            const uint32_t xa = slot + kQuad + 512 * xrow + 128 * i + 32 * c;
+                            X[i][0] = lds_slot4(xa);
+                            X[i][1] = lds_slot4(xa + 16);
+                        }
+                        dep ^= X[i][0].x ^ X[i][1].x;
+                    }
+                }
+                dep ^= A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+                asm volatile("" ::"r"(dep));
+                __syncwarp();
+                produce();
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i < uq) {
+                        uint4 xa, xb;
+                        if constexpr (Sl::kX) {
+                            xa = X[i][0];
+                            xb = X[i][1];
+                        } else {
+                            load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
+                        }
+                        if (i == 0) unit_mma<NS, 0>(A[0], W.x, S.x, xa, xb, lane_base, sig_base, d);
+                        if (i == 1) unit_mma<NS, 16>(A[1], W.y, S.x, xa, xb, lane_base, sig_base, d);
+                        if (i == 2) unit_mma<NS, 0>(A[2], W.z, S.y, xa, xb, lane_base, sig_base, d);
+                        if (i == 3) unit_mma<NS, 16>(A[3], W.w, S.y, xa, xb, lane_base, sig_base, d);
+                    }
+                }
             }
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
         }
         if (failed) break;
         // this group's partial sums of rows g and g + 8 (batch columns 2c, 2c + 1)
