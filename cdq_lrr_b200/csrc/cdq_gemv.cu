@@ -579,10 +579,20 @@ constexpr int kFixThreads = 256;
 constexpr int kFixGroups = 4;  // residual groups whose bucket bounds are fetched together
 
 template <int M, int MAXJ>
-__global__ void __launch_bounds__(kFixThreads)
+__global__ void __launch_bounds__(kFixThreads, M == 1 ? 8 : 2)
 fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
-    const GemvJob& J = batch.jobs[blockIdx.y];  // one grid row per job
-    const int b16 = (int)(blockIdx.x * (kFixThreads / 32) + (threadIdx.x >> 5));
+    // block -> job: rb_begin holds each job's first block (uniform search of the launch record)
+    int j = 0;
+    if constexpr (MAXJ > 1) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (batch.jobs[mid].rb_begin <= (int)blockIdx.x) lo = mid; else hi = mid - 1;
+        }
+        j = lo;
+    }
+    const GemvJob& J = batch.jobs[j];
+    const int b16 = ((int)blockIdx.x - J.rb_begin) * (kFixThreads / 32) + (int)(threadIdx.x >> 5);
     if (b16 >= J.r16) return;
     const uint32_t* const res_ptr = J.res_ptr;
     const uint32_t* const res_ent = J.res_ent;
@@ -604,7 +614,32 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     float acc[M];
 #pragma unroll
     for (int n = 0; n < M; ++n) acc[n] = 0.f;
-    for (int g0 = 0; g0 < kg; g0 += kFixGroups) {
+    if (kg == 1) {  // one residual group (cols <= 1024): no group loop
+        const int64_t b = (int64_t)b16 * 16 + ri;
+        const uint32_t eb = __ldg(res_ptr + b) + half, ee = min(__ldg(res_ptr + b + 1), n_res);
+#pragma unroll
+        for (int t = 0; t < kMH; ++t) {
+            const int n = 2 * t + half;
+            if (n < M && live) psum[t] = __ldcg(partial + (int64_t)n * rpad + row);
+        }
+        constexpr int kBatch1 = M <= 2 ? 8 : 4;
+        for (uint32_t e0 = eb; e0 < ee; e0 += 2 * kBatch1) {
+            uint32_t en[kBatch1];
+#pragma unroll
+            for (int t = 0; t < kBatch1; ++t) en[t] = e0 + 2 * t < ee ? __ldg(res_ent + e0 + 2 * t) : 0u;
+#pragma unroll
+            for (int t = 0; t < kBatch1; ++t) {
+                const uint32_t col = en[t] >> 16;
+                if (e0 + 2 * t < ee && col < (uint32_t)cols) {
+                    const float v = __uint_as_float(en[t] << 16);
+#pragma unroll
+                    for (int n = 0; n < M; ++n)
+                        acc[n] = fmaf(v, bf16_to_f32(__ldg(x + (int64_t)n * cols + col)), acc[n]);
+                }
+            }
+        }
+    }
+    for (int g0 = 0; kg > 1 && g0 < kg; g0 += kFixGroups) {
         float pv[kMH][kFixGroups];
         uint32_t eb[kFixGroups], ee[kFixGroups];
 #pragma unroll
@@ -630,7 +665,7 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
 #pragma unroll
         for (int k = 0; k < kFixGroups; ++k) {
             if (g0 + k >= kg) break;
-            constexpr int kBatch = M <= 2 ? 12 : 4;  // entries of this half in flight at once
+            constexpr int kBatch = M <= 2 ? 8 : 4;  // entries of this half in flight at once
             for (uint32_t e0 = eb[k]; e0 < ee[k]; e0 += 2 * kBatch) {
                 uint32_t en[kBatch];
 #pragma unroll
@@ -677,8 +712,15 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     if (e != cudaSuccess) return e;
     int max_r16 = 1;
     for (int j = 0; j < b.n; ++j) max_r16 = std::max(max_r16, b.jobs[j].r16);
-    const dim3 fix_grid((unsigned)((max_r16 + kFixThreads / 32 - 1) / (kFixThreads / 32)), (unsigned)b.n);
-    fixup_kernel<M, MAXJ><<<fix_grid, kFixThreads, 0, stream>>>(b);
+    // each job's row blocks, kFixThreads / 32 per block, jobs back to back
+    GemvBatch<MAXJ> fb = b;
+    int blocks = 0;
+    for (int j = 0; j < fb.n; ++j) {
+        fb.jobs[j].rb_begin = blocks;
+        blocks += (fb.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
+    }
+    (void)max_r16;
+    fixup_kernel<M, MAXJ><<<std::max(blocks, 1), kFixThreads, 0, stream>>>(fb);
     return cudaGetLastError();
 }
 
