@@ -51,9 +51,12 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("qwen05", "tp7b"), default="qwen05",
+    ap.add_argument("--workload", choices=("qwen05", "tp7b", "tp70b", "msweep"), default="qwen05",
                     help="qwen05: the 168-projection batch-1 GEMV (default); tp7b: the 28-layer "
-                         "Qwen2.5-7B-shape projection stack, tensor-parallel over the ranks")
+                         "Qwen2.5-7B-shape projection stack, tensor-parallel over the ranks; tp70b: "
+                         "the Llama-70B MLP shapes [28672,8192] and [8192,28672], tensor-parallel; "
+                         "msweep: the qwen05 projections at batch 1, 4, 16 and 64")
+    ap.add_argument("--states", type=int, choices=(26, 16), default=26, help="tp70b: lattice size")
     ap.add_argument("--batch", type=int, default=1, help="tp7b: activation rows (1 or 8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
@@ -242,20 +245,20 @@ def cpu_baseline(seconds: float, use_product_quantizer_packs=None) -> dict:
 # ------------------------------------------------------------------- our arm
 
 
-def random_pack(rows: int, cols: int, seed: int, device, stc_frac: float = 0.0156):
-    """A valid 26-state pack with seeded random symbols, fp8 scales in
-    [2^-6, 2^-2) and round(stc_frac * numel) residuals at random positions,
-    laid out on the host (no kernel launches)."""
+def random_pack(rows: int, cols: int, seed: int, device, stc_frac: float = 0.0156, n_states: int = 26):
+    """A valid pack with seeded random symbols, fp8 scales in [2^-6, 2^-2)
+    and round(stc_frac * numel) residuals at random positions, laid out on the
+    host (no kernel launches)."""
     import numpy as np
     from cdq_lrr_b200 import ops
     rng = np.random.default_rng(seed)
     n = rows * cols
-    q = rng.integers(0, 26, (n // 32, 32), dtype=np.uint8)
+    q = rng.integers(0, n_states, (n // 32, 32), dtype=np.uint8)
     scales = rng.integers(0x08, 0x28, n // 32, dtype=np.uint8)
     k = int(round(n * stc_frac))
     ridx = np.sort(rng.choice(n, k, replace=False)).astype(np.int64)
     rval = rng.integers(0x3C00, 0x3F00, k, dtype=np.uint16)
-    return ops.DevicePack.from_reference(q, scales, ridx, rval, rows, cols, 26, device=device)
+    return ops.DevicePack.from_reference(q, scales, ridx, rval, rows, cols, n_states, device=device)
 
 
 def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
@@ -480,8 +483,87 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_msweep(args) -> None:
+    """Batch sweep (1, 4, 16, 64) over the 168 Qwen2.5-0.5B-shape projections:
+    seeded random valid packs, one grouped launch pair per batch chunk of at
+    most 8 rows (batches above 8 stream the weights once per 8-row chunk)."""
+    import torch
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    packs = [random_pack(rows, cols, seed=i, device=dev) for i, (_, rows, cols) in enumerate(layer_list())]
+    ref_bytes = sum(p.reference_bytes() for p in packs)
+    sweep = []
+    for M in (1, 4, 16, 64):
+        mc = min(M, 8)
+        tasks = []
+        io_bytes = 0
+        for i, p in enumerate(packs):
+            x = synth_activation(M, p.cols, seed=10000 + i, device=dev)
+            y = torch.empty(M, p.rows, dtype=torch.bfloat16, device=dev)
+            io_bytes += (x.numel() + y.numel()) * 2
+            for m0 in range(0, M, mc):
+                tasks.append(ops.GemvTask(p, x[m0:m0 + mc], y[m0:m0 + mc]))
+        g = ops.GroupedLinear(tasks, m=mc)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            g()
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+        stream.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        flops = 2.0 * M * sum(p.rows * p.cols for p in packs)
+        sweep.append({"batch": M, "ms_per_step": round(ms, 5),
+                      "gb_s": round((ref_bytes + io_bytes) / (ms * 1e-3) / 1e9, 2),
+                      "tflop_s": round(flops / (ms * 1e-3) / 1e12, 3),
+                      "weight_passes": -(-M // 8)})
+        del graph
+    first = sweep[0]
+    line = {"metric": METRIC, "value": first["gb_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": first["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random packs)",
+            "config": {"workload": "Qwen2.5-0.5B-shape CDQ-26 projections (168), batch sweep",
+                       "batches": [1, 4, 16, 64]},
+            "sweep": sweep}
+    print(json.dumps(line), flush=True)
+
+
 def run_tp7b(args) -> None:
-    """Tensor-parallel GEMV stack of a 28-layer Qwen2.5-7B-shape model: per
+    from cdq_lrr_b200.synth import QWEN7B, layer_shapes
+    kinds = {"q_proj": "col", "k_proj": "col", "v_proj": "col", "o_proj": "row",
+             "gate_proj": "col", "up_proj": "col", "down_proj": "row"}
+    shapes = [(n, r, c, kinds[n]) for n, r, c in layer_shapes(QWEN7B)]
+    run_tp(args, shapes, QWEN7B["layers"], 26,
+           "Qwen2.5-7B-shape projection stack (28 layers x 7)")
+
+
+def run_tp70b(args) -> None:
+    from cdq_lrr_b200.synth import LLAMA70B_SHAPES
+    (r1, c1), (r2, c2) = LLAMA70B_SHAPES
+    shapes = [("up_proj", r1, c1, "col"), ("down_proj", r2, c2, "row")]
+    run_tp(args, shapes, 4, args.states,
+           f"Llama-70B MLP shapes [{r1},{c1}] (rows split) and [{r2},{c2}] (K split), 4 copies, "
+           f"{args.states}-state")
+
+
+def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
+    """Tensor-parallel GEMV stack: per
     layer, q/k/v/gate/up split by output rows (no collective) and o/down split
     along K with a float32 all-reduce (NCCL) of their partial outputs. Each
     rank holds seeded random valid 26-state packs of its shards (the GEMV's
@@ -491,26 +573,27 @@ def run_tp7b(args) -> None:
     import torch
     import torch.distributed as dist
     from cdq_lrr_b200 import ops, tp
-    from cdq_lrr_b200.synth import QWEN7B, layer_shapes, synth_activation
+    from cdq_lrr_b200.synth import synth_activation
 
     ws_, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", torch.cuda.current_device())
     m = args.batch
-    kinds = {"q_proj": "col", "k_proj": "col", "v_proj": "col", "o_proj": "row",
-             "gate_proj": "col", "up_proj": "col", "down_proj": "row"}
+    kinds = {n: k for n, _, _, k in shapes}
     shard_host = {}
-    for i, (name, rows, cols) in enumerate(layer_shapes(QWEN7B)):
-        if kinds[name] == "col":
+    for i, (name, rows, cols, kind) in enumerate(shapes):
+        if kind == "col":
             r0, r1 = tp.row_bounds(rows, ws_, rank)
-            shard_host[name] = (random_pack(r1 - r0, cols, seed=100 * rank + i, device="cpu"), rows)
+            shard_host[name] = (random_pack(r1 - r0, cols, seed=100 * rank + i, device="cpu",
+                                            n_states=n_states), rows)
         else:
             c0, c1 = tp.k_bounds(cols, ws_, rank)
-            shard_host[name] = (random_pack(rows, c1 - c0, seed=100 * rank + i, device="cpu"), rows)
+            shard_host[name] = (random_pack(rows, c1 - c0, seed=100 * rank + i, device="cpu",
+                                            n_states=n_states), rows)
     layers = []
     alg_bytes = 0
-    for li in range(QWEN7B["layers"]):
+    for li in range(n_layers):
         tasks, reduce_ys = [], []
-        for name, rows, cols in layer_shapes(QWEN7B):
+        for name, rows, cols, kind in shapes:
             hp, full_rows = shard_host[name]
             pack = hp.to(dev)
             x = synth_activation(m, pack.cols, seed=li * 7 + len(tasks), device=dev)
@@ -572,9 +655,9 @@ def run_tp7b(args) -> None:
             "n_gpus": ws_, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random packs of the shard shapes)",
-            "config": {"workload": f"Qwen2.5-7B-shape projection stack (28 layers x 7), batch {m}, "
-                                   f"tensor-parallel x{ws_}: q/k/v/gate/up split by rows, o/down split "
-                                   "along K with a float32 NCCL all-reduce",
+            "config": {"workload": f"{label}, batch {m}, tensor-parallel x{ws_}: column-parallel "
+                                   "weights split by rows, row-parallel weights split along K with a "
+                                   "float32 NCCL all-reduce",
                        "batch": m, "algorithmic_gb_all_ranks": round(total / 1e9, 3),
                        "parallelism": f"tp{ws_}", "launch": "one CUDA graph per step (GEMVs + all-reduces)",
                        "l2": "packed working set far above the 126 MB L2"},
@@ -595,6 +678,10 @@ def main():
         run_reference(args)
     elif args.workload == "tp7b":
         run_tp7b(args)
+    elif args.workload == "tp70b":
+        run_tp70b(args)
+    elif args.workload == "msweep":
+        run_msweep(args)
     else:
         run_ours(args)
 
