@@ -485,8 +485,8 @@ def run_reference(args) -> None:
 
 def run_msweep(args) -> None:
     """Batch sweep (1, 4, 16, 64) over the 168 Qwen2.5-0.5B-shape projections:
-    seeded random valid packs, one grouped launch pair per batch chunk of at
-    most 8 rows (batches above 8 stream the weights once per 8-row chunk)."""
+    seeded random valid packs, one grouped launch pair per step (batches above
+    8 decode each unit once and multiply ceil(M/8) n-tiles of 8 rows)."""
     import torch
     from cdq_lrr_b200 import ops
     from cdq_lrr_b200.synth import synth_activation
@@ -496,16 +496,14 @@ def run_msweep(args) -> None:
     ref_bytes = sum(p.reference_bytes() for p in packs)
     sweep = []
     for M in (1, 4, 16, 64):
-        mc = min(M, 8)
         tasks = []
         io_bytes = 0
         for i, p in enumerate(packs):
             x = synth_activation(M, p.cols, seed=10000 + i, device=dev)
             y = torch.empty(M, p.rows, dtype=torch.bfloat16, device=dev)
             io_bytes += (x.numel() + y.numel()) * 2
-            for m0 in range(0, M, mc):
-                tasks.append(ops.GemvTask(p, x[m0:m0 + mc], y[m0:m0 + mc]))
-        g = ops.GroupedLinear(tasks, m=mc)
+            tasks.append(ops.GemvTask(p, x, y))
+        g = ops.GroupedLinear(tasks, m=M)
         stream = torch.cuda.Stream(device=dev)
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -531,7 +529,7 @@ def run_msweep(args) -> None:
         sweep.append({"batch": M, "ms_per_step": round(ms, 5),
                       "gb_s": round((ref_bytes + io_bytes) / (ms * 1e-3) / 1e9, 2),
                       "tflop_s": round(flops / (ms * 1e-3) / 1e12, 3),
-                      "weight_passes": -(-M // 8)})
+                      "weight_passes": 1})
         del graph
     first = sweep[0]
     line = {"metric": METRIC, "value": first["gb_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,

@@ -17,7 +17,7 @@ STATUS = {
     0: "CDQ_OK", 1: "CDQ_ERR_SHAPE", 2: "CDQ_ERR_STATES", 3: "CDQ_ERR_ARG", 4: "CDQ_ERR_CUDA",
     5: "CDQ_ERR_FORMAT", 6: "CDQ_ERR_CAPACITY", 7: "CDQ_ERR_WORKSPACE", 8: "CDQ_ERR_UNSUPPORTED",
 }
-MAX_BATCH = 8
+MAX_BATCH = 64
 MAX_COLS = 65536
 MAX_JOBS = 192  # jobs per grouped launch (the launch record fits the kernel-parameter space)
 

@@ -266,6 +266,46 @@ __device__ __forceinline__ void unit_mma(const uint4& a, uint32_t w4, uint32_t s
              what_pair<NS, 14>(w, lane_base, ss0), what_pair<NS, 15>(w, lane_base, ss1), xb.z, xb.w);
 }
 
+// One unit for batches above 8: the unit's 16 w_hat pair registers are built
+// once and multiply NT n-tiles of 8 batch rows each (activations from global
+// memory: row 8t + g of n-tile t, clamped to the last batch row; rows past it
+// only feed output columns that are never stored). zero_x: the phantom tile's
+// lanes take zero activations.
+template <int NS, int SH, int NT>
+__device__ __forceinline__ void unit_mma_wide(const uint4& a, uint32_t w4, uint32_t sw, const uint16_t* xu,
+                                              int64_t cols, int g, int m, bool zero_x, uint32_t lane_base,
+                                              uint32_t sig_base, float (&d)[NT][4]) {
+    const uint32_t w[5] = {a.x, a.y, a.z, a.w, w4};
+    const uint32_t lo = SH <= 2 ? (sw << (2 - SH)) : (sw >> (SH - 2));
+    const uint32_t hi = sw >> (SH + 6);
+    const uint32_t ss0 = lds((lo & 0x3FCu) | sig_base);
+    const uint32_t ss1 = lds((hi & 0x3FCu) | sig_base);
+    const uint32_t A[16] = {
+        what_pair<NS, 0>(w, lane_base, ss0),  what_pair<NS, 1>(w, lane_base, ss1),
+        what_pair<NS, 2>(w, lane_base, ss0),  what_pair<NS, 3>(w, lane_base, ss1),
+        what_pair<NS, 4>(w, lane_base, ss0),  what_pair<NS, 5>(w, lane_base, ss1),
+        what_pair<NS, 6>(w, lane_base, ss0),  what_pair<NS, 7>(w, lane_base, ss1),
+        what_pair<NS, 8>(w, lane_base, ss0),  what_pair<NS, 9>(w, lane_base, ss1),
+        what_pair<NS, 10>(w, lane_base, ss0), what_pair<NS, 11>(w, lane_base, ss1),
+        what_pair<NS, 12>(w, lane_base, ss0), what_pair<NS, 13>(w, lane_base, ss1),
+        what_pair<NS, 14>(w, lane_base, ss0), what_pair<NS, 15>(w, lane_base, ss1)};
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (8 * t < m) {
+            uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+            if (!zero_x) {
+                const uint16_t* xr = xu + (int64_t)min(8 * t + g, m - 1) * cols;
+                xa = ldg_x4(xr);
+                xb = ldg_x4(xr + 8);
+            }
+            mma16816(d[t], A[0], A[1], A[2], A[3], xa.x, xa.y);
+            mma16816(d[t], A[4], A[5], A[6], A[7], xa.z, xa.w);
+            mma16816(d[t], A[8], A[9], A[10], A[11], xb.x, xb.y);
+            mma16816(d[t], A[12], A[13], A[14], A[15], xb.z, xb.w);
+        }
+    }
+}
+
 __device__ __forceinline__ void store_out(const GemvJob& J, int n, int row, float v) {
     if (J.bias) v += bf16_to_f32(J.bias[row]);
     if (J.out_f32) {
@@ -375,6 +415,8 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     // lanes of batch columns >= M read row 0: their mma output columns are
     // never stored, so any finite or non-finite value there is harmless
     const int xrow = g < M ? g : 0;
+    constexpr int NT = (M + 7) / 8;             // n-tiles of 8 batch rows
+    const int m_rt = M <= 8 ? M : batch.m;      // batch rows of this launch
 
     // Producer cursor (lane 0 issues; every lane keeps the same values): the
     // next quad of this warp's stream of items.
@@ -436,7 +478,22 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const int phantom_u = (J.kt & 1) && I.cp0 + n_units == J.kp ? n_units - 1 : -1;
         const bool phantom_item = phantom_u >= 0;
         const uint16_t* xp = J.x + (int64_t)xrow * J.cols + 64 * I.cp0 + 16 * c;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint16_t* xw = J.x + 64 * I.cp0 + 16 * c;  // batch row 0 (wide batches)
+        float d[NT][4];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
+        // unit i of quad q: the narrow path (one n-tile) or the wide one
+        auto run_unit = [&](const uint4& A, uint32_t w4, uint32_t sw, bool hi_half, const uint4& xa,
+                            const uint4& xb, int unit) {
+            if constexpr (NT == 1) {
+                if (hi_half) unit_mma<NS, 16>(A, w4, sw, xa, xb, lane_base, sig_base, d[0]);
+                else unit_mma<NS, 0>(A, w4, sw, xa, xb, lane_base, sig_base, d[0]);
+            } else {
+                const bool zx = unit == phantom_u && c >= 2;
+                if (hi_half) unit_mma_wide<NS, 16, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
+                else unit_mma_wide<NS, 0, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
+            }
+        };
         for (int q = 0; q < nq; ++q) {
             if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
                 failed = true;
@@ -469,18 +526,16 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
                 produce();
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    uint4 xa, xb;
+                    uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
                     if constexpr (Sl::kX) {
                         xa = X[i][0];
                         xb = X[i][1];
-                    } else {
+                    } else if constexpr (NT == 1) {
                         xa = ldg_x4(xq + 64 * i);
                         xb = ldg_x4(xq + 64 * i + 8);
                     }
-                    if (i == 0) unit_mma<NS, 0>(A[0], W.x, S.x, xa, xb, lane_base, sig_base, d);
-                    if (i == 1) unit_mma<NS, 16>(A[1], W.y, S.x, xa, xb, lane_base, sig_base, d);
-                    if (i == 2) unit_mma<NS, 0>(A[2], W.z, S.y, xa, xb, lane_base, sig_base, d);
-                    if (i == 3) unit_mma<NS, 16>(A[3], W.w, S.y, xa, xb, lane_base, sig_base, d);
+                    const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
+                    run_unit(A[i], w4, i < 2 ? S.x : S.y, (i & 1) != 0, xa, xb, 4 * q + i);
                 }
             } else {
                 // a short last quad (1..3 units, compact) or the quad holding a phantom tile
@@ -529,17 +584,15 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     if (i < uq) {
-                        uint4 xa, xb;
+                        uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
                         if constexpr (Sl::kX) {
                             xa = X[i][0];
                             xb = X[i][1];
-                        } else {
+                        } else if constexpr (NT == 1) {
                             load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
                         }
-                        if (i == 0) unit_mma<NS, 0>(A[0], W.x, S.x, xa, xb, lane_base, sig_base, d);
-                        if (i == 1) unit_mma<NS, 16>(A[1], W.y, S.x, xa, xb, lane_base, sig_base, d);
-                        if (i == 2) unit_mma<NS, 0>(A[2], W.z, S.y, xa, xb, lane_base, sig_base, d);
-                        if (i == 3) unit_mma<NS, 16>(A[3], W.w, S.y, xa, xb, lane_base, sig_base, d);
+                        const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
+                        run_unit(A[i], w4, i < 2 ? S.x : S.y, (i & 1) != 0, xa, xb, 4 * q + i);
                     }
                 }
             }
@@ -547,14 +600,17 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             c_phase ^= c_slot == 0 ? 1u : 0u;
         }
         if (failed) break;
-        // this group's partial sums of rows g and g + 8 (batch columns 2c, 2c + 1)
+        // this group's partial sums of rows g and g + 8 (batch columns 8t + 2c, 8t + 2c + 1)
         const int64_t rpad = (int64_t)J.r16 * 16;
-        const int n0 = 2 * c;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int64_t row = I.b16 * 16 + g + 8 * h;
-            if (n0 < M) J.partial[((int64_t)n0 * J.kg + I.grp) * rpad + row] = d[2 * h];
-            if (n0 + 1 < M) J.partial[((int64_t)(n0 + 1) * J.kg + I.grp) * rpad + row] = d[2 * h + 1];
+        for (int t = 0; t < NT; ++t) {
+            const int n0 = 8 * t + 2 * c;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t row = I.b16 * 16 + g + 8 * h;
+                if (n0 < m_rt) J.partial[((int64_t)n0 * J.kg + I.grp) * rpad + row] = d[t][2 * h];
+                if (n0 + 1 < m_rt) J.partial[((int64_t)(n0 + 1) * J.kg + I.grp) * rpad + row] = d[t][2 * h + 1];
+            }
         }
     }
     if (failed) {
@@ -603,100 +659,78 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     const int64_t rpad = (int64_t)J.r16 * 16;
     const int lane = threadIdx.x & 31, ri = lane >> 1, half = lane & 1;
     const int row = b16 * 16 + ri;
-
-    // the group partial sums do not depend on the residuals: fetch them first
-    // (half 0 holds even batch columns, half 1 odd ones; kFixGroups groups at a time)
-    constexpr int kMH = (M + 1) / 2;
-    float psum[kMH];
-#pragma unroll
-    for (int k = 0; k < kMH; ++k) psum[k] = 0.f;
     const bool live = row < rows;
-    float acc[M];
+    // batch rows in chunks of M (one chunk unless the launch is wider than 8)
+    const int m_total = M < 8 ? M : batch.m;
+    constexpr int kMH = (M + 1) / 2;
+    for (int n0 = 0; n0 < m_total; n0 += M) {
+        const int mc = min(M, m_total - n0);  // rows of this chunk
+        const uint16_t* const xc = x + (int64_t)n0 * cols;
+        const float* const pc = partial + (int64_t)n0 * kg * rpad;
+        // the group partial sums do not depend on the residuals: fetch them first
+        // (half 0 holds even batch columns of the chunk, half 1 odd ones)
+        float psum[kMH];
 #pragma unroll
-    for (int n = 0; n < M; ++n) acc[n] = 0.f;
-    if (kg == 1) {  // one residual group (cols <= 1024): no group loop
-        const int64_t b = (int64_t)b16 * 16 + ri;
-        const uint32_t eb = __ldg(res_ptr + b) + half, ee = min(__ldg(res_ptr + b + 1), n_res);
+        for (int k = 0; k < kMH; ++k) psum[k] = 0.f;
+        float acc[M];
 #pragma unroll
-        for (int t = 0; t < kMH; ++t) {
-            const int n = 2 * t + half;
-            if (n < M && live) psum[t] = __ldcg(partial + (int64_t)n * rpad + row);
-        }
-        constexpr int kBatch1 = M <= 2 ? 8 : 4;
-        for (uint32_t e0 = eb; e0 < ee; e0 += 2 * kBatch1) {
-            uint32_t en[kBatch1];
-#pragma unroll
-            for (int t = 0; t < kBatch1; ++t) en[t] = e0 + 2 * t < ee ? __ldg(res_ent + e0 + 2 * t) : 0u;
-#pragma unroll
-            for (int t = 0; t < kBatch1; ++t) {
-                const uint32_t col = en[t] >> 16;
-                if (e0 + 2 * t < ee && col < (uint32_t)cols) {
-                    const float v = __uint_as_float(en[t] << 16);
-#pragma unroll
-                    for (int n = 0; n < M; ++n)
-                        acc[n] = fmaf(v, bf16_to_f32(__ldg(x + (int64_t)n * cols + col)), acc[n]);
-                }
-            }
-        }
-    }
-    for (int g0 = 0; kg > 1 && g0 < kg; g0 += kFixGroups) {
-        float pv[kMH][kFixGroups];
-        uint32_t eb[kFixGroups], ee[kFixGroups];
-#pragma unroll
-        for (int k = 0; k < kFixGroups; ++k) {
-            eb[k] = ee[k] = 0;
-#pragma unroll
-            for (int t = 0; t < kMH; ++t) pv[t][k] = 0.f;
-            if (g0 + k < kg) {
-                const int64_t b = ((int64_t)b16 * kg + g0 + k) * 16 + ri;
-                eb[k] = __ldg(res_ptr + b) + half;
-                ee[k] = min(__ldg(res_ptr + b + 1), n_res);
-#pragma unroll
-                for (int t = 0; t < kMH; ++t) {
-                    const int n = 2 * t + half;
-                    if (n < M && live) pv[t][k] = __ldcg(partial + ((int64_t)n * kg + g0 + k) * rpad + row);
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < kFixGroups; ++k)
-#pragma unroll
-            for (int t = 0; t < kMH; ++t) psum[t] += pv[t][k];  // group order
-#pragma unroll
-        for (int k = 0; k < kFixGroups; ++k) {
-            if (g0 + k >= kg) break;
+        for (int n = 0; n < M; ++n) acc[n] = 0.f;
+        auto add_entries = [&](uint32_t eb, uint32_t ee) {
             constexpr int kBatch = M <= 2 ? 8 : 4;  // entries of this half in flight at once
-            for (uint32_t e0 = eb[k]; e0 < ee[k]; e0 += 2 * kBatch) {
+            for (uint32_t e0 = eb; e0 < ee; e0 += 2 * kBatch) {
                 uint32_t en[kBatch];
 #pragma unroll
-                for (int t = 0; t < kBatch; ++t) en[t] = e0 + 2 * t < ee[k] ? __ldg(res_ent + e0 + 2 * t) : 0u;
-                float xv[kBatch][M];
+                for (int t = 0; t < kBatch; ++t) en[t] = e0 + 2 * t < ee ? __ldg(res_ent + e0 + 2 * t) : 0u;
 #pragma unroll
                 for (int t = 0; t < kBatch; ++t) {
                     const uint32_t col = en[t] >> 16;
-                    const bool ok = e0 + 2 * t < ee[k] && col < (uint32_t)cols;
+                    if (e0 + 2 * t < ee && col < (uint32_t)cols) {
+                        const float v = __uint_as_float(en[t] << 16);
 #pragma unroll
-                    for (int n = 0; n < M; ++n)
-                        xv[t][n] = ok ? bf16_to_f32(__ldg(x + (int64_t)n * cols + col)) : 0.f;
-                }
-#pragma unroll
-                for (int t = 0; t < kBatch; ++t) {
-                    const float v = __uint_as_float(en[t] << 16);
-                    if (e0 + 2 * t < ee[k] && (en[t] >> 16) < (uint32_t)cols) {
-#pragma unroll
-                        for (int n = 0; n < M; ++n) acc[n] = fmaf(v, xv[t][n], acc[n]);
+                        for (int n = 0; n < M; ++n)
+                            if (n < mc) acc[n] = fmaf(v, bf16_to_f32(__ldg(xc + (int64_t)n * cols + col)), acc[n]);
                     }
                 }
             }
+        };
+        for (int g0 = 0; g0 < kg; g0 += kFixGroups) {
+            float pv[kMH][kFixGroups];
+            uint32_t eb[kFixGroups], ee[kFixGroups];
+#pragma unroll
+            for (int k = 0; k < kFixGroups; ++k) {
+                eb[k] = ee[k] = 0;
+#pragma unroll
+                for (int t = 0; t < kMH; ++t) pv[t][k] = 0.f;
+                if (g0 + k < kg) {
+                    const int64_t bk = ((int64_t)b16 * kg + g0 + k) * 16 + ri;
+                    eb[k] = __ldg(res_ptr + bk) + half;
+                    ee[k] = min(__ldg(res_ptr + bk + 1), n_res);
+#pragma unroll
+                    for (int t = 0; t < kMH; ++t) {
+                        const int n = 2 * t + half;
+                        if (n < mc && live) pv[t][k] = __ldcg(pc + ((int64_t)n * kg + g0 + k) * rpad + row);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kFixGroups; ++k)
+#pragma unroll
+                for (int t = 0; t < kMH; ++t) psum[t] += pv[t][k];  // group order
+#pragma unroll
+            for (int k = 0; k < kFixGroups; ++k) {
+                if (g0 + k >= kg) break;
+                add_entries(eb[k], ee[k]);
+            }
         }
-    }
 #pragma unroll
-    for (int n = 0; n < M; ++n) acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
-    if (!live) return;
+        for (int n = 0; n < M; ++n) acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
+        if (live) {
 #pragma unroll
-    for (int t = 0; t < kMH; ++t) {
-        const int n = 2 * t + half;
-        if (n < M) store_out(J, n, row, psum[t] + acc[n]);
+            for (int t = 0; t < kMH; ++t) {
+                const int n = 2 * t + half;
+                if (n < mc) store_out(J, n0 + n, row, psum[t] + acc[n]);
+            }
+        }
     }
 }
 
@@ -720,7 +754,8 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
         blocks += (fb.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
     }
     (void)max_r16;
-    fixup_kernel<M, MAXJ><<<std::max(blocks, 1), kFixThreads, 0, stream>>>(fb);
+    // batches above 8 are fixed up in chunks of 8 batch rows
+    fixup_kernel<(M <= 8 ? M : 8), MAXJ><<<std::max(blocks, 1), kFixThreads, 0, stream>>>(fb);
     return cudaGetLastError();
 }
 
@@ -739,9 +774,14 @@ cudaError_t dispatch(const GemvBatch<MAXJ>& b, int ns, int m, cudaStream_t s, in
         CDQ_M_CASE(7)
         CDQ_M_CASE(8)
         default:
-            return cudaErrorInvalidValue;
+            break;
     }
 #undef CDQ_M_CASE
+    // wider batches: n-tiles of 8 rows, the batch size itself read from the launch record
+    if (m <= 16) return ns == 26 ? launch_one<26, 16, MAXJ>(b, s, sms) : launch_one<16, 16, MAXJ>(b, s, sms);
+    if (m <= 32) return ns == 26 ? launch_one<26, 32, MAXJ>(b, s, sms) : launch_one<16, 32, MAXJ>(b, s, sms);
+    if (m <= 64) return ns == 26 ? launch_one<26, 64, MAXJ>(b, s, sms) : launch_one<16, 64, MAXJ>(b, s, sms);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -865,6 +905,8 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     J.partial = static_cast<float*>(scratch);
     b.total_items = (int64_t)J.r16 * J.kg;
     b.total_row_blocks = J.r16;
+    b.m = (int32_t)m;
+    b.reserved0 = 0;
     return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms) == cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;

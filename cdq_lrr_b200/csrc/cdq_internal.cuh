@@ -35,6 +35,8 @@ struct GemvBatch {
     int64_t total_items;
     int32_t n;
     int32_t total_row_blocks;  // fix-up pass work
+    int32_t m;                 // batch rows of every job of the launch
+    int32_t reserved0;
     GemvJob jobs[MAXJ];
 };
 

@@ -194,10 +194,23 @@ def linear(pack: DevicePack, x: torch.Tensor, bias: torch.Tensor | None = None,
     stream = _stream(x.device)
     for m0 in range(0, m_total, L.MAX_BATCH):
         m = min(L.MAX_BATCH, m_total - m0)
-        ws = pack.linear_workspace(L.MAX_BATCH)
+        ws = pack.linear_workspace(m)
         L.check(fn(C.byref(st), _vp(x2[m0:m0 + m]), m, _vp(y[m0:m0 + m]), _vp(bias),
                    _vp(ws), ws.numel(), stream), "cdq_linear")
     return y.reshape(*lead, pack.rows)
+
+
+def _job_workspace(pack: DevicePack, m: int, seen: set, keep: list) -> torch.Tensor:
+    """The pack's own workspace for its first job of a launch; further jobs of
+    the same launch on the same pack get a workspace each (the jobs run
+    concurrently), held in `keep` by the caller for as long as it launches."""
+    if id(pack) not in seen:
+        seen.add(id(pack))
+        return pack.linear_workspace(m)
+    s = L.sizes(pack.rows, pack.cols, pack.n_states, max_batch=m)
+    ws = torch.empty(max(s.linear_workspace_bytes, 256), dtype=torch.uint8, device=pack.device)
+    keep.append(ws)
+    return ws
 
 
 @dataclass
@@ -213,9 +226,11 @@ def linear_grouped(tasks: list[GemvTask], m: int) -> None:
     if not tasks:
         return
     jobs = (L.cdq_gemv_job * len(tasks))()
+    seen: set[int] = set()
+    extra: list[torch.Tensor] = []  # freed after the launch: the allocator is stream-ordered
     for j, t in zip(jobs, tasks):
         _require_cuda(t.x, "cdq grouped linear")
-        ws = t.pack.linear_workspace(L.MAX_BATCH)
+        ws = _job_workspace(t.pack, m, seen, extra)
         j.w = t.pack.struct()
         j.x = t.x.data_ptr()
         j.y = t.y.data_ptr()
@@ -236,9 +251,11 @@ class GroupedLinear:
         self.tasks = list(tasks)
         self.m = m
         self.jobs = (L.cdq_gemv_job * len(self.tasks))()
+        seen: set[int] = set()
+        self._extra_ws: list[torch.Tensor] = []
         for j, t in zip(self.jobs, self.tasks):
             _require_cuda(t.x, "cdq grouped linear")
-            ws = t.pack.linear_workspace(L.MAX_BATCH)
+            ws = _job_workspace(t.pack, m, seen, self._extra_ws)
             j.w = t.pack.struct()
             j.x = t.x.data_ptr()
             j.y = t.y.data_ptr()

@@ -48,7 +48,7 @@ typedef enum cdq_status {
 /* Largest supported cols: residual entries store the column in 16 bits. */
 #define CDQ_MAX_COLS 65536
 #define CDQ_TILE 32
-#define CDQ_MAX_BATCH 8         /* cdq_linear serves M <= CDQ_MAX_BATCH      */
+#define CDQ_MAX_BATCH 64        /* cdq_linear serves M <= CDQ_MAX_BATCH      */
 
 /*
  * Device layout of one packed weight ("device pack"), built so that one

@@ -46,7 +46,7 @@ def test_sizes_and_errors(L):
     lib = L.lib()
     assert lib.cdq_get_sizes(4864, 900, 26, 0.0156, 1, C.byref(out)) == 1   # cols % 32
     assert lib.cdq_get_sizes(4864, 896, 25, 0.0156, 1, C.byref(out)) == 2   # states
-    assert lib.cdq_get_sizes(4864, 896, 26, 0.0156, 9, C.byref(out)) == 3   # batch
+    assert lib.cdq_get_sizes(4864, 896, 26, 0.0156, 65, C.byref(out)) == 3  # batch
     assert lib.cdq_get_sizes(16, 65568, 26, 0.0156, 1, C.byref(out)) == 1   # > 65536 cols
 
 

@@ -161,6 +161,45 @@ def test_linear_batch_above_8_splits():
     _check_gemv(y, O.linear_f64(O.dequantize(p), _bits(x)))
 
 
+@pytest.mark.parametrize("shape,ns", [((128, 512), 26), ((64, 2080), 26), ((45, 96), 16), ((896, 4864), 16)])
+@pytest.mark.parametrize("m", [9, 16, 33, 64])
+def test_linear_wide_batch(shape, ns, m):
+    """Batches 9..64: each unit is decoded once and multiplied against
+    ceil(m/8) n-tiles; every row must match the oracle and equal the same
+    row computed alone (a row's arithmetic does not depend on the batch)."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    rows, cols = shape
+    w = synth_weight(rows, cols, seed=rows + cols + m)
+    p = O.quantize(_bits(w), n_states=ns)
+    dp = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                       p["residual_values"], rows, cols, ns, device="cuda")
+    x = synth_activation(m, cols, seed=m).cuda()
+    bias = synth_activation(1, rows, seed=3)[0].cuda()
+    y = ops.linear(dp, x, bias, out_f32=True)
+    ref = O.linear_f64(O.dequantize(p), _bits(x)) + O.bf16_bits_to_f32(_bits(bias)).astype(np.float64)
+    _check_gemv(y, ref)
+    for i in (0, m // 2, m - 1):
+        assert torch.equal(y[i:i + 1], ops.linear(dp, x[i:i + 1], bias, out_f32=True))
+
+
+def test_grouped_wide_batch_shared_pack():
+    """One pack in several jobs of one wide-batch grouped launch: each job gets
+    its own group-sum workspace."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    pack, _ = ops.quantize(synth_weight(896, 896, seed=5).cuda(), n_states=26)
+    tasks, singles = [], []
+    for i in range(3):
+        x = synth_activation(24, 896, seed=300 + i).cuda()
+        tasks.append(ops.GemvTask(pack, x, torch.empty(24, 896, dtype=torch.float32, device="cuda")))
+        singles.append(ops.linear(pack, x, out_f32=True))
+    ops.linear_grouped(tasks, 24)
+    torch.cuda.synchronize()
+    for t, s in zip(tasks, singles):
+        assert torch.equal(t.y, s)
+
+
 def test_grouped_equals_single_launches():
     from cdq_lrr_b200 import ops
     from cdq_lrr_b200.synth import synth_activation, synth_weight
