@@ -58,6 +58,8 @@ def parse_args():
                          "msweep: the qwen05 projections at batch 1, 4, 16 and 64")
     ap.add_argument("--states", type=int, choices=(26, 16), default=26, help="tp70b: lattice size")
     ap.add_argument("--batch", type=int, default=1, help="tp7b: activation rows (1 or 8)")
+    ap.add_argument("--tile-min-batch", type=int, default=16,
+                    help="smallest batch that takes the tcgen05 tile path (the library default is 16)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -526,7 +528,8 @@ def run_msweep(args) -> None:
         stream.synchronize()
         ms = e0.elapsed_time(e1) / args.steps
         flops = 2.0 * M * sum(p.rows * p.cols for p in packs)
-        sweep.append({"batch": M, "ms_per_step": round(ms, 5),
+        sweep.append({"batch": M, "path": "tcgen05 tile" if M >= args.tile_min_batch else "mma.sync stream",
+                      "ms_per_step": round(ms, 5),
                       "gb_s": round((ref_bytes + io_bytes) / (ms * 1e-3) / 1e9, 2),
                       "tflop_s": round(flops / (ms * 1e-3) / 1e12, 3),
                       "weight_passes": 1})
@@ -674,7 +677,10 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "tp7b":
+        return
+    from cdq_lrr_b200 import _lib
+    _lib.set_tile_min_batch(args.tile_min_batch)
+    if args.workload == "tp7b":
         run_tp7b(args)
     elif args.workload == "tp70b":
         run_tp70b(args)

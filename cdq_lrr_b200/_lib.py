@@ -67,6 +67,8 @@ _SIGS = {
     "cdq_linear_f32": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P, C.c_size_t, _P]),
     "cdq_linear_noalloc": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P]),
     "cdq_linear_grouped": (C.c_int, [C.POINTER(cdq_gemv_job), C.c_int32, C.c_int64, _P]),
+    "cdq_set_tile_min_batch": (C.c_int, [C.c_int32]),
+    "cdq_kernel_error": (C.c_int, [C.POINTER(C.c_int32)]),
     "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                C.POINTER(cdq_packed), _P, _P, C.c_size_t, _P]),
@@ -108,6 +110,18 @@ def exported_symbols() -> list[str]:
 def check(status: int, what: str) -> None:
     if status != 0:
         raise CdqError(status, what)
+
+
+def set_tile_min_batch(m: int) -> None:
+    """Batches of at least m rows take the tcgen05 tile path (default 16)."""
+    check(lib().cdq_set_tile_min_batch(m), "cdq_set_tile_min_batch")
+
+
+def kernel_error() -> int:
+    """The sticky in-kernel error code of the fused linear (0: none)."""
+    v = C.c_int32(0)
+    check(lib().cdq_kernel_error(C.byref(v)), "cdq_kernel_error")
+    return v.value
 
 
 def sizes(rows: int, cols: int, n_states: int, stc_frac: float = 0.0156,

@@ -204,4 +204,18 @@ cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n
     return CDQ_OK;
 }
 
+cdq_status cdq_set_tile_min_batch(int32_t m) {
+    if (m < 1) return CDQ_ERR_ARG;
+    gemv_set_tile_min_batch(m);
+    return CDQ_OK;
+}
+
+cdq_status cdq_kernel_error(int32_t* code) {
+    if (!code) return CDQ_ERR_ARG;
+    int v = 0;
+    if (gemv_read_error(&v) != cudaSuccess) return CDQ_ERR_CUDA;
+    *code = v;
+    return CDQ_OK;
+}
+
 }  // extern "C"

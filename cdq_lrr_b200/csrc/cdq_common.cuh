@@ -144,6 +144,25 @@ CDQ_HD Geometry geometry(int64_t rows, int64_t cols, int n_states) {
     return g;
 }
 
+// Workspace of one fused-linear call with batch m (bytes). The streaming path
+// keeps float32 sums per (batch row, residual group, padded row); the tcgen05
+// tile path keeps the call's prepared activations: the B-operand stages of
+// every quad (batch padded to N = 16, 32 or 64, 512 bytes per batch row per
+// quad) and x^T (64 * kp columns x the batch padded to 8, bf16).
+CDQ_HD int64_t ws_align256(int64_t b) { return (b + 255) / 256 * 256; }
+CDQ_HD int tile_nb(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
+CDQ_HD int64_t tile_xperm_bytes(const Geometry& g, int64_t m) { return (g.kp + 3) / 4 * tile_nb(m) * 512; }
+CDQ_HD int64_t tile_prep_bytes(const Geometry& g, int64_t m) {
+    return ws_align256(tile_xperm_bytes(g, m)) + ws_align256(g.kp * 64 * ((m + 7) / 8 * 8) * 2);
+}
+CDQ_HD int64_t gemv_partial_bytes(const Geometry& g, int64_t m) {
+    return ws_align256(m * g.kg * g.r16 * 16 * 4);
+}
+CDQ_HD int64_t linear_workspace_need(const Geometry& g, int64_t m) {
+    const int64_t a = gemv_partial_bytes(g, m), b = tile_prep_bytes(g, m);
+    return a > b ? a : b;
+}
+
 // Quad holding unit (b16, cp): byte offset of the quad, its unit count u and
 // the unit's index i inside it.
 CDQ_HD int64_t quad_base(const Geometry& g, int64_t b16, int64_t cp, int* u, int* i) {
@@ -186,8 +205,11 @@ CDQ_HD int64_t scale_offset(const Geometry& g, int64_t b16, int64_t cp, int ri, 
     return base + g.sig_off * u + 2 * (u * k + i) + (ri >> 3);
 }
 
+// Residual CSR bucket of (16-row block, residual group, row in block): row
+// major, so the buckets of one row (all its groups, columns ascending) are
+// consecutive and [res_ptr[row * kg], res_ptr[(row + 1) * kg]) is the row.
 CDQ_HD int64_t bucket_index(const Geometry& g, int64_t r16, int64_t grp, int ri) {
-    return (r16 * g.kg + grp) * 16 + ri;
+    return (r16 * 16 + ri) * g.kg + grp;
 }
 
 }  // namespace cdq

@@ -63,7 +63,7 @@ __global__ void dequant_residuals(const uint32_t* __restrict__ res_ptr,
     const Geometry g = geometry(rows, cols, ns);
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= g.r16 * g.kg * 16) return;
-    const int64_t row = (b / (g.kg * 16)) * 16 + (b & 15);
+    const int64_t row = b / g.kg;  // buckets are (row, group), row major
     if (row >= rows) return;
     for (uint32_t e = res_ptr[b]; e < res_ptr[b + 1]; ++e) {
         const uint32_t ent = res_ent[e];

@@ -693,35 +693,27 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
                 }
             }
         };
+        // the row's residual bounds (its buckets are consecutive: one range)
+        const uint32_t reb = __ldg(res_ptr + (int64_t)row * kg) + half;
+        const uint32_t ree = min(__ldg(res_ptr + (int64_t)(row + 1) * kg), n_res);
         for (int g0 = 0; g0 < kg; g0 += kFixGroups) {
             float pv[kMH][kFixGroups];
-            uint32_t eb[kFixGroups], ee[kFixGroups];
 #pragma unroll
             for (int k = 0; k < kFixGroups; ++k) {
-                eb[k] = ee[k] = 0;
 #pragma unroll
-                for (int t = 0; t < kMH; ++t) pv[t][k] = 0.f;
-                if (g0 + k < kg) {
-                    const int64_t bk = ((int64_t)b16 * kg + g0 + k) * 16 + ri;
-                    eb[k] = __ldg(res_ptr + bk) + half;
-                    ee[k] = min(__ldg(res_ptr + bk + 1), n_res);
-#pragma unroll
-                    for (int t = 0; t < kMH; ++t) {
-                        const int n = 2 * t + half;
-                        if (n < mc && live) pv[t][k] = __ldcg(pc + ((int64_t)n * kg + g0 + k) * rpad + row);
-                    }
+                for (int t = 0; t < kMH; ++t) {
+                    const int n = 2 * t + half;
+                    pv[t][k] = n < mc && live && g0 + k < kg
+                                   ? __ldcg(pc + ((int64_t)n * kg + g0 + k) * rpad + row)
+                                   : 0.f;
                 }
             }
 #pragma unroll
             for (int k = 0; k < kFixGroups; ++k)
 #pragma unroll
                 for (int t = 0; t < kMH; ++t) psum[t] += pv[t][k];  // group order
-#pragma unroll
-            for (int k = 0; k < kFixGroups; ++k) {
-                if (g0 + k >= kg) break;
-                add_entries(eb[k], ee[k]);
-            }
         }
+        add_entries(reb, ree);
 #pragma unroll
         for (int n = 0; n < M; ++n) acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
         if (live) {
@@ -734,6 +726,32 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     }
 }
 
+#include "cdq_tile.cuh"
+
+// The fix-up pass over every job's row blocks (kFixThreads / 32 per block, jobs
+// back to back); batches above 8 are fixed up in chunks of 8 batch rows.
+template <int MAXJ>
+cudaError_t launch_fixup(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream) {
+    GemvBatch<MAXJ> fb = b;
+    int blocks = 0;
+    for (int j = 0; j < fb.n; ++j) {
+        fb.jobs[j].rb_begin = blocks;
+        blocks += (fb.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
+    }
+    const int grid = std::max(blocks, 1);
+    switch (m) {
+        case 1: fixup_kernel<1, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 2: fixup_kernel<2, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 3: fixup_kernel<3, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 4: fixup_kernel<4, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 5: fixup_kernel<5, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 6: fixup_kernel<6, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        case 7: fixup_kernel<7, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+        default: fixup_kernel<8, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
+    }
+    return cudaGetLastError();
+}
+
 template <int NS, int M, int MAXJ>
 cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
     auto kern = gemv_kernel<NS, M, MAXJ>;
@@ -744,23 +762,69 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     kern<<<grid, kThreads, kSmemBytes, stream>>>(b);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    int max_r16 = 1;
-    for (int j = 0; j < b.n; ++j) max_r16 = std::max(max_r16, b.jobs[j].r16);
-    // each job's row blocks, kFixThreads / 32 per block, jobs back to back
-    GemvBatch<MAXJ> fb = b;
-    int blocks = 0;
-    for (int j = 0; j < fb.n; ++j) {
-        fb.jobs[j].rb_begin = blocks;
-        blocks += (fb.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
+    return launch_fixup(b, b.m, stream);
+}
+
+// The tile path: a launch that lays out the activations (once per distinct x
+// of the call, in the workspace of the first job that reads it), then the
+// tile kernel, one persistent CTA per SM, jobs dealt heaviest (most units per
+// row) first.
+template <int NS, int NB, int MAXJ>
+cudaError_t launch_tile(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
+    GemvBatch<MAXJ> tb = b;
+    int order[MAXJ];
+    for (int j = 0; j < b.n; ++j) order[j] = j;
+    std::stable_sort(order, order + b.n, [&](int a, int c) { return b.jobs[a].kp > b.jobs[c].kp; });
+    for (int j = 0; j < b.n; ++j) tb.jobs[j] = b.jobs[order[j]];
+    int64_t items = 0;
+    int prep_blocks = 0;
+    for (int j = 0; j < tb.n; ++j) {
+        GemvJob& J = tb.jobs[j];
+        J.item_begin = items;
+        items += (J.r16 + 7) / 8;
+        // the activations are prepared once per (x, cols): later jobs reuse them
+        J.reserved0 = 1;
+        J.reserved_ptr = J.partial;
+        for (int i = 0; i < j; ++i) {
+            if (tb.jobs[i].x == J.x && tb.jobs[i].cols == J.cols && tb.jobs[i].reserved0) {
+                J.reserved0 = 0;
+                J.reserved_ptr = tb.jobs[i].reserved_ptr;
+                break;
+            }
+        }
+        J.rb_begin = prep_blocks;
+        if (J.reserved0) prep_blocks += (J.kp + 3) / 4;
     }
-    (void)max_r16;
-    // batches above 8 are fixed up in chunks of 8 batch rows
-    fixup_kernel<(M <= 8 ? M : 8), MAXJ><<<std::max(blocks, 1), kFixThreads, 0, stream>>>(fb);
+    if (items >= INT32_MAX) return cudaErrorInvalidValue;
+    tb.total_items = items;
+    tile::x_prep_kernel<NB, MAXJ><<<std::max(prep_blocks, 1), 256, 0, stream>>>(tb);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    auto kern = tile::tile_kernel<NS, NB, MAXJ>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms));
+    kern<<<grid, tile::kThreads, kSmemBytes, stream>>>(tb);
     return cudaGetLastError();
 }
 
+int g_tile_min_batch = 16;  // batches from this size on take the tcgen05 tile path
+
+// The tile path needs enough 128-row tiles to occupy most SMs.
 template <int MAXJ>
-cudaError_t dispatch(const GemvBatch<MAXJ>& b, int ns, int m, cudaStream_t s, int sms) {
+bool tile_fits(const GemvBatch<MAXJ>& b, int sms) {
+    int64_t tiles = 0;
+    for (int j = 0; j < b.n; ++j) tiles += (b.jobs[j].r16 + 7) / 8;
+    return 2 * tiles >= sms;
+}
+
+template <int MAXJ>
+cudaError_t dispatch(const GemvBatch<MAXJ>& b, int ns, int m, cudaStream_t s, int sms, bool allow_tile) {
+    if (allow_tile && m >= g_tile_min_batch && m <= 64 && tile_fits(b, sms)) {
+        if (m <= 16) return ns == 26 ? launch_tile<26, 16, MAXJ>(b, s, sms) : launch_tile<16, 16, MAXJ>(b, s, sms);
+        if (m <= 32) return ns == 26 ? launch_tile<26, 32, MAXJ>(b, s, sms) : launch_tile<16, 32, MAXJ>(b, s, sms);
+        return ns == 26 ? launch_tile<26, 64, MAXJ>(b, s, sms) : launch_tile<16, 64, MAXJ>(b, s, sms);
+    }
 #define CDQ_M_CASE(MM)                                                  \
     case MM:                                                            \
         return ns == 26 ? launch_one<26, MM, MAXJ>(b, s, sms) : launch_one<16, MM, MAXJ>(b, s, sms);
@@ -795,13 +859,16 @@ cudaError_t upload_lattices() {
     return cudaMemcpyToSymbol(c_lat16, kLattice16, sizeof kLattice16);
 }
 
-cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_t s, int sms) {
-    return dispatch<1>(b, ns, m, s, sms);
+cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_t s, int sms,
+                               bool allow_tile) {
+    return dispatch<1>(b, ns, m, s, sms, allow_tile);
 }
 cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cudaStream_t s,
                                 int sms) {
-    return dispatch<kMaxJobs>(b, ns, m, s, sms);
+    return dispatch<kMaxJobs>(b, ns, m, s, sms, true);
 }
+
+void gemv_set_tile_min_batch(int m) { g_tile_min_batch = m; }
 
 cudaError_t gemv_read_error(int* out) {
     int v = 0;
@@ -872,7 +939,7 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
         (uintptr_t)y % 2 || (bias && (uintptr_t)bias % 2))
         return CDQ_ERR_ARG;
     const Geometry g = geometry(w->rows, w->cols, w->n_states);
-    if (linear_workspace_need(g, m) > (int64_t)kNoAllocScratchBytes) return CDQ_ERR_WORKSPACE;
+    if (gemv_partial_bytes(g, m) > (int64_t)kNoAllocScratchBytes) return CDQ_ERR_WORKSPACE;
 
     void* scratch = nullptr;
     int sms = 0;
@@ -907,7 +974,8 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     b.total_row_blocks = J.r16;
     b.m = (int32_t)m;
     b.reserved0 = 0;
-    return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms) == cudaSuccess
+    // the streaming path only: its scratch is sized for the group sums
+    return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms, false) == cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;
 }

@@ -149,8 +149,8 @@ cdq_status cdq_get_sizes(int32_t rows, int32_t cols, int32_t n_states, double st
     out->units_bytes = g.r16 * g.kp * g.unit;
     out->res_ptr_count = g.r16 * g.kg * 16 + 1;
     out->max_res = residual_budget(numel, stc_frac);
-    // per-group partial sums [max_batch][kg][r16*16] f32 of the streaming pass
-    out->linear_workspace_bytes = align256((int64_t)max_batch * g.kg * g.r16 * 16 * 4);
+    // streaming-path group sums or tile-path prepared activations, whichever is larger
+    out->linear_workspace_bytes = linear_workspace_need(g, max_batch);
     // tile variance f32, tie counts u32 (n_tiles + 1), histograms, scalars
     out->quantize_workspace_bytes = align256(n_tiles * 4) + align256((n_tiles + 1) * 4) +
                                     align256(4 * 2048 * 4) + align256(1024);

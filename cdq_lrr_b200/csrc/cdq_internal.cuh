@@ -40,17 +40,15 @@ struct GemvBatch {
     GemvJob jobs[MAXJ];
 };
 
-// Workspace of one linear call: float32 partial sums per (batch column,
-// residual group, padded row), 256-byte aligned size.
-inline int64_t linear_workspace_need(const Geometry& g, int64_t m) {
-    return (m * g.kg * g.r16 * 16 * 4 + 255) / 256 * 256;
-}
-
 cudaError_t upload_lattices();
-cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_t s, int sms);
+// allow_tile: the launch may take the tcgen05 tile path (the jobs' workspaces
+// hold linear_workspace_need bytes); false keeps the streaming path.
+cudaError_t gemv_launch_single(const GemvBatch<1>& b, int ns, int m, cudaStream_t s, int sms,
+                               bool allow_tile = true);
 cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cudaStream_t s,
                                 int sms);
 cudaError_t gemv_read_error(int* out);
+void gemv_set_tile_min_batch(int m);
 
 cudaError_t dequant_setup();
 cudaError_t quantize_setup();

@@ -280,7 +280,7 @@ __device__ __forceinline__ uint32_t snap(float x, float sq) {
     return q;
 }
 
-// 3/4b. residual count of every bucket (16-row block, residual group, row)
+// 3/4b. residual count of every bucket (row, residual group), row major
 __global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t cols, int ns,
                         uint32_t* __restrict__ counts, WS ws, int fallback_pass) {
     const QState* st = ws.st;
@@ -291,8 +291,7 @@ __global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t co
     unsigned long long total = 0;
     for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
          b += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b16 = b / (g.kg * 16), grp = (b / 16) % g.kg;
-        const int64_t row = b16 * 16 + (b & 15);
+        const int64_t row = b / g.kg, grp = b % g.kg;
         uint32_t cnt = 0;
         if (row < rows) {
             const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
@@ -446,9 +445,7 @@ __global__ void k_pack_res(const uint16_t* __restrict__ w, int32_t rows, int32_t
     const Rule rule = make_rule(ws.st);
     for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb;
          b += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b16 = b / (g.kg * 16), grp = (b / 16) % g.kg;
-        const int ri = (int)(b & 15);
-        const int64_t row = b16 * 16 + ri;
+        const int64_t row = b / g.kg, grp = b % g.kg;
         if (row >= rows) continue;
         uint32_t pos = out.res_ptr[b];
         const int64_t c0 = grp * kGroupTiles, c1 = min(c0 + kGroupTiles, g.kt);
@@ -459,7 +456,7 @@ __global__ void k_pack_res(const uint16_t* __restrict__ w, int32_t rows, int32_t
             uint32_t m = tile_mask(x, ws.var[tl], rule, rule.fallback ? ws.tie[tl] : 0u);
             if (!m) continue;
             const float sq = bf16_to_f32(fp8_to_bf16(
-                out.units[scale_offset(g, b16, c / 2, ri, (int)(c % 2))]));
+                out.units[scale_offset(g, row / 16, c / 2, (int)(row % 16), (int)(c % 2))]));
             const uint16_t* wt = w + tl * 32;
             while (m) {
                 const int e = __ffs(m) - 1;

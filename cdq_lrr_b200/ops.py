@@ -134,7 +134,7 @@ class DevicePack:
         counts = (rp[1:] - rp[:-1])
         kg = (kt + 31) // 32
         b = torch.arange(counts.numel())
-        rows = (b // (kg * 16)) * 16 + (b % 16)
+        rows = b // kg  # buckets are (row, group), row major
         row_of = torch.repeat_interleave(rows, counts)
         col = (ent >> 16) & 0xFFFF
         tile = row_of * kt + col // TILE

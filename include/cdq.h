@@ -73,10 +73,12 @@ typedef enum cdq_status {
  *   (the lattice's exact zero).
  * Rows beyond `rows` and the missing tile of an odd KT hold zero codes and
  * scale 0.
- *   res_ptr : residual CSR offsets, R16*KG*16 + 1 entries (KG = ceil(KT/32));
- *             bucket (b16, g, r) lists row 16*b16 + r, tile columns
- *             [32g, 32g + 32).
- *   res_ent : n_res words (col << 16) | bf16 bits, sorted by bucket then col.
+ *   res_ptr : residual CSR offsets, R16*16*KG + 1 entries (KG = ceil(KT/32));
+ *             bucket row * KG + g lists row `row` (0 <= row < R16*16), tile
+ *             columns [32g, 32g + 32), so one row's entries are the range
+ *             [res_ptr[row*KG], res_ptr[(row+1)*KG]).
+ *   res_ent : n_res words (col << 16) | bf16 bits, sorted by bucket then col
+ *             (by row, then column).
  *   res_q   : n_res lattice indices the quantizer chose at the residual
  *             positions (read only by format conversion, never by cdq_linear).
  */
@@ -100,7 +102,7 @@ typedef struct cdq_sizes {
     int64_t units_bytes;
     int64_t res_ptr_count;     /* uint32 entries */
     int64_t max_res;           /* upper bound on n_res from cdq_quantize: 2k */
-    int64_t linear_workspace_bytes;    /* per call of cdq_linear (float32 group sums) */
+    int64_t linear_workspace_bytes;    /* per call of cdq_linear (group sums or prepared x) */
     int64_t quantize_workspace_bytes;
 } cdq_sizes;
 
@@ -117,11 +119,14 @@ CDQ_API const char* cdq_version(void);
  * streamed from HBM and dequantized in registers (bit-exact w_hat pairs fed
  * to the tensor cores), FP32 accumulation, result rounded once to bf16.
  * M <= CDQ_MAX_BATCH.
- * workspace: linear_workspace_bytes of device memory (float32 partial sums per
- * residual group; no zeroing needed, every call writes the slots it reads).
- * Two launches per call: the streaming pass, then a fix-up pass that adds the
- * groups, the residual entries and the bias. Calls that share one workspace
- * must not overlap on the GPU.
+ * workspace: linear_workspace_bytes of device memory; no zeroing needed, every
+ * call writes what it reads. Streaming path (M below the tile threshold, or a
+ * launch with too few 128-row tiles to fill the GPU): two launches, the
+ * streaming pass writes float32 sums per residual group to the workspace and
+ * a fix-up pass adds the groups, the residual entries and the bias. tcgen05
+ * tile path: two launches, a small one that lays out the activations in the
+ * workspace, then the tile kernel, whose epilogue adds the residual entries
+ * and the bias. Calls that share one workspace must not overlap on the GPU.
  * bias may be NULL. x, y, bias: bf16 bit patterns, row-major.
  * Replaces CDQLinear.forward, code/cdq_lrr_qwen05.py:196-198, and the
  * loader's CDQLinear.forward, code/cdq_loader.py:53-58.
@@ -172,6 +177,27 @@ typedef struct cdq_gemv_job {
  * runs one projection per F.linear call, code/cdq_lrr_qwen05.py:198).
  */
 CDQ_API cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, void* stream);
+
+/*
+ * Kernel selection for the fused linear (process-wide, all devices): batches
+ * of at least m rows take the tcgen05 tile path (the weight rows are the
+ * M = 128 side of a tensor-core mma with tensor-memory accumulators, the
+ * batch its N side, padded to 16, 32 or 64); smaller batches take the
+ * streaming mma.sync path. Default 16; a value above CDQ_MAX_BATCH turns the
+ * tile path off. Both paths write the same per-group sums and share the
+ * fix-up pass. Not thread-safe against concurrent calls of the linear entry
+ * points. No counterpart in the reference.
+ */
+CDQ_API cdq_status cdq_set_tile_min_batch(int32_t m);
+
+/*
+ * The sticky in-kernel error code of the fused linear on the current device
+ * (0: none; 1: shared-memory window misplaced; 2: a weight copy never landed
+ * within the wait limit; 3: a tile-path pipeline wait gave up). A kernel that
+ * records an error leaves its outputs incomplete but returns normally, so the
+ * context stays usable. Reads after a device synchronisation; does not reset.
+ */
+CDQ_API cdq_status cdq_kernel_error(int32_t* code);
 
 /*
  * Bit-exact w_hat [rows, cols] bf16 from a device pack.

@@ -183,6 +183,122 @@ def test_linear_wide_batch(shape, ns, m):
         assert torch.equal(y[i:i + 1], ops.linear(dp, x[i:i + 1], bias, out_f32=True))
 
 
+@pytest.fixture
+def tile_min_batch():
+    """Sets the smallest batch that takes the tcgen05 tile path; restores 16."""
+    from cdq_lrr_b200 import _lib as L
+    yield L.set_tile_min_batch
+    L.set_tile_min_batch(16)
+
+
+def _tile_copies(rows: int) -> int:
+    """Jobs of one projection that give a grouped launch enough 128-row tiles
+    (one per two SMs of a B200) to take the tile path."""
+    return -(-74 // -(-rows // 128))
+
+
+@pytest.mark.parametrize("shape,ns", [((128, 512), 26), ((200, 2080), 26), ((45, 96), 16), ((896, 4864), 16),
+                                      ((4864, 896), 26)])
+@pytest.mark.parametrize("m", [1, 5, 16, 40])
+def test_tile_path_against_oracle(tile_min_batch, shape, ns, m):
+    """The tcgen05 tile path (forced for every batch here) against the oracle:
+    one projection in enough jobs of a grouped launch to take the tile path,
+    half of them on one shared activation matrix (prepared once) and half on
+    their own; ragged row tiles (rows not a multiple of 128), odd tile counts
+    (a phantom tile) and several residual groups included."""
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    tile_min_batch(1)
+    rows, cols = shape
+    w = synth_weight(rows, cols, seed=rows * 7 + cols + m)
+    p = O.quantize(_bits(w), n_states=ns)
+    dp = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                       p["residual_values"], rows, cols, ns, device="cuda")
+    w_hat = O.dequantize(p)
+    bias = synth_activation(1, rows, seed=4)[0].cuda()
+    b64 = O.bf16_bits_to_f32(_bits(bias)).astype(np.float64)
+    shared = synth_activation(m, cols, seed=m + 1).cuda()
+    tasks = []
+    for k in range(_tile_copies(rows)):
+        x = shared if k % 2 == 0 else synth_activation(m, cols, seed=1000 + k).cuda()
+        tasks.append(ops.GemvTask(dp, x, torch.empty(m, rows, dtype=torch.float32, device="cuda"), bias))
+    ops.linear_grouped(tasks, m)
+    torch.cuda.synchronize()
+    assert L.kernel_error() == 0
+    for k, t in enumerate(tasks[:4]):
+        _check_gemv(t.y, O.linear_f64(w_hat, _bits(t.x)) + b64)
+
+
+def test_tile_path_grouped_matches_streaming(tile_min_batch):
+    """A grouped tile-path launch (jobs of both lattices and ragged shapes)
+    matches the streaming path on the same jobs (single launches, which are
+    too small for the tile path). The two add the same fp32 terms in a
+    different order: the bar is 1e-5 of the output scale, far below the 1e-3
+    oracle bar."""
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    tile_min_batch(1)
+    shapes = [(896, 896, 26), (128, 896, 26), (4864, 896, 26), (896, 4864, 26), (96, 320, 16), (40, 2080, 16)]
+    for m in (1, 24):
+        by_ns = {}
+        singles = []
+        for rep in range(3):
+            for i, (r, c, ns) in enumerate(shapes):
+                pack, _ = ops.quantize(synth_weight(r, c, seed=400 + i).cuda(), n_states=ns)
+                x = synth_activation(m, c, seed=500 + 10 * rep + i).cuda()
+                t = ops.GemvTask(pack, x, torch.empty(m, r, dtype=torch.float32, device="cuda"))
+                by_ns.setdefault(ns, []).append(t)
+                singles.append((t, ops.linear(pack, x, out_f32=True)))
+        for ts in by_ns.values():
+            ops.linear_grouped(ts, m)
+        torch.cuda.synchronize()
+        for t, s in singles:
+            tol = 1e-5 * (s.abs().max().item() + 1e-6)
+            assert (t.y - s).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("m", [1, 16, 64])
+def test_tile_full_mode_many_jobs(tile_min_batch, m):
+    """A grouped launch with many jobs on the tile path: the tile epilogue adds
+    the residual entries and the bias and writes the final output (bf16 and
+    float32 outputs, both lattices, rows not a multiple of 128, several
+    residual groups per row)."""
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    tile_min_batch(1)
+    shapes = [(896, 896, 26), (4864, 896, 26), (896, 4864, 26), (1000, 2080, 16), (4864, 896, 16),
+              (200, 96, 26)] * 4
+    refs, tasks = [], []
+    for i, (r, c, ns) in enumerate(shapes):
+        w = synth_weight(r, c, seed=600 + i)
+        p = O.quantize(_bits(w), n_states=ns)
+        dp = ops.DevicePack.from_reference(p["quant_indices"], p["scales_f8"], p["residual_indices"],
+                                           p["residual_values"], r, c, ns, device="cuda")
+        x = synth_activation(m, c, seed=700 + i).cuda()
+        bias = synth_activation(1, r, seed=800 + i)[0].cuda() if i % 2 == 0 else None
+        out_dtype = torch.float32 if i % 3 == 0 else torch.bfloat16
+        tasks.append(ops.GemvTask(dp, x, torch.empty(m, r, dtype=out_dtype, device="cuda"), bias))
+        ref = O.linear_f64(O.dequantize(p), _bits(x))
+        if bias is not None:
+            ref = ref + O.bf16_bits_to_f32(_bits(bias)).astype(np.float64)
+        refs.append(ref)
+    by_ns = {}
+    for t, (_, _, ns) in zip(tasks, shapes):
+        by_ns.setdefault(ns, []).append(t)
+    for ts in by_ns.values():
+        ops.linear_grouped(ts, m)
+    torch.cuda.synchronize()
+    assert L.kernel_error() == 0
+    for t, ref in zip(tasks, refs):
+        if t.y.dtype == torch.float32:
+            _check_gemv(t.y, ref)
+        else:
+            err = np.abs(t.y.float().cpu().numpy() - ref).max()
+            assert err <= 2 ** -7 * np.abs(ref).max() + 1e-3, err
+
+
 def test_grouped_wide_batch_shared_pack():
     """One pack in several jobs of one wide-batch grouped launch: each job gets
     its own group-sum workspace."""
@@ -239,7 +355,7 @@ def test_large_projection_properties():
     counts = rp[1:] - rp[:-1]
     kg = (cols // 32 + 31) // 32
     b = torch.arange(counts.numel(), device="cuda")
-    row_of = torch.repeat_interleave((b // (kg * 16)) * 16 + (b % 16), counts)
+    row_of = torch.repeat_interleave(b // kg, counts)  # buckets are (row, group), row major
     col = ent >> 16
     assert torch.equal(w_hat[row_of, col], w[row_of, col])
     # every non-residual weight is within half a lattice gap of sigma-scaled value
