@@ -51,13 +51,17 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("qwen05", "tp7b", "tp70b", "msweep"), default="qwen05",
+    ap.add_argument("--workload", choices=("qwen05", "tp7b", "tp70b", "msweep", "tpsweep"), default="qwen05",
                     help="qwen05: the 168-projection batch-1 GEMV (default); tp7b: the 28-layer "
                          "Qwen2.5-7B-shape projection stack, tensor-parallel over the ranks; tp70b: "
                          "the Llama-70B MLP shapes [28672,8192] and [8192,28672], tensor-parallel; "
-                         "msweep: the qwen05 projections at batch 1, 4, 16 and 64")
+                         "msweep: the qwen05 projections at batch 1, 4, 16 and 64; tpsweep: tp7b "
+                         "(batch 1 and 8) on 1, 2, 4 ... GPUs and tp70b in both tiers on all GPUs, "
+                         "one-shot and NCCL all-reduce, in one launch")
     ap.add_argument("--states", type=int, choices=(26, 16), default=26, help="tp70b: lattice size")
     ap.add_argument("--batch", type=int, default=1, help="tp7b: activation rows (1 or 8)")
+    ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",
+                    help="tp7b/tp70b: the row-parallel reduction")
     ap.add_argument("--tile-min-batch", type=int, default=16,
                     help="smallest batch that takes the tcgen05 tile path (the library default is 16)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -563,56 +567,70 @@ def run_tp70b(args) -> None:
            f"{args.states}-state")
 
 
-def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
-    """Tensor-parallel GEMV stack: per
+def tp_measure(args, shapes, n_layers: int, n_states: int, batch: int, allreduce: str, group,
+               world: int, rank: int, local: int) -> dict | None:
+    """Tensor-parallel GEMV stack on the ranks of `group` (world ranks): per
     layer, q/k/v/gate/up split by output rows (no collective) and o/down split
-    along K with a float32 all-reduce (NCCL) of their partial outputs. Each
-    rank holds seeded random valid 26-state packs of its shards (the GEMV's
-    speed does not depend on the code values; the sharding itself is tested
-    for exactness separately). A step = every layer's grouped shard GEMV plus
-    its two all-reduces, replayed from one CUDA graph."""
+    along K with a float32 all-reduce of their partial outputs, by the
+    one-shot peer-memory kernel (allreduce "oneshot") or NCCL ("nccl"). Each
+    rank holds seeded random valid packs of its shards (the GEMV's speed does
+    not depend on the code values; the sharding itself is tested for
+    exactness separately). A step = every layer's grouped shard GEMV plus its
+    two all-reduces, replayed from one CUDA graph. Returns the result on the
+    group's rank 0 (None elsewhere)."""
     import torch
     import torch.distributed as dist
     from cdq_lrr_b200 import ops, tp
     from cdq_lrr_b200.synth import synth_activation
 
-    ws_, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", torch.cuda.current_device())
-    m = args.batch
-    kinds = {n: k for n, _, _, k in shapes}
+    m = batch
     shard_host = {}
     for i, (name, rows, cols, kind) in enumerate(shapes):
         if kind == "col":
-            r0, r1 = tp.row_bounds(rows, ws_, rank)
-            shard_host[name] = (random_pack(r1 - r0, cols, seed=100 * rank + i, device="cpu",
-                                            n_states=n_states), rows)
+            r0, r1 = tp.row_bounds(rows, world, rank)
+            shard_host[name] = random_pack(r1 - r0, cols, seed=100 * rank + i, device="cpu", n_states=n_states)
         else:
-            c0, c1 = tp.k_bounds(cols, ws_, rank)
-            shard_host[name] = (random_pack(rows, c1 - c0, seed=100 * rank + i, device="cpu",
-                                            n_states=n_states), rows)
+            c0, c1 = tp.k_bounds(cols, world, rank)
+            shard_host[name] = random_pack(rows, c1 - c0, seed=100 * rank + i, device="cpu", n_states=n_states)
     layers = []
     alg_bytes = 0
+    max_red = 0
     for li in range(n_layers):
         tasks, reduce_ys = [], []
         for name, rows, cols, kind in shapes:
-            hp, full_rows = shard_host[name]
-            pack = hp.to(dev)
+            pack = shard_host[name].to(dev)
             x = synth_activation(m, pack.cols, seed=li * 7 + len(tasks), device=dev)
-            if kinds[name] == "col":
+            if kind == "col":
                 y = torch.empty(m, pack.rows, dtype=torch.bfloat16, device=dev)
             else:
                 y = torch.empty(m, pack.rows, dtype=torch.float32, device=dev)
                 reduce_ys.append(y)
+                max_red = max(max_red, y.numel())
             tasks.append(ops.GemvTask(pack, x, y))
             alg_bytes += pack.reference_bytes() + x.numel() * 2 + y.numel() * (2 if y.dtype == torch.bfloat16 else 4)
         layers.append((ops.GroupedLinear(tasks, m=m), reduce_ys))
+    oar = tp.OneShotAllReduce(max_red, group=group) if world > 1 and allreduce == "oneshot" else None
 
     def step():
         for g, ys in layers:
             g()
             for y in ys:
-                if ws_ > 1:
-                    dist.all_reduce(y)
+                if oar is not None:
+                    oar(y)
+                elif world > 1:
+                    dist.all_reduce(y, group=group)
+
+    def gbar():
+        if world > 1:
+            dist.barrier(group=group)
+
+    def gmax(v: float, op=None) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op or dist.ReduceOp.MAX, group=group)
+        return float(t.item())
 
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
@@ -620,7 +638,7 @@ def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
         for _ in range(3):
             step()
     stream.synchronize()
-    barrier(ws_)
+    gbar()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
@@ -630,7 +648,7 @@ def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
         for _ in range(args.warmup):
             graph.replay()
     stream.synchronize()
-    barrier(ws_)
+    gbar()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -642,34 +660,105 @@ def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
         e1.record(stream)
     stream.synchronize()
     t1 = time.perf_counter()
-    barrier(ws_)
+    gbar()
     torch.cuda.synchronize()
     sampler.stop()
     ms = e0.elapsed_time(e1) / args.steps
-    ms_max = max_over_ranks(ws_, ms)
-    total = sum_over_ranks(ws_, float(alg_bytes))
+    ms_max = gmax(ms)
+    total = gmax(float(alg_bytes), dist.ReduceOp.SUM if world > 1 else None)
     del graph  # holds NCCL work: released before the process group
+    from cdq_lrr_b200 import _lib as L
+    err = L.ar_error()
+    if oar is not None:
+        oar.close()
+    layers.clear()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
     peak, peak_kind = measured_peak()
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(total / (ms_max * 1e-3) / 1e9, 2), "unit": UNIT,
-            "n_gpus": ws_, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random packs of the shard shapes)",
-            "config": {"workload": f"{label}, batch {m}, tensor-parallel x{ws_}: column-parallel "
-                                   "weights split by rows, row-parallel weights split along K with a "
-                                   "float32 NCCL all-reduce",
-                       "batch": m, "algorithmic_gb_all_ranks": round(total / 1e9, 3),
-                       "parallelism": f"tp{ws_}", "launch": "one CUDA graph per step (GEMVs + all-reduces)",
+    per_gpu = total / world / (ms_max * 1e-3) / 1e9
+    return {"n_gpus": world, "batch": m, "allreduce": allreduce if world > 1 else "none",
+            "value": round(total / (ms_max * 1e-3) / 1e9, 2), "ms_per_step": round(ms_max, 5),
+            "algorithmic_gb_all_ranks": round(total / 1e9, 3),
+            "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(per_gpu / peak, 4), "peak_kind": f"of {peak_kind}"},
+            "allreduce_error": err, "clocks": sampler.summary(t0, t1)}
+
+
+def tp_line(label: str, r: dict, steps: int, warmup: int) -> dict:
+    ar = {"oneshot": "a one-shot peer-memory float32 all-reduce (own kernel)",
+          "nccl": "a float32 NCCL all-reduce", "none": "no collective (one GPU)"}[r["allreduce"]]
+    return {"metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": r["n_gpus"], "steps": steps,
+            "warmup": warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random packs of the shard shapes)",
+            "config": {"workload": f"{label}, batch {r['batch']}, tensor-parallel x{r['n_gpus']}: column-parallel "
+                                   f"weights split by rows, row-parallel weights split along K with {ar}",
+                       "batch": r["batch"], "algorithmic_gb_all_ranks": r["algorithmic_gb_all_ranks"],
+                       "parallelism": f"tp{r['n_gpus']}", "allreduce": r["allreduce"],
+                       "launch": "one CUDA graph per step (GEMVs + all-reduces)",
                        "l2": "packed working set far above the 126 MB L2"},
-            "roofline": {"bound": "hbm", "achieved_per_gpu": round(total / ws_ / (ms_max * 1e-3) / 1e9, 2),
-                         "peak": peak, "unit": "GB/s",
-                         "frac": round(total / ws_ / (ms_max * 1e-3) / 1e9 / peak, 4),
-                         "peak_kind": f"of {peak_kind}"},
-            "clocks": sampler.summary(t0, t1),
-        }
+            "roofline": r["roofline"], "clocks": r["clocks"]}
+
+
+def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
+    ws_, rank, local = dist_setup(args.gpus)
+    import torch.distributed as dist
+    group = dist.group.WORLD if ws_ > 1 else None
+    r = tp_measure(args, shapes, n_layers, n_states, args.batch, args.allreduce, group, ws_, rank, local)
+    if r is not None:
+        print(json.dumps(tp_line(label, r, args.steps, args.warmup)), flush=True)
+    if ws_ > 1:
+        dist.destroy_process_group()
+
+
+def run_tpsweep(args) -> None:
+    """Every tensor-parallel configuration in one launch: the 7B-shape stack at
+    batch 1 and 8 on 1, 2, 4 ... world GPUs (subgroups of the first ranks; the
+    others wait), each with the one-shot all-reduce and, at batch 1, with
+    NCCL; the 70B MLP shapes in both lattice tiers on all GPUs. One JSON line
+    (rank 0) with every result in "sweep"."""
+    import torch
+    import torch.distributed as dist
+    from cdq_lrr_b200.synth import LLAMA70B_SHAPES, QWEN7B, layer_shapes
+    ws_, rank, local = dist_setup(args.gpus)
+    kinds = {"q_proj": "col", "k_proj": "col", "v_proj": "col", "o_proj": "row",
+             "gate_proj": "col", "up_proj": "col", "down_proj": "row"}
+    s7 = [(n, r, c, kinds[n]) for n, r, c in layer_shapes(QWEN7B)]
+    (r1, c1), (r2, c2) = LLAMA70B_SHAPES
+    s70 = [("up_proj", r1, c1, "col"), ("down_proj", r2, c2, "row")]
+    worlds = [w for w in (1, 2, 4, 8) if w <= ws_]
+    runs = []
+    for w in worlds:
+        for b, ar in ((1, "oneshot"), (1, "nccl"), (8, "oneshot")):
+            if w == 1 and ar == "nccl":
+                continue
+            runs.append(("7b", s7, QWEN7B["layers"], 26, b, ar, w))
+    for ns in (26, 16):
+        runs.append(("70b", s70, 4, ns, 1, "oneshot", ws_))
+    runs.append(("70b", s70, 4, 26, 1, "nccl", ws_))
+    results = []
+    groups = {}
+    for w in worlds:  # every rank creates every subgroup, in the same order
+        groups[w] = dist.new_group(list(range(w))) if ws_ > 1 else None
+    for tag, shapes, nl, ns, b, ar, w in runs:
+        if rank < w:
+            g = groups[w] if w > 1 else None
+            r = tp_measure(args, shapes, nl, ns, b, ar, g, w, rank, local)
+            if r is not None:
+                r["workload"] = tag if tag == "7b" else f"70b-{ns}"
+                results.append(r)
+        if ws_ > 1:
+            dist.barrier()
+    if rank == 0:
+        head = next((r for r in results if r["n_gpus"] == ws_ and r["workload"] == "7b"), results[0])
+        line = tp_line("Qwen2.5-7B-shape projection stack (28 layers x 7)", head, args.steps, args.warmup)
+        line["config"]["workloads"] = {"7b": "Qwen2.5-7B-shape projection stack (28 layers x 7), 26-state",
+                                       "70b-26": f"Llama-70B MLP shapes [{r1},{c1}] and [{r2},{c2}], 4 copies, 26-state",
+                                       "70b-16": f"Llama-70B MLP shapes [{r1},{c1}] and [{r2},{c2}], 4 copies, 16-state"}
+        line["sweep"] = results
         print(json.dumps(line), flush=True)
     if ws_ > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -686,6 +775,8 @@ def main():
         run_tp70b(args)
     elif args.workload == "msweep":
         run_msweep(args)
+    elif args.workload == "tpsweep":
+        run_tpsweep(args)
     else:
         run_ours(args)
 

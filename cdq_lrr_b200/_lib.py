@@ -41,6 +41,13 @@ class cdq_sizes(C.Structure):
         "max_res", "linear_workspace_bytes", "quantize_workspace_bytes")]
 
 
+class cdq_ipc_handle(C.Structure):
+    _fields_ = [("bytes", C.c_uint8 * 64)]
+
+
+AR_MAX_RANKS = 8  # CDQ_AR_MAX_RANKS
+
+
 class cdq_gemv_job(C.Structure):
     _fields_ = [("w", cdq_packed), ("x", C.c_void_p), ("y", C.c_void_p), ("bias", C.c_void_p),
                 ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
@@ -68,6 +75,13 @@ _SIGS = {
     "cdq_linear_noalloc": (C.c_int, [C.POINTER(cdq_packed), _P, C.c_int64, _P, _P, _P]),
     "cdq_linear_grouped": (C.c_int, [C.POINTER(cdq_gemv_job), C.c_int32, C.c_int64, _P]),
     "cdq_set_tile_min_batch": (C.c_int, [C.c_int32]),
+    "cdq_ar_create": (C.c_int, [C.c_int64, C.POINTER(C.c_void_p), C.POINTER(cdq_ipc_handle)]),
+    "cdq_ar_open": (C.c_int, [C.POINTER(cdq_ipc_handle), C.POINTER(C.c_void_p)]),
+    "cdq_ar_close": (C.c_int, [C.c_void_p]),
+    "cdq_ar_destroy": (C.c_int, [C.c_void_p]),
+    "cdq_allreduce_f32": (C.c_int, [C.POINTER(C.c_void_p), C.c_int32, C.c_int32, C.c_int64, C.c_void_p,
+                                    C.c_int64, C.c_void_p]),
+    "cdq_ar_error": (C.c_int, [C.POINTER(C.c_int32)]),
     "cdq_kernel_error": (C.c_int, [C.POINTER(C.c_int32)]),
     "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,
@@ -115,6 +129,13 @@ def check(status: int, what: str) -> None:
 def set_tile_min_batch(m: int) -> None:
     """Batches of at least m rows take the tcgen05 tile path (default 16)."""
     check(lib().cdq_set_tile_min_batch(m), "cdq_set_tile_min_batch")
+
+
+def ar_error() -> int:
+    """The sticky error code of the one-shot all-reduce (0: none)."""
+    v = C.c_int32(0)
+    check(lib().cdq_ar_error(C.byref(v)), "cdq_ar_error")
+    return v.value
 
 
 def kernel_error() -> int:

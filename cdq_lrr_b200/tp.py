@@ -72,19 +72,87 @@ def shard_reference(ref: dict, rows: int, cols: int, kind: str, world: int, rank
     raise ValueError(f"unknown shard kind {kind!r}")
 
 
+class OneShotAllReduce:
+    """In-place float32 sum across the ranks of a process group by one kernel
+    over NVLink peer memory (cdq_allreduce_f32): every rank's region is
+    exported once with a CUDA IPC handle and mapped by every other rank, so a
+    call costs one launch, one flag exchange and W peer reads per element, and
+    every rank gets bit-identical sums (rank-order addition). Every rank must
+    make the same calls in the same order; capturable in a CUDA graph.
+    close() releases the mappings (after a barrier, so no peer still reads)."""
+
+    def __init__(self, cap: int, group=None, device=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _lib as L
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > L.AR_MAX_RANKS:
+            raise ValueError(f"one-shot all-reduce serves at most {L.AR_MAX_RANKS} ranks")
+        self.cap = int(cap)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            own = C.c_void_p()
+            h = L.cdq_ipc_handle()
+            L.check(L.lib().cdq_ar_create(self.cap, C.byref(own), C.byref(h)), "cdq_ar_create")
+            handles = [bytes(h.bytes)]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(h.bytes), group=group)
+            ptrs = []
+            for q in range(self.world):
+                if q == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                hq = L.cdq_ipc_handle()
+                C.memmove(hq.bytes, handles[q], 64)
+                p = C.c_void_p()
+                L.check(L.lib().cdq_ar_open(C.byref(hq), C.byref(p)), "cdq_ar_open")
+                ptrs.append(p.value)
+        self._own = own.value
+        self._regions = (C.c_void_p * L.AR_MAX_RANKS)(*ptrs)
+
+    def __call__(self, y: torch.Tensor) -> torch.Tensor:
+        from . import _lib as L
+        if y.dtype != torch.float32 or not y.is_cuda or not y.is_contiguous():
+            raise ValueError("one-shot all-reduce: contiguous float32 CUDA tensor expected")
+        L.check(L.lib().cdq_allreduce_f32(self._regions, self.world, self.rank, self.cap, y.data_ptr(),
+                                          y.numel(), torch.cuda.current_stream(y.device).cuda_stream),
+                "cdq_allreduce_f32")
+        return y
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        from . import _lib as L
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                if q != self.rank:
+                    L.lib().cdq_ar_close(self._regions[q])
+            L.lib().cdq_ar_destroy(self._own)
+        self._own = None
+
+
 class TPLinear:
     """One projection's shard on this rank.
 
     kind "col": y_local = x @ w_shard^T (+ bias slice), bf16 [M, rows_shard].
     kind "row": y = all_reduce_sum(x[:, K slice] @ w_shard^T) (+ bias), bf16
     [M, rows]; the partial sums are float32 and the reduction runs on the
-    current stream through torch.distributed (NCCL between GPUs)."""
+    current stream, through the given OneShotAllReduce or else
+    torch.distributed (NCCL between GPUs)."""
 
     def __init__(self, pack: ops.DevicePack, kind: str, offset: int, full_rows: int,
-                 bias: torch.Tensor | None = None, group=None):
+                 bias: torch.Tensor | None = None, group=None, allreduce: OneShotAllReduce | None = None):
         self.pack, self.kind, self.offset, self.full_rows = pack, kind, offset, full_rows
         self.bias = bias
         self.group = group
+        self.allreduce = allreduce
 
     @classmethod
     def from_reference(cls, ref: dict, rows: int, cols: int, n_states: int, kind: str, world: int,
@@ -104,7 +172,9 @@ class TPLinear:
             return ops.linear(self.pack, x, self.bias)
         xs = x[..., self.offset:self.offset + self.pack.cols].contiguous()
         y = ops.linear(self.pack, xs, None, out_f32=True)
-        if torch.distributed.is_available() and torch.distributed.is_initialized():
+        if self.allreduce is not None:
+            self.allreduce(y)
+        elif torch.distributed.is_available() and torch.distributed.is_initialized():
             torch.distributed.all_reduce(y, group=self.group)
         if self.bias is not None:
             y = y + self.bias.float()

@@ -200,6 +200,37 @@ CDQ_API cdq_status cdq_set_tile_min_batch(int32_t m);
 CDQ_API cdq_status cdq_kernel_error(int32_t* code);
 
 /*
+ * One-shot all-reduce of float32 vectors over NVLink peer memory (the
+ * row-parallel partial outputs of tensor parallelism). Each rank creates a
+ * region on its device (staging buffers of 2 x cap floats, a signal pad and
+ * epoch counters; allocated and zeroed by the library), exports its CUDA IPC
+ * handle, and maps every peer's region with cdq_ar_open. cdq_allreduce_f32
+ * then sums data[0, n) across the ranks in place: each rank publishes its
+ * vector in its own region, flags every peer (system-scope release), waits for
+ * every peer's flag (acquire; a bounded wait that records error code 1 of
+ * cdq_ar_error and leaves data unreduced), and adds the ranks' vectors in rank
+ * order, so every rank holds bit-identical sums. regions[q] is rank q's region
+ * as mapped on this rank (regions[rank] = own region). Every rank must make
+ * the same sequence of calls with the same n; calls on one rank must be
+ * stream-ordered. No multicast objects, no collective library.
+ * The reference has no multi-GPU path.
+ */
+#define CDQ_AR_MAX_RANKS 8
+#define CDQ_AR_BLOCKS 16
+typedef struct cdq_ipc_handle {
+    uint8_t bytes[64];
+} cdq_ipc_handle;
+CDQ_API cdq_status cdq_ar_create(int64_t cap, void** region, cdq_ipc_handle* handle);
+CDQ_API cdq_status cdq_ar_open(const cdq_ipc_handle* handle, void** peer_region);
+CDQ_API cdq_status cdq_ar_close(void* peer_region);
+CDQ_API cdq_status cdq_ar_destroy(void* region);
+CDQ_API cdq_status cdq_allreduce_f32(void* const* regions, int32_t world, int32_t rank, int64_t cap,
+                                     float* data, int64_t n, void* stream);
+/* Sticky error code of the all-reduce on the current device (0: none; 1: a
+ * peer's flag did not arrive within the wait limit). Does not reset. */
+CDQ_API cdq_status cdq_ar_error(int32_t* code);
+
+/*
  * Bit-exact w_hat [rows, cols] bf16 from a device pack.
  * Replaces dequantize, code/cdq_lrr_qwen05.py:141-152, and
  * CDQLinear.dequant_weight, code/cdq_lrr_qwen05.py:188-194.

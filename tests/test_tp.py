@@ -101,3 +101,117 @@ def test_tp_emulated_on_one_gpu(world):
             y32 = torch.stack(parts).sum(0) + bias.float()
             err = (y32 - y_full32).abs().max().item()
             assert err <= 1e-3 * (y_full32.abs().max().item() + 1e-6), err
+
+
+def test_allreduce_argument_checks():
+    """The one-shot all-reduce rejects bad arguments before any device work."""
+    import ctypes as C
+    from cdq_lrr_b200 import _lib as L
+    lib = L.lib()
+    regions = (C.c_void_p * 8)()
+    assert lib.cdq_allreduce_f32(None, 2, 0, 16, C.c_void_p(16), 8, None) == 3
+    assert lib.cdq_allreduce_f32(regions, 9, 0, 16, C.c_void_p(16), 8, None) == 3    # > 8 ranks
+    assert lib.cdq_allreduce_f32(regions, 2, 2, 16, C.c_void_p(16), 8, None) == 3    # rank >= world
+    assert lib.cdq_allreduce_f32(regions, 2, 0, 16, C.c_void_p(16), 17, None) == 3   # n > cap
+    assert lib.cdq_allreduce_f32(regions, 2, 0, 16, C.c_void_p(16), 8, None) == 3    # missing region
+    h = L.cdq_ipc_handle()
+    assert lib.cdq_ar_create(0, C.byref(C.c_void_p()), C.byref(h)) == 3
+    assert lib.cdq_ar_open(None, None) == 3
+
+
+@pytest.mark.gpu
+def test_oneshot_allreduce_single_rank_graph():
+    """One rank: the one-shot all-reduce is the identity, eagerly and replayed
+    from a CUDA graph (alternating staging buffers), with no error recorded."""
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200 import tp
+    ar = tp.OneShotAllReduce(5000)
+    y = torch.randn(3, 1111, device="cuda")
+    ref = y.clone()
+    ar(y)
+    assert torch.equal(y, ref)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ar(y)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            ar(y)
+        for _ in range(5):
+            g.replay()
+    s.synchronize()
+    assert torch.equal(y, ref)
+    assert L.ar_error() == 0
+    del g
+    ar.close()
+
+
+def _oneshot_rank(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from cdq_lrr_b200 import _lib as L
+        from cdq_lrr_b200 import tp
+        ar = tp.OneShotAllReduce(1 << 16)
+        outs = []
+        for it, n in enumerate((7, 3584, 65536, 3584, 1)):
+            g = torch.Generator().manual_seed(1000 * it + rank)
+            y = torch.randn(n, generator=g).cuda()
+            ar(y)
+            outs.append(y.cpu().numpy().copy())
+        s = torch.cuda.Stream()
+        y = torch.zeros(4096, device="cuda")
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                y.fill_(float(rank + 1))
+                ar(y)
+            for _ in range(4):
+                graph.replay()
+        s.synchronize()
+        outs.append(y.cpu().numpy().copy())
+        err = L.ar_error()
+        del graph
+        ar.close()
+        q.put((rank, outs, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_oneshot_allreduce_two_ranks():
+    """Two ranks on two GPUs: the sums equal the rank-order float32 sums bit for
+    bit on both ranks, over alternating staging buffers, changing lengths and
+    CUDA-graph replays. Skipped on a one-GPU machine."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 200
+    procs = [ctx.Process(target=_oneshot_rank, args=(r, world, port, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    res = {}
+    for _ in range(world):
+        rank, outs, err = q.get(timeout=240)
+        res[rank] = (outs, err)
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    for it, n in enumerate((7, 3584, 65536, 3584, 1)):
+        parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * it + r)).numpy() for r in range(world)]
+        ref = np.float32(0) + parts[0]
+        for p in parts[1:]:
+            ref = (ref + p).astype(np.float32)
+        for r in range(world):
+            assert np.array_equal(res[r][0][it], ref), (it, r)
+    for r in range(world):
+        assert np.all(res[r][0][-1] == sum(range(1, world + 1)))
+        assert res[r][1] == 0
