@@ -277,12 +277,19 @@ def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
     decode.patch_cdq(model)
     g = torch.Generator().manual_seed(7)
     ids = torch.randint(0, 151936, (1, prompt_len), generator=g).cuda()
-    decode.greedy_decode(model, ids, 8)  # warm-up (allocations, lattice set-up)
-    r = decode.greedy_decode(model, ids, new_tokens)
+    decode.fused_greedy_decode(model, ids, 8)  # warm-up (allocations, lattice set-up)
+    r = decode.fused_greedy_decode(model, ids, new_tokens)
+    decode.greedy_decode(model, ids, 8)
+    h = decode.greedy_decode(model, ids, new_tokens)
     out = {"tokens_per_s": round(r["tokens_per_s"], 2),
            "ms_per_token": round(r["decode_ms_per_token"], 4),
            "prefill_ms": round(r["prefill_ms"], 3), "prompt_tokens": prompt_len,
            "new_tokens": new_tokens, "cuda_graph": r["graphed"],
+           "step": "fused decode step (library RMSNorm, rotary + cache append + GQA attention, SiLU-mul "
+                   "kernels around grouped CDQ projections; torch embedding, lm_head GEMV, argmax), "
+                   "token and position advanced on the device, one CUDA graph per token",
+           "hf_step_tokens_per_s": round(h["tokens_per_s"], 2),
+           "hf_step": "the same model through HF's Qwen2 forward (CDQ projections patched in), CUDA graph",
            "model": "Qwen2.5-0.5B architecture, random init, 168 CDQ-26 projections, bf16 tied lm_head",
            "timing": "CUDA events around the decode loop (device time incl. host launch gaps)"}
     del model

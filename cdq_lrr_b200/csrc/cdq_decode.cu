@@ -1,0 +1,199 @@
+// Batch-1 decode-step kernels around the fused CDQ linear, for a Qwen2-style
+// decoder (the reference runs HF's Qwen2 layers around its CDQLinear:
+// code/cdq_lrr_qwen05.py:300-330). Each kernel reproduces the rounding steps
+// of the HF bf16 module it replaces:
+//   add_rmsnorm  h = bf16(h + delta) (the residual add), then
+//                out = bf16(w * bf16(h_f32 * rsqrt(mean(h_f32^2) + eps)))
+//                (Qwen2RMSNorm);
+//   attn_decode  rotary embedding of q and k at the step's position
+//                (bf16(bf16(x * cos) + bf16(rotate_half(x) * sin))), append of
+//                k and v to the static cache, and grouped-query attention over
+//                positions 0..pos (fp32 scores, softmax and weighted sum, one
+//                bf16 rounding of the output);
+//   silu_mul     out = bf16(bf16(silu(g)) * u) (Qwen2MLP's act_fn(gate) * up);
+//   advance      the step's greedy token becomes the next step's input, is
+//                recorded, and the position moves on, all on the device, so a
+//                CUDA graph of the whole step replays without the host.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "cdq.h"
+
+namespace {
+
+__device__ __forceinline__ float bf(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+__device__ __forceinline__ uint16_t tobf(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ float rbf(float v) { return bf(tobf(v)); }
+
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __restrict__ h,
+                                                                   const uint16_t* __restrict__ delta,
+                                                                   const uint16_t* __restrict__ w, float eps,
+                                                                   uint16_t* __restrict__ out, int n) {
+    __shared__ float red[kNormThreads / 32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        float v = bf(h[i]);
+        if (delta) {
+            v = rbf(v + bf(delta[i]));
+            h[i] = tobf(v);
+        }
+        ss = fmaf(v, v, ss);
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < kNormThreads / 32; ++k) tot += red[k];
+    const float r = rsqrtf(tot / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        out[i] = tobf(bf(w[i]) * rbf(bf(h[i]) * r));
+    }
+}
+
+constexpr int kHd = 64;           // head dimension
+constexpr int kAttnThreads = 128;
+
+// One block per query head. scores[] holds the head's scores (dynamic shared memory, cap floats).
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+    const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t, const int32_t* __restrict__ pos_p,
+    uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int max_len, int n_heads, int n_kv, float scale,
+    uint16_t* __restrict__ out, int cap) {
+    extern __shared__ float scores[];
+    __shared__ float qe[kHd], ke[kHd], ve[kHd], red[kAttnThreads / 32], part[kHd];
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int group = n_heads / n_kv, kvh = h / group;
+    const int P = *pos_p;
+    if (P < 0 || P >= max_len || P >= cap) return;  // the host sizes the cache; nothing to attend otherwise
+    const uint16_t* cs = cos_t + (int64_t)P * kHd;
+    const uint16_t* sn = sin_t + (int64_t)P * kHd;
+    if (tid < kHd) {
+        const int d = tid, o = d < kHd / 2 ? d + kHd / 2 : d - kHd / 2;
+        const float sgn = d < kHd / 2 ? -1.f : 1.f;
+        const float qd = bf(q[h * kHd + d]), qo = bf(q[h * kHd + o]);
+        qe[d] = rbf(rbf(qd * bf(cs[d])) + rbf(sgn * qo * bf(sn[d])));
+        const float kd = bf(k[kvh * kHd + d]), ko = bf(k[kvh * kHd + o]);
+        ke[d] = rbf(rbf(kd * bf(cs[d])) + rbf(sgn * ko * bf(sn[d])));
+        ve[d] = bf(v[kvh * kHd + d]);
+        if (h % group == 0) {  // one block per kv head appends the step's k and v
+            kc[((int64_t)kvh * max_len + P) * kHd + d] = tobf(ke[d]);
+            vc[((int64_t)kvh * max_len + P) * kHd + d] = v[kvh * kHd + d];
+        }
+    }
+    __syncthreads();
+    // scores over positions 0..P (position P from this block's own k)
+    const uint16_t* kb = kc + (int64_t)kvh * max_len * kHd;
+    float mx = -INFINITY;
+    for (int j = tid; j <= P; j += kAttnThreads) {
+        float s = 0.f;
+        if (j < P) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + (int64_t)j * kHd);
+#pragma unroll
+            for (int c = 0; c < kHd / 8; ++c) {
+                const uint4 u = kr[c];
+                const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    s = fmaf(qe[8 * c + 2 * t], __uint_as_float(wv[t] << 16), s);
+                    s = fmaf(qe[8 * c + 2 * t + 1], __uint_as_float(wv[t] & 0xFFFF0000u), s);
+                }
+            }
+        } else {
+#pragma unroll 8
+            for (int d = 0; d < kHd; ++d) s = fmaf(qe[d], ke[d], s);
+        }
+        s *= scale;
+        scores[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k2 = 1; k2 < kAttnThreads / 32; ++k2) mx = fmaxf(mx, red[k2]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int j = tid; j <= P; j += kAttnThreads) {
+        const float e = expf(scores[j] - mx);
+        scores[j] = e;
+        sum += e;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int k2 = 0; k2 < kAttnThreads / 32; ++k2) sum += red[k2];
+    // weighted values: thread (half, d) takes positions of one parity
+    const int d = tid & (kHd - 1), half = tid / kHd;
+    const uint16_t* vb = vc + (int64_t)kvh * max_len * kHd;
+    float acc = 0.f;
+    for (int j = half; j <= P; j += 2) acc = fmaf(scores[j], j < P ? bf(vb[(int64_t)j * kHd + d]) : ve[d], acc);
+    if (half == 1) part[d] = acc;
+    __syncthreads();
+    if (half == 0) out[h * kHd + d] = tobf((acc + part[d]) / sum);
+}
+
+__global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
+                                uint16_t* __restrict__ out, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float x = bf(g[i]);
+        out[i] = tobf(rbf(x / (1.f + expf(-x))) * bf(u[i]));
+    }
+}
+
+__global__ void advance_kernel(const int64_t* __restrict__ next, int64_t* __restrict__ ids,
+                               int64_t* __restrict__ tokens, int32_t* __restrict__ pos, int32_t* __restrict__ count,
+                               int cap) {
+    const int c = *count;
+    if (c < cap) tokens[c] = *next;
+    *ids = *next;
+    *pos += 1;
+    *count = c + 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+cdq_status cdq_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps, uint16_t* out,
+                           int32_t n, void* stream) {
+    if (!h || !w || !out || n < 1) return CDQ_ERR_ARG;
+    add_rmsnorm_kernel<<<1, kNormThreads, 0, (cudaStream_t)stream>>>(h, delta, w, eps, out, n);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* cos_t,
+                           const uint16_t* sin_t, const int32_t* pos, uint16_t* k_cache, uint16_t* v_cache,
+                           int32_t max_len, int32_t n_heads, int32_t n_kv, int32_t head_dim, float scale,
+                           uint16_t* out, void* stream) {
+    if (!q || !k || !v || !cos_t || !sin_t || !pos || !k_cache || !v_cache || !out) return CDQ_ERR_ARG;
+    if (head_dim != kHd || n_kv < 1 || n_heads < n_kv || n_heads % n_kv || max_len < 1 || max_len > 16384)
+        return CDQ_ERR_UNSUPPORTED;
+    if ((uintptr_t)k_cache % 16 || (uintptr_t)v_cache % 16) return CDQ_ERR_ARG;
+    const int smem = max_len * 4;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return CDQ_ERR_CUDA;
+    attn_decode_kernel<<<n_heads, kAttnThreads, smem, (cudaStream_t)stream>>>(
+        q, k, v, cos_t, sin_t, pos, k_cache, v_cache, max_len, n_heads, n_kv, scale, out, max_len);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n, void* stream) {
+    if (!g || !u || !out || n < 1 || n > ((int64_t)1 << 30)) return CDQ_ERR_ARG;
+    const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+    silu_mul_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(g, u, out, (int)n);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_decode_advance(const int64_t* next, int64_t* ids, int64_t* tokens, int32_t* pos, int32_t* count,
+                              int32_t cap, void* stream) {
+    if (!next || !ids || !tokens || !pos || !count || cap < 1) return CDQ_ERR_ARG;
+    advance_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(next, ids, tokens, pos, count, cap);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+}  // extern "C"

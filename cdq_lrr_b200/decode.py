@@ -195,3 +195,154 @@ def greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool 
     return {"tokens": torch.cat(toks, dim=1), "prefill_ms": e[0].elapsed_time(e[1]),
             "decode_ms_per_token": e[2].elapsed_time(e[3]) / steps,
             "tokens_per_s": 1e3 * steps / max(e[2].elapsed_time(e[3]), 1e-9), "graphed": dec.graphed}
+
+
+class FusedDecoder:
+    """Batch-1 greedy decoder whose one-token step runs on this library's
+    kernels only, plus torch's embedding gather, the tied bf16 lm_head GEMV
+    and argmax: per layer, the fused residual-add + RMSNorm, one grouped CDQ
+    launch for q/k/v (with their biases), the rotary embedding + cache append +
+    grouped-query attention kernel, o_proj, the second add + RMSNorm, one
+    grouped launch for gate/up, SiLU(gate) * up, down_proj. The step's token
+    and position live on the device (cdq_decode_advance), so one CUDA graph of
+    the step replays per token with no host work in between. Prefill runs the
+    HF model itself into the same static cache (the reference's forward,
+    code/cdq_lrr_qwen05.py:300-330), whose [1, kv_heads, max_len, head_dim]
+    tensors the attention kernel then reads and appends to."""
+
+    def __init__(self, model, max_len: int):
+        from transformers import StaticCache
+        from . import _lib as L
+        from . import ops
+        self.L = L
+        self.model = model
+        cfg = model.config
+        self.dev = next(model.parameters()).device
+        self.max_len = max_len
+        self.H = cfg.hidden_size
+        self.n_heads, self.n_kv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.hd = getattr(cfg, "head_dim", None) or self.H // self.n_heads
+        self.eps = float(cfg.rms_norm_eps)
+        self.cache = StaticCache(config=cfg, max_cache_len=max_len)
+        bf16, dev = torch.bfloat16, self.dev
+        pos_ids = torch.arange(max_len, device=dev)[None]
+        with torch.no_grad():
+            cos, sin = model.model.rotary_emb(torch.zeros(1, 1, self.H, dtype=bf16, device=dev), pos_ids)
+        self.cos, self.sin = cos[0].contiguous(), sin[0].contiguous()
+        z = lambda n, dt=bf16: torch.zeros(n, dtype=dt, device=dev)  # noqa: E731
+        self.ids = z(1, torch.long)
+        self.pos = z(1, torch.int32)
+        self.count = z(1, torch.int32)
+        self.tokens = z(max_len, torch.long)
+        self.h, self.xn = z(self.H), z(self.H)
+        qd, kvd = self.n_heads * self.hd, self.n_kv * self.hd
+        self.q, self.k, self.v, self.att = z(qd), z(kvd), z(kvd), z(qd)
+        self.o = z(self.H)
+        self.inter = model.model.layers[0].mlp.gate_proj.out_features
+        self.g, self.u, self.act, self.dn = z(self.inter), z(self.inter), z(self.inter), z(self.H)
+        row = lambda t: t.view(1, -1)  # noqa: E731
+        self.layers = []
+        for layer in model.model.layers:
+            a, mlp = layer.self_attn, layer.mlp
+            T = lambda mod, x, y: ops.GemvTask(mod.device_pack, row(x), row(y), mod.bias)  # noqa: E731
+            self.layers.append({
+                "ln1": layer.input_layernorm.weight, "ln2": layer.post_attention_layernorm.weight,
+                "qkv": ops.GroupedLinear([T(a.q_proj, self.xn, self.q), T(a.k_proj, self.xn, self.k),
+                                          T(a.v_proj, self.xn, self.v)], m=1),
+                "o": ops.GroupedLinear([T(a.o_proj, self.att, self.o)], m=1),
+                "gu": ops.GroupedLinear([T(mlp.gate_proj, self.xn, self.g), T(mlp.up_proj, self.xn, self.u)], m=1),
+                "down": ops.GroupedLinear([T(mlp.down_proj, self.act, self.dn)], m=1),
+            })
+        self.norm_w = model.model.norm.weight
+        self.lm_w = model.lm_head.weight
+        self.graph = None
+
+    def _call(self, name: str, *args) -> None:
+        self.L.check(getattr(self.L.lib(), name)(*args), name)
+
+    def _step(self) -> None:
+        p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        s = torch.cuda.current_stream(self.dev).cuda_stream
+        self.h.copy_(torch.nn.functional.embedding(self.ids, self.model.model.embed_tokens.weight)[0])
+        for li, Ly in enumerate(self.layers):
+            cl = self.cache.layers[li]
+            self._call("cdq_add_rmsnorm", p(self.h), p(self.dn) if li else None, p(Ly["ln1"]), self.eps,
+                       p(self.xn), self.H, s)
+            Ly["qkv"]()
+            self._call("cdq_attn_decode", p(self.q), p(self.k), p(self.v), p(self.cos), p(self.sin), p(self.pos),
+                       p(cl.keys), p(cl.values), self.max_len, self.n_heads, self.n_kv, self.hd,
+                       float(self.hd) ** -0.5, p(self.att), s)
+            Ly["o"]()
+            self._call("cdq_add_rmsnorm", p(self.h), p(self.o), p(Ly["ln2"]), self.eps, p(self.xn), self.H, s)
+            Ly["gu"]()
+            self._call("cdq_silu_mul", p(self.g), p(self.u), p(self.act), self.inter, s)
+            Ly["down"]()
+        self._call("cdq_add_rmsnorm", p(self.h), p(self.dn), p(self.norm_w), self.eps, p(self.xn), self.H, s)
+        self.logits = torch.nn.functional.linear(self.xn.view(1, -1), self.lm_w)
+        nxt = self.logits.argmax(-1)
+        self._call("cdq_decode_advance", p(nxt), p(self.ids), p(self.tokens), p(self.pos), p(self.count),
+                   self.max_len, s)
+
+    @torch.no_grad()
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        n = prompt.shape[1]
+        pos = torch.arange(n, device=self.dev)
+        out = self.model(input_ids=prompt, past_key_values=self.cache, cache_position=pos,
+                         position_ids=pos[None], use_cache=True, logits_to_keep=1)
+        tok = out.logits[:, -1].argmax(-1)
+        self.reset(tok, n)
+        return tok
+
+    def reset(self, tok: torch.Tensor, position: int) -> None:
+        self.ids.copy_(tok.view(1))
+        self.pos.fill_(position)
+        self.count.zero_()
+
+    @torch.no_grad()
+    def capture(self) -> None:
+        """Two eager warm-up steps (they write the cache at the next two
+        positions, which decoding overwrites), then the graph of one step;
+        the token, position and count are restored afterwards."""
+        tok, at = self.ids.clone(), int(self.pos.item())
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.reset(tok, at)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._step()
+        self.graph = g
+        self.reset(tok, at)
+
+    @torch.no_grad()
+    def step(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+
+@torch.no_grad()
+def fused_greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True) -> dict:
+    """greedy_decode's contract on the fused decode step (FusedDecoder)."""
+    P = prompt.shape[1]
+    dec = FusedDecoder(model, P + new_tokens + 2)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    e[0].record()
+    tok = dec.prefill(prompt)
+    e[1].record()
+    if use_graph:
+        dec.capture()
+    e[2].record()
+    for _ in range(new_tokens - 1):
+        dec.step()
+    e[3].record()
+    torch.cuda.synchronize()
+    steps = max(new_tokens - 1, 1)
+    toks = torch.cat([tok.view(1, 1), dec.tokens[: new_tokens - 1].view(1, -1)], dim=1)
+    return {"tokens": toks, "prefill_ms": e[0].elapsed_time(e[1]),
+            "decode_ms_per_token": e[2].elapsed_time(e[3]) / steps,
+            "tokens_per_s": 1e3 * steps / max(e[2].elapsed_time(e[3]), 1e-9), "graphed": use_graph}

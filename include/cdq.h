@@ -231,6 +231,32 @@ CDQ_API cdq_status cdq_allreduce_f32(void* const* regions, int32_t world, int32_
 CDQ_API cdq_status cdq_ar_error(int32_t* code);
 
 /*
+ * Batch-1 decode-step kernels around the fused linear, for a Qwen2-style
+ * decoder layer (the reference runs HF's Qwen2 modules around CDQLinear,
+ * code/cdq_lrr_qwen05.py:300-330; these replace Qwen2RMSNorm, the rotary
+ * embedding, the static-cache update, attention and Qwen2MLP's act_fn(gate)*up
+ * with the same bf16 rounding steps). All tensors bf16 bit patterns on the
+ * device, enqueued on `stream`.
+ *   cdq_add_rmsnorm: h = h + delta (if delta), out = w * norm(h); n <= 1 block.
+ *   cdq_attn_decode: q [n_heads*64], k, v [n_kv*64]; cos_t/sin_t [max_len][64];
+ *     *pos (device int32) the step's position; k_cache/v_cache [n_kv][max_len][64]
+ *     (HF StaticCache layout, batch 1), the step's k and v written at *pos;
+ *     out [n_heads*64]. head_dim must be 64.
+ *   cdq_silu_mul: out = silu(g) * u.
+ *   cdq_decode_advance: tokens[*count] = *next (if *count < cap), *ids = *next,
+ *     ++*pos, ++*count: the step's greedy token feeds the next step on the device.
+ */
+CDQ_API cdq_status cdq_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps,
+                                   uint16_t* out, int32_t n, void* stream);
+CDQ_API cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                   const uint16_t* cos_t, const uint16_t* sin_t, const int32_t* pos,
+                                   uint16_t* k_cache, uint16_t* v_cache, int32_t max_len, int32_t n_heads,
+                                   int32_t n_kv, int32_t head_dim, float scale, uint16_t* out, void* stream);
+CDQ_API cdq_status cdq_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n, void* stream);
+CDQ_API cdq_status cdq_decode_advance(const int64_t* next, int64_t* ids, int64_t* tokens, int32_t* pos,
+                                      int32_t* count, int32_t cap, void* stream);
+
+/*
  * Bit-exact w_hat [rows, cols] bf16 from a device pack.
  * Replaces dequantize, code/cdq_lrr_qwen05.py:141-152, and
  * CDQLinear.dequant_weight, code/cdq_lrr_qwen05.py:188-194.
