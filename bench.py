@@ -62,6 +62,9 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=1, help="tp7b: activation rows (1 or 8)")
     ap.add_argument("--allreduce", choices=("oneshot", "nccl"), default="oneshot",
                     help="tp7b/tp70b: the row-parallel reduction")
+    ap.add_argument("--tp-worlds", type=int, nargs="*", default=None,
+                    help="tpsweep: the tensor-parallel widths to run at batch 1 (default 1, 2, 4 ... up to "
+                         "the number of GPUs); batch 8, NCCL and the 70B shapes run on all GPUs")
     ap.add_argument("--tile-min-batch", type=int, default=16,
                     help="smallest batch that takes the tcgen05 tile path (the library default is 16)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -719,10 +722,10 @@ def run_tp(args, shapes, n_layers: int, n_states: int, label: str) -> None:
 
 
 def run_tpsweep(args) -> None:
-    """Every tensor-parallel configuration in one launch: the 7B-shape stack at
-    batch 1 and 8 on 1, 2, 4 ... world GPUs (subgroups of the first ranks; the
-    others wait), each with the one-shot all-reduce and, at batch 1, with
-    NCCL; the 70B MLP shapes in both lattice tiers on all GPUs. One JSON line
+    """The tensor-parallel configurations in one launch: the 7B-shape stack at
+    batch 1 on each width of --tp-worlds (subgroups of the first ranks; the
+    others wait) with the one-shot all-reduce; on all GPUs also batch 1 with
+    NCCL, batch 8, and the 70B MLP shapes in both lattice tiers. One JSON line
     (rank 0) with every result in "sweep"."""
     import torch
     import torch.distributed as dist
@@ -733,16 +736,17 @@ def run_tpsweep(args) -> None:
     s7 = [(n, r, c, kinds[n]) for n, r, c in layer_shapes(QWEN7B)]
     (r1, c1), (r2, c2) = LLAMA70B_SHAPES
     s70 = [("up_proj", r1, c1, "col"), ("down_proj", r2, c2, "row")]
-    worlds = [w for w in (1, 2, 4, 8) if w <= ws_]
+    worlds = [w for w in (1, 2, 4, 8) if w <= ws_ and (args.tp_worlds is None or w in args.tp_worlds)]
+    if ws_ not in worlds:
+        worlds.append(ws_)
     runs = []
     for w in worlds:
-        for b, ar in ((1, "oneshot"), (1, "nccl"), (8, "oneshot")):
-            if w == 1 and ar == "nccl":
-                continue
-            runs.append(("7b", s7, QWEN7B["layers"], 26, b, ar, w))
+        runs.append(("7b", s7, QWEN7B["layers"], 26, 1, "oneshot", w))
+    if ws_ > 1:
+        runs.append(("7b", s7, QWEN7B["layers"], 26, 1, "nccl", ws_))
+    runs.append(("7b", s7, QWEN7B["layers"], 26, 8, "oneshot", ws_))
     for ns in (26, 16):
         runs.append(("70b", s70, 4, ns, 1, "oneshot", ws_))
-    runs.append(("70b", s70, 4, 26, 1, "nccl", ws_))
     results = []
     groups = {}
     for w in worlds:  # every rank creates every subgroup, in the same order
