@@ -130,7 +130,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     const int d = tid & (kHd - 1), half = tid / kHd;
     const uint16_t* vb = vc + (int64_t)kvh * max_len * kHd;
     float acc = 0.f;
-    for (int j = half; j <= P; j += 2) acc = fmaf(scores[j], j < P ? bf(vb[(int64_t)j * kHd + d]) : ve[d], acc);
+#pragma unroll 8
+    for (int j = half; j < P; j += 2) acc = fmaf(scores[j], bf(vb[(int64_t)j * kHd + d]), acc);
+    if ((P & 1) == half) acc = fmaf(scores[P], ve[d], acc);  // the step's own value
     if (half == 1) part[d] = acc;
     __syncthreads();
     if (half == 0) out[h * kHd + d] = tobf((acc + part[d]) / sum);

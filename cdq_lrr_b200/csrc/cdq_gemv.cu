@@ -482,6 +482,17 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         float d[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
+        // A job of one residual group (every row's K in this item): the warp
+        // finishes its 16 rows itself, with the fix-up pass's arithmetic in the
+        // fix-up pass's order. Lane (row rr, half rh) reads the row's residual
+        // bounds now and warms L2 with its entries after the first quad.
+        const bool direct = NT == 1 && J.kg == 1;
+        const int rr = I.b16 * 16 + (lane >> 1), rh = lane & 1;
+        uint32_t reb = 0, ree = 0;
+        if (direct) {
+            reb = __ldg(J.res_ptr + rr) + rh;
+            ree = min(__ldg(J.res_ptr + rr + 1), J.n_res);
+        }
         // unit i of quad q: the narrow path (one n-tile) or the wide one
         auto run_unit = [&](const uint4& A, uint32_t w4, uint32_t sw, bool hi_half, const uint4& xa,
                             const uint4& xb, int unit) {
@@ -598,8 +609,59 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             }
             c_slot ^= 1u;
             c_phase ^= c_slot == 0 ? 1u : 0u;
+            if (direct && q == 0 && reb < ree) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(J.res_ent + reb));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(J.res_ent + ree - 1));
+            }
         }
         if (failed) break;
+        if constexpr (NT == 1) {
+            if (direct) {
+                // y = (this group's sum) + (the row's residual entries, bf16 value x
+                // activation in fp32, entry order, split over the lane pair) + bias
+                float acc[M];
+#pragma unroll
+                for (int n = 0; n < M; ++n) acc[n] = 0.f;
+                for (uint32_t e0 = reb; e0 < ree; e0 += 16) {
+                    uint32_t en[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) en[t] = e0 + 2 * t < ree ? __ldg(J.res_ent + e0 + 2 * t) : 0u;
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        const uint32_t col = en[t] >> 16;
+                        if (e0 + 2 * t < ree && col < (uint32_t)J.cols) {
+                            const float v = __uint_as_float(en[t] << 16);
+#pragma unroll
+                            for (int n = 0; n < M; ++n)
+                                acc[n] = fmaf(v, bf16_to_f32(__ldg(J.x + (int64_t)n * J.cols + col)), acc[n]);
+                        }
+                    }
+                }
+                float R[4] = {0.f, 0.f, 0.f, 0.f};  // (row g, 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
+#pragma unroll
+                for (int n = 0; n < M; ++n) {
+                    acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
+                    const float a = __shfl_sync(0xFFFFFFFFu, acc[n], 2 * g);
+                    const float b = __shfl_sync(0xFFFFFFFFu, acc[n], 2 * g + 16);
+                    if (n == 2 * c) {
+                        R[0] = a;
+                        R[2] = b;
+                    }
+                    if (n == 2 * c + 1) {
+                        R[1] = a;
+                        R[3] = b;
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = I.b16 * 16 + g + 8 * h;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        if (row < J.rows && 2 * c + j < M) store_out(J, 2 * c + j, row, d[0][2 * h + j] + R[2 * h + j]);
+                }
+                continue;
+            }
+        }
         // this group's partial sums of rows g and g + 8 (batch columns 8t + 2c, 8t + 2c + 1)
         const int64_t rpad = (int64_t)J.r16 * 16;
 #pragma unroll
@@ -730,14 +792,21 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
 
 // The fix-up pass over every job's row blocks (kFixThreads / 32 per block, jobs
 // back to back); batches above 8 are fixed up in chunks of 8 batch rows.
+// single_done: the streaming pass finished the jobs of one residual group
+// (batch <= 8), which the fix-up pass then leaves out (no launch if none is left).
 template <int MAXJ>
-cudaError_t launch_fixup(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream) {
+cudaError_t launch_fixup(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream, bool single_done = false) {
     GemvBatch<MAXJ> fb = b;
-    int blocks = 0;
-    for (int j = 0; j < fb.n; ++j) {
-        fb.jobs[j].rb_begin = blocks;
-        blocks += (fb.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
+    int blocks = 0, n = 0;
+    for (int j = 0; j < b.n; ++j) {
+        if (single_done && b.jobs[j].kg == 1) continue;
+        fb.jobs[n] = b.jobs[j];
+        fb.jobs[n].rb_begin = blocks;
+        blocks += (b.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
+        ++n;
     }
+    fb.n = n;
+    if (n == 0) return cudaSuccess;
     const int grid = std::max(blocks, 1);
     switch (m) {
         case 1: fixup_kernel<1, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
@@ -762,7 +831,7 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     kern<<<grid, kThreads, kSmemBytes, stream>>>(b);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_fixup(b, b.m, stream);
+    return launch_fixup(b, b.m, stream, M <= 8);
 }
 
 // The tile path: a launch that lays out the activations (once per distinct x
