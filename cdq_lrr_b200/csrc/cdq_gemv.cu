@@ -482,11 +482,13 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         float d[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
-        // A job of one residual group (every row's K in this item): the warp
-        // finishes its 16 rows itself, with the fix-up pass's arithmetic in the
-        // fix-up pass's order. Lane (row rr, half rh) reads the row's residual
-        // bounds now and warms L2 with its entries after the first quad.
-        const bool direct = NT == 1 && J.kg == 1;
+        // A job of one residual group (every row's K in this item), in a launch
+        // small enough that the fix-up launch would cost more than the rows'
+        // residual tail stalls this warp: the warp finishes its 16 rows itself,
+        // with the fix-up pass's arithmetic in the fix-up pass's order. Lane
+        // (row rr, half rh) reads the row's residual bounds now and warms L2
+        // with its entries after the first quad.
+        const bool direct = NT == 1 && J.kg == 1 && batch.finish_single;
         const int rr = I.b16 * 16 + (lane >> 1), rh = lane & 1;
         uint32_t reb = 0, ree = 0;
         if (direct) {
@@ -828,10 +830,16 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     if (e != cudaSuccess) return e;
     const int64_t want = (b.total_items + kWarps - 1) / kWarps;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, num_sms));
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(b);
+    // at most one item per warp of the grid (the projections of a decode step):
+    // finishing single-group rows in the streaming pass saves the fix-up
+    // launch; larger launches keep the two passes (the rows' residual tail
+    // would stall warps that have more items to stream)
+    GemvBatch<MAXJ> sb = b;
+    sb.finish_single = M <= 8 && b.total_items <= (int64_t)kWarps * num_sms ? 1 : 0;
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(sb);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_fixup(b, b.m, stream, M <= 8);
+    return launch_fixup(b, b.m, stream, sb.finish_single != 0);
 }
 
 // The tile path: a launch that lays out the activations (once per distinct x
@@ -1042,7 +1050,7 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     b.total_items = (int64_t)J.r16 * J.kg;
     b.total_row_blocks = J.r16;
     b.m = (int32_t)m;
-    b.reserved0 = 0;
+    b.finish_single = 0;
     // the streaming path only: its scratch is sized for the group sums
     return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms, false) == cudaSuccess
                ? CDQ_OK

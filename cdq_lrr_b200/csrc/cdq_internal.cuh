@@ -36,7 +36,7 @@ struct GemvBatch {
     int32_t n;
     int32_t total_row_blocks;  // fix-up pass work
     int32_t m;                 // batch rows of every job of the launch
-    int32_t reserved0;
+    int32_t finish_single;     // streaming pass finishes single-group jobs itself (small launches)
     GemvJob jobs[MAXJ];
 };
 
