@@ -1,4 +1,6 @@
-// Fused dequant-GEMV for the CDQ-LRR device pack, batch M <= 8.
+// Fused dequant linear for the CDQ-LRR device pack: the streaming pass (batch
+// M <= 64, n-tiles of 8 above 8), the fix-up pass and the launchers of both
+// paths.
 //
 // y[m, row] = sum_col w_hat[row, col] * x[m, col] (+ bias[row]) where
 // w_hat = bf16(LATTICE[q] * sigma) is rebuilt in registers from the packed
@@ -32,7 +34,12 @@
 // slot of the workspace (no residuals, fences or atomics on its path); the
 // fix-up pass adds, per output, the group slots in group order, the row's
 // residual entries (bf16 value x activation in fp32) and the bias, and
-// rounds once. Both passes are deterministic.
+// rounds once. Both passes are deterministic. In a launch with at most one
+// item per warp (the projections of a decode step), the streaming warp itself
+// finishes the rows of single-group jobs with the same arithmetic in the same
+// order, and the fix-up pass runs only for the multi-group jobs. Batches of
+// 16 and more go to the tcgen05 tile path (cdq_tile.cuh) when the launch has
+// enough 128-row tiles.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
