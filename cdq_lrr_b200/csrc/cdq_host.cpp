@@ -207,7 +207,7 @@ cdq_status cdq_host_from_reference(int32_t rows, int32_t cols, int32_t n_states,
                 }
         }
     }
-    // residual CSR: bucket (b16, group, row in block)
+    // residual CSR: bucket (row, group), row major
     const int64_t nb = g.r16 * g.kg * 16;
     std::vector<int64_t> cnt(nb + 1, 0);
     auto bucket_of = [&](int64_t f) {

@@ -104,6 +104,35 @@ class DevicePack:
         host.n_res = int(ri.size)
         return host if torch.device(device).type == "cpu" else host.to(device)
 
+    @classmethod
+    def from_reference_device(cls, quant_indices: torch.Tensor, scales_f8: torch.Tensor,
+                              residual_indices: torch.Tensor, residual_values: torch.Tensor,
+                              rows: int, cols: int, n_states: int) -> "DevicePack":
+        """Reference pack tensors already on a CUDA device -> device layout, on the
+        GPU (cdq_pack_from_reference_device; byte-identical to from_reference)."""
+        dev = quant_indices.device
+        for t in (scales_f8, residual_indices, residual_values):
+            if t.device != dev:
+                raise ValueError("reference pack tensors must be on one CUDA device")
+        q = quant_indices.reshape(-1).contiguous().view(torch.uint8)
+        sc = scales_f8.reshape(-1).contiguous().view(torch.uint8)
+        ri = residual_indices.reshape(-1).to(torch.int64).contiguous()
+        rv = residual_values.reshape(-1).contiguous().view(torch.int16)
+        if q.numel() != rows * cols or sc.numel() != rows * cols // TILE or ri.numel() != rv.numel():
+            raise ValueError("reference pack tensors do not match the weight shape")
+        pack = cls.empty(rows, cols, n_states, ri.numel(), dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = pack.struct()
+        with torch.cuda.device(dev):
+            L.check(L.lib().cdq_pack_from_reference_device(
+                rows, cols, n_states, q.data_ptr(), sc.data_ptr(), ri.data_ptr() if ri.numel() else None,
+                rv.data_ptr() if rv.numel() else None, ri.numel(), C.byref(st), err.data_ptr(),
+                torch.cuda.current_stream(dev).cuda_stream), "cdq_pack_from_reference_device")
+        if int(err.item()) != 0:
+            raise ValueError("malformed reference pack (lattice index or residual positions)")
+        pack.n_res = int(ri.numel())
+        return pack
+
     def to_reference(self) -> dict[str, np.ndarray]:
         """Device layout -> reference pack arrays (numpy, host)."""
         host = self.to("cpu")

@@ -231,6 +231,24 @@ CDQ_API cdq_status cdq_allreduce_f32(void* const* regions, int32_t world, int32_
 CDQ_API cdq_status cdq_ar_error(int32_t* code);
 
 /*
+ * Device-side ingest of a reference-format pack: q [rows*cols/32][32] lattice
+ * indices, scales_f8 [rows*cols/32] e4m3fn bytes, ridx [n_res] strictly
+ * ascending flat indices (int64) and rval [n_res] bf16 bits, all in device
+ * memory (for example the arrays of a .cdq file copied to the GPU), into the
+ * device buffers of `out` (sized by cdq_get_sizes with n_res <= max_res).
+ * Byte-identical to cdq_host_from_reference; three launches on `stream`, no
+ * temporary memory. *error (device int32, zeroed by the caller) becomes 1 on
+ * malformed input (an index >= n_states, residual positions out of range or
+ * not ascending), in which case the pack is incomplete.
+ * Replaces the per-tile Python parse of the loader (code/cdq_loader.py:79-87)
+ * and CDQLinear's buffer set-up (code/cdq_lrr_qwen05.py:155-166).
+ */
+CDQ_API cdq_status cdq_pack_from_reference_device(int32_t rows, int32_t cols, int32_t n_states,
+                                                  const uint8_t* q, const uint8_t* scales_f8,
+                                                  const int64_t* ridx, const uint16_t* rval, int64_t n_res,
+                                                  cdq_packed* out, int32_t* error, void* stream);
+
+/*
  * Batch-1 decode-step kernels around the fused linear, for a Qwen2-style
  * decoder layer (the reference runs HF's Qwen2 modules around CDQLinear,
  * code/cdq_lrr_qwen05.py:300-330; these replace Qwen2RMSNorm, the rotary

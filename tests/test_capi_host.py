@@ -186,3 +186,18 @@ def test_bit_packers_mirror_reference(L):
     assert torch.equal(v2.view(torch.int16), vals.view(torch.int16))
     ob, vb = O.pack_residual_blobs(np.array([3]), offs.numpy(), vals.view(torch.int16).numpy().view(np.uint16))
     assert ob.tobytes() == blob
+
+
+def test_device_ingest_argument_checks():
+    """The device ingest entry point rejects bad shapes, lattices and null
+    buffers before touching the GPU."""
+    import ctypes as C
+    from cdq_lrr_b200 import _lib as L
+    lib = L.lib()
+    st = L.cdq_packed()
+    P = C.c_void_p(16)
+    assert lib.cdq_pack_from_reference_device(4, 32, 25, P, P, None, None, 0, C.byref(st), P, None) == 2
+    assert lib.cdq_pack_from_reference_device(4, 33, 26, P, P, None, None, 0, C.byref(st), P, None) == 1
+    assert lib.cdq_pack_from_reference_device(4, 32, 26, None, P, None, None, 0, C.byref(st), P, None) == 3
+    assert lib.cdq_pack_from_reference_device(4, 32, 26, P, P, None, None, 0, C.byref(st), None, None) == 3
+    assert lib.cdq_pack_from_reference_device(4, 32, 26, P, P, None, None, 5, C.byref(st), P, None) == 3

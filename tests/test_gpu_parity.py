@@ -384,3 +384,70 @@ def test_linear_shapes_batches_bias(shape, ns, m):
     y = ops.linear(dp, x, bias.cuda(), out_f32=True)
     torch.cuda.synchronize()
     _check_gemv(y, O.linear_f64(O.dequantize(p), _bits(x), _bits(bias)))
+
+
+def _random_reference(rows, cols, ns, seed, frac=0.0156, pairs=True):
+    rng = np.random.default_rng(seed)
+    n = rows * cols
+    q = rng.integers(0, ns, (n // 32, 32), dtype=np.uint8)
+    sc = rng.integers(0, 0x7F, n // 32, dtype=np.uint8)
+    k = int(round(n * frac))
+    ri = rng.choice(n, k, replace=False)
+    if pairs and k > 4:  # force some pairs whose two elements are both residuals
+        ev = (ri[: k // 4] // 2) * 2
+        ri = np.unique(np.concatenate([ri, ev, ev + 1]))
+    ri = np.sort(np.unique(ri)).astype(np.int64)
+    rv = rng.integers(0, 0xFFFF, ri.size, dtype=np.uint16)
+    return q, sc, ri, rv
+
+
+@pytest.mark.parametrize("shape,ns", [((45, 96), 26), ((200, 2080), 26), ((128, 512), 16), ((896, 4864), 26),
+                                      ((33, 1088), 16), ((16, 32), 26)])
+def test_device_ingest_matches_host(shape, ns):
+    """The GPU converter from the reference format produces the host
+    converter's device pack byte for byte (ragged row blocks, odd tile counts,
+    several residual groups, adjacent residual pairs, both lattices)."""
+    from cdq_lrr_b200 import ops
+    rows, cols = shape
+    q, sc, ri, rv = _random_reference(rows, cols, ns, seed=rows + cols + ns)
+    host = ops.DevicePack.from_reference(q, sc, ri, rv, rows, cols, ns, device="cpu")
+    dev = ops.DevicePack.from_reference_device(torch.from_numpy(q).cuda(), torch.from_numpy(sc).cuda(),
+                                               torch.from_numpy(ri).cuda(),
+                                               torch.from_numpy(rv.view(np.int16)).cuda(), rows, cols, ns)
+    torch.cuda.synchronize()
+    assert dev.n_res == host.n_res == ri.size
+    assert torch.equal(dev.units.cpu(), host.units)
+    assert torch.equal(dev.res_ptr.cpu(), host.res_ptr)
+    assert torch.equal(dev.res_ent[: ri.size].cpu(), host.res_ent[: ri.size])
+    assert torch.equal(dev.res_q[: ri.size].cpu(), host.res_q[: ri.size])
+
+
+def test_device_ingest_golden_and_rejects_malformed(golden, golden_meta):
+    """Golden reference packs ingested on the GPU dequantize to the oracle's
+    w_hat; an out-of-range lattice index or unsorted residuals are refused."""
+    from cdq_lrr_b200 import ops
+    for name in CASES:
+        ns = golden_meta["cases"][name]["n_states"]
+        rows, cols = golden[f"{name}.weight"].shape
+        p = {k: golden[f"{name}.{k}"] for k in ("quant_indices", "scales_f8", "residual_indices", "residual_values")}
+        dp = ops.DevicePack.from_reference_device(
+            torch.from_numpy(np.ascontiguousarray(p["quant_indices"])).cuda(),
+            torch.from_numpy(np.ascontiguousarray(p["scales_f8"]).reshape(-1)).cuda(),
+            torch.from_numpy(np.ascontiguousarray(p["residual_indices"]).astype(np.int64)).cuda(),
+            torch.from_numpy(np.ascontiguousarray(p["residual_values"]).view(np.int16)).cuda(), rows, cols, ns)
+        w_hat = ops.dequant(dp)
+        torch.cuda.synchronize()
+        assert _nan_equal(_bits(w_hat), golden[f"{name}.w_hat"]), name
+    q, sc, ri, rv = _random_reference(32, 64, 26, seed=1)
+    bad_q = q.copy()
+    bad_q[0, 0] = 26
+    with pytest.raises(ValueError):
+        ops.DevicePack.from_reference_device(torch.from_numpy(bad_q).cuda(), torch.from_numpy(sc).cuda(),
+                                             torch.from_numpy(ri).cuda(), torch.from_numpy(rv.view(np.int16)).cuda(),
+                                             32, 64, 26)
+    if ri.size > 1:
+        bad_r = ri[::-1].copy()
+        with pytest.raises(ValueError):
+            ops.DevicePack.from_reference_device(torch.from_numpy(q).cuda(), torch.from_numpy(sc).cuda(),
+                                                 torch.from_numpy(bad_r).cuda(),
+                                                 torch.from_numpy(rv.view(np.int16)).cuda(), 32, 64, 26)
