@@ -87,7 +87,24 @@ class DevicePack:
     @classmethod
     def from_reference(cls, quant_indices, scales_f8, residual_indices, residual_values,
                        rows: int, cols: int, n_states: int, device="cpu") -> "DevicePack":
-        """Reference pack tensors (code/cdq_lrr_qwen05.py:121-133) -> device layout."""
+        """Reference pack tensors (code/cdq_lrr_qwen05.py:121-133) -> device layout.
+        For a CUDA device the arrays are copied there as they are and converted
+        by the device ingest (byte-identical to the host converter used for
+        device="cpu")."""
+        if torch.device(device).type == "cuda":
+            def up(a, dt):
+                t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(_np(a, dt)))
+                return t.to(device)
+            rv = residual_values
+            if not isinstance(rv, torch.Tensor):
+                rv = torch.from_numpy(np.ascontiguousarray(_np(rv, np.uint16)).view(np.int16))
+            try:
+                return cls.from_reference_device(up(quant_indices, np.uint8), up(scales_f8, np.uint8),
+                                                 up(residual_indices, np.int64), rv.to(device), rows, cols, n_states)
+            except ValueError as e:
+                if "malformed" not in str(e):
+                    raise
+                raise L.CdqError(3, "cdq_pack_from_reference_device") from e
         q = np.ascontiguousarray(_np(quant_indices, np.uint8).reshape(-1))
         sc = np.ascontiguousarray(_np(scales_f8, np.uint8).reshape(-1))
         ri = np.ascontiguousarray(_np(residual_indices, np.int64).reshape(-1))
