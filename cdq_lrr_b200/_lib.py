@@ -84,6 +84,9 @@ _SIGS = {
     "cdq_ar_error": (C.c_int, [C.POINTER(C.c_int32)]),
     "cdq_pack_from_reference_device": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, C.c_int64,
                                                  C.POINTER(cdq_packed), _P, _P]),
+    "cdq_file_checkpoints": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), C.c_int32, _P, _P]),
+    "cdq_file_decode_device": (C.c_int, [_P, C.c_int64, C.c_int32, C.c_int64, C.c_int64, C.c_int32, _P, _P,
+                                         _P, _P, _P, _P, _P, _P]),
     "cdq_add_rmsnorm": (C.c_int, [_P, _P, _P, C.c_float, _P, C.c_int32, _P]),
     "cdq_attn_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                   C.c_float, _P, _P]),

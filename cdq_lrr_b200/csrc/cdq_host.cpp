@@ -333,6 +333,28 @@ cdq_status cdq_file_scan(const uint8_t* data, int64_t len, int32_t* n_states,
     return CDQ_OK;
 }
 
+cdq_status cdq_file_checkpoints(const uint8_t* data, int64_t len, int32_t n_states, const cdq_file_tensor* t,
+                                int32_t every, int64_t* byte_off, int64_t* res_off) {
+    if (!data || !t || !byte_off || !res_off || every < 1) return CDQ_ERR_ARG;
+    if (n_states != 26 && n_states != 16) return CDQ_ERR_STATES;
+    if (t->record_offset < 0 || t->record_offset + t->record_bytes > len) return CDQ_ERR_FORMAT;
+    const int ib = idx_bytes(n_states);
+    int64_t pos = t->record_offset, n = 0;
+    for (int64_t k = 0; k < t->n_tiles; ++k) {
+        if (k % every == 0) {
+            byte_off[k / every] = pos - t->record_offset;
+            res_off[k / every] = n;
+        }
+        if (pos + 2 + ib > len) return CDQ_ERR_FORMAT;
+        const int tc = data[pos + 1];
+        if (tc > 32) return CDQ_ERR_FORMAT;
+        pos += 2 + ib + blob_bytes(tc);
+        if (pos > len) return CDQ_ERR_FORMAT;
+        n += tc;
+    }
+    return n == t->n_res && pos - t->record_offset == t->record_bytes ? CDQ_OK : CDQ_ERR_FORMAT;
+}
+
 cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
                            const cdq_file_tensor* t, uint8_t* q, uint8_t* scales_f8,
                            int64_t* ridx, uint16_t* rval) {

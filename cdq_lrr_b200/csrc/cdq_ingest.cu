@@ -17,6 +17,11 @@
 //      first entry by binary search over the sorted residuals.
 // Malformed input (an index >= n_states, residual positions out of range or
 // not ascending) sets *error to 1; the pack is then incomplete.
+//
+// The reference arrays themselves can come from the .cdq bytes on the device
+// too (cdq_file_decode_device): the file's tile records are variable-length,
+// so a host pass over their count bytes (cdq_file_checkpoints) records where
+// every span of tiles starts, and one thread per span unpacks it.
 #include <cuda_runtime.h>
 
 #include "cdq.h"
@@ -120,6 +125,88 @@ __global__ void ingest_bounds(Geometry g, const int64_t* __restrict__ ridx, int6
     }
 }
 
+// Tile records of a .cdq tensor (code/cdq_pack.py:183-190): scale byte,
+// residual count tc, 20 (5-bit LSB-first) or 16 (nibble) index bytes, then
+// tc residuals of 21 bits (5-bit offset, 16-bit bf16) LSB-first. One thread per
+// span of `every` tiles, from the span's checkpoint (byte offset within the
+// records, first residual index); residuals of a tile sorted by offset.
+__global__ void file_decode_spans(const uint8_t* __restrict__ rec, int64_t rec_bytes, int ns, int64_t n_tiles,
+                                  int64_t n_res, int every, const int64_t* __restrict__ byte_off,
+                                  const int64_t* __restrict__ res_off, uint8_t* __restrict__ q,
+                                  uint8_t* __restrict__ sc, int64_t* __restrict__ ridx, uint16_t* __restrict__ rval,
+                                  int* __restrict__ error) {
+    const int64_t spans = (n_tiles + every - 1) / every;
+    const int ib = ns == 26 ? 20 : 16;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < spans; c += (int64_t)gridDim.x * blockDim.x) {
+        int64_t pos = byte_off[c], n = res_off[c];
+        const int64_t k1 = (c + 1) * every < n_tiles ? (c + 1) * every : n_tiles;
+        bool bad = false;
+        for (int64_t k = c * every; k < k1 && !bad; ++k) {
+            if (pos + 2 + ib > rec_bytes) {
+                bad = true;
+                break;
+            }
+            sc[k] = rec[pos];
+            const int tc = rec[pos + 1];
+            const uint8_t* in = rec + pos + 2;
+            uint8_t* qk = q + k * 32;
+            if (ns == 26) {
+                for (int i = 0; i < 32; ++i) {
+                    const int bit = 5 * i, by = bit >> 3, sh = bit & 7;
+                    const uint32_t v = in[by] | (by + 1 < 20 ? (uint32_t)in[by + 1] << 8 : 0u);
+                    const uint8_t s = (uint8_t)((v >> sh) & 0x1Fu);
+                    bad |= s >= 26;
+                    qk[i] = s;
+                }
+            } else {
+                for (int i = 0; i < 16; ++i) {
+                    qk[2 * i] = in[i] & 0xF;
+                    qk[2 * i + 1] = in[i] >> 4;
+                }
+            }
+            pos += 2 + ib;
+            const int64_t bb = ((int64_t)tc * 21 + 7) / 8;
+            if (tc > 32 || pos + bb > rec_bytes || n + tc > n_res) {
+                bad = true;
+                break;
+            }
+            int offs[32];
+            uint16_t vals[32];
+            for (int j = 0; j < tc; ++j) {
+                uint32_t w[2] = {0u, 0u};
+                for (int f = 0; f < 2; ++f) {
+                    const int64_t p0 = 21LL * j + (f ? 5 : 0);
+                    uint32_t v = 0;
+                    for (int i = 0; i < 3; ++i) {
+                        const int64_t by = (p0 >> 3) + i;
+                        if (by < bb) v |= (uint32_t)rec[pos + by] << (8 * i);
+                    }
+                    w[f] = (v >> (p0 & 7)) & (f ? 0xFFFFu : 0x1Fu);
+                }
+                // insertion by offset (the packer writes them ascending)
+                int at = j;
+                while (at > 0 && offs[at - 1] > (int)w[0]) {
+                    offs[at] = offs[at - 1];
+                    vals[at] = vals[at - 1];
+                    --at;
+                }
+                offs[at] = (int)w[0];
+                vals[at] = (uint16_t)w[1];
+            }
+            for (int j = 0; j < tc; ++j) {
+                bad |= j > 0 && offs[j] == offs[j - 1];
+                ridx[n + j] = k * 32 + offs[j];
+                rval[n + j] = vals[j];
+            }
+            n += tc;
+            pos += bb;
+        }
+        const int64_t end_pos = c + 1 < spans ? byte_off[c + 1] : rec_bytes;
+        const int64_t end_n = c + 1 < spans ? res_off[c + 1] : n_res;
+        if (bad || pos != end_pos || n != end_n) atomicExch(error, 1);
+    }
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t b = (n + threads - 1) / threads;
     return (int)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
@@ -152,4 +239,19 @@ extern "C" cdq_status cdq_pack_from_reference_device(int32_t rows, int32_t cols,
     out->n_states = n_states;
     out->n_res = n_res;
     return CDQ_OK;
+}
+
+extern "C" cdq_status cdq_file_decode_device(const uint8_t* records, int64_t record_bytes, int32_t n_states,
+                                            int64_t n_tiles, int64_t n_res, int32_t every,
+                                            const int64_t* byte_off, const int64_t* res_off, uint8_t* q,
+                                            uint8_t* scales_f8, int64_t* ridx, uint16_t* rval, int32_t* error,
+                                            void* stream) {
+    if (n_states != 26 && n_states != 16) return CDQ_ERR_STATES;
+    if (!records || record_bytes < 0 || n_tiles < 1 || n_res < 0 || every < 1 || !byte_off || !res_off || !q ||
+        !scales_f8 || !error || (n_res > 0 && (!ridx || !rval)))
+        return CDQ_ERR_ARG;
+    const int64_t spans = (n_tiles + every - 1) / every;
+    file_decode_spans<<<grid_for(spans, 128), 128, 0, (cudaStream_t)stream>>>(
+        records, record_bytes, n_states, n_tiles, n_res, every, byte_off, res_off, q, scales_f8, ridx, rval, error);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }

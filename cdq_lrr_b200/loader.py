@@ -19,7 +19,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
-from .pack_file import decode_tensor, scan_cdq
+from .pack_file import decode_tensor_device, scan_cdq
 from .quant import CAMKII_LATTICE
 
 MAGIC, VER = b"CDQ1", 1
@@ -103,10 +103,10 @@ def load_cdq(model, path="qwen05.cdq"):
             mod = model.get_submodule(modname)
         except AttributeError:
             continue
-        d = decode_tensor(raw, n_states, t)
-        pack = ops.DevicePack.from_reference(d["quant_indices"], d["scales_f8"],
-                                             d["residual_indices"], d["residual_values"],
-                                             int(t.rows), int(t.cols), n_states, device=dev)
+        d = decode_tensor_device(raw, n_states, t, dev)  # records unpacked and converted on the GPU
+        pack = ops.DevicePack.from_reference_device(d["quant_indices"], d["scales_f8"],
+                                                    d["residual_indices"], d["residual_values"],
+                                                    int(t.rows), int(t.cols), n_states)
         bias = mod.bias.data if getattr(mod, "bias", None) is not None else None
         cdq = CDQLinear(bias=bias, device_pack=pack)
         parent, _, attr = modname.rpartition(".")

@@ -192,6 +192,40 @@ def decode_tensor(data: bytes, n_states: int, t) -> dict:
     return {"quant_indices": q, "scales_f8": sc, "residual_indices": ri, "residual_values": rv}
 
 
+SPAN_TILES = 256  # tiles per device decode thread
+
+
+def decode_tensor_device(data: bytes, n_states: int, t, device="cuda") -> dict:
+    """One scanned tensor -> reference pack arrays on a CUDA device: a host pass
+    over the records' count bytes finds where every 256-tile span starts
+    (cdq_file_checkpoints), the records go to the device once, and one thread
+    per span unpacks it (cdq_file_decode_device). Same arrays as decode_tensor."""
+    buf = np.frombuffer(data, dtype=np.uint8)
+    spans = -(-int(t.n_tiles) // SPAN_TILES)
+    boff = np.empty(spans, dtype=np.int64)
+    roff = np.empty(spans, dtype=np.int64)
+    L.check(L.lib().cdq_file_checkpoints(buf.ctypes.data_as(C.c_void_p), buf.size, n_states, C.byref(t),
+                                         SPAN_TILES, boff.ctypes.data_as(C.c_void_p),
+                                         roff.ctypes.data_as(C.c_void_p)), f"checkpoints {t.name.decode()}")
+    dev = torch.device(device)
+    rec = torch.from_numpy(buf[t.record_offset:t.record_offset + t.record_bytes].copy()).to(dev)
+    boff_d, roff_d = torch.from_numpy(boff).to(dev), torch.from_numpy(roff).to(dev)
+    q = torch.empty((t.n_tiles, TILE), dtype=torch.uint8, device=dev)
+    sc = torch.empty(t.n_tiles, dtype=torch.uint8, device=dev)
+    ri = torch.empty(t.n_res, dtype=torch.int64, device=dev)
+    rv = torch.empty(t.n_res, dtype=torch.int16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().cdq_file_decode_device(
+            rec.data_ptr(), t.record_bytes, n_states, t.n_tiles, t.n_res, SPAN_TILES, boff_d.data_ptr(),
+            roff_d.data_ptr(), q.data_ptr(), sc.data_ptr(), ri.data_ptr() if t.n_res else None,
+            rv.data_ptr() if t.n_res else None, err.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
+            f"device decode {t.name.decode()}")
+    if int(err.item()):
+        raise L.CdqError(5, f"device decode {t.name.decode()}")
+    return {"quant_indices": q, "scales_f8": sc, "residual_indices": ri, "residual_values": rv}
+
+
 def read_cdq(path) -> dict:
     """code/cdq_pack.py:193-234: {name: {rows, cols, n_tiles, scales_f8_u8, q,
     tag_counts, res_blobs, n_states}}."""
@@ -234,6 +268,12 @@ def read_device_packs(path, device="cuda") -> dict[str, DevicePack]:
     n_states, tabs = scan_cdq(data)
     out = {}
     for t in tabs:
+        if torch.device(device).type == "cuda":  # the records are unpacked and converted on the GPU
+            d = decode_tensor_device(data, n_states, t, device)
+            out[t.name.decode()] = DevicePack.from_reference_device(
+                d["quant_indices"], d["scales_f8"], d["residual_indices"], d["residual_values"],
+                int(t.rows), int(t.cols), n_states)
+            continue
         d = decode_tensor(data, n_states, t)
         out[t.name.decode()] = DevicePack.from_reference(
             d["quant_indices"], d["scales_f8"], d["residual_indices"], d["residual_values"],

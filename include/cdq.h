@@ -355,6 +355,28 @@ CDQ_API cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_s
                                    uint8_t* scales_f8, int64_t* residual_indices,
                                    uint16_t* residual_values);
 
+/*
+ * .cdq tile records decoded on the device. cdq_file_checkpoints (host) walks
+ * one tensor's records (a tensor of cdq_file_scan) and writes, for every span
+ * of `every` tiles, the span's byte offset from record_offset and its first
+ * residual index (ceil(n_tiles / every) entries each). cdq_file_decode_device
+ * then unpacks every span in parallel from the records copied to the device
+ * (the record_bytes bytes from record_offset) into the reference arrays
+ * (q [n_tiles][32], scales_f8 [n_tiles], ridx / rval [n_res], as
+ * cdq_file_decode writes them); *error (device int32, zeroed by the caller)
+ * becomes 1 on malformed records. Replaces the per-tile Python loop of the
+ * loader (code/cdq_loader.py:79-87) and read_cdq (code/cdq_pack.py:218-229).
+ */
+CDQ_API cdq_status cdq_file_checkpoints(const uint8_t* data, int64_t len, int32_t n_states,
+                                        const cdq_file_tensor* t, int32_t every, int64_t* byte_off,
+                                        int64_t* res_off);
+CDQ_API cdq_status cdq_file_decode_device(const uint8_t* records, int64_t record_bytes, int32_t n_states,
+                                          int64_t n_tiles, int64_t n_res, int32_t every,
+                                          const int64_t* byte_off, const int64_t* res_off, uint8_t* q,
+                                          uint8_t* scales_f8, int64_t* ridx, uint16_t* rval, int32_t* error,
+                                          void* stream);
+
+
 /* Encodes the header (magic, version, count, lattice) into out (capacity
  * cap); *written gets the byte count (8 + 52 or 8 + 32). */
 CDQ_API cdq_status cdq_file_encode_header(int32_t n_states, int32_t n_tensors, uint8_t* out,

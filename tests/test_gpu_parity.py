@@ -451,3 +451,54 @@ def test_device_ingest_golden_and_rejects_malformed(golden, golden_meta):
             ops.DevicePack.from_reference_device(torch.from_numpy(q).cuda(), torch.from_numpy(sc).cuda(),
                                                  torch.from_numpy(bad_r).cuda(),
                                                  torch.from_numpy(rv.view(np.int16)).cuda(), 32, 64, 26)
+
+
+def test_device_file_decode_matches_host(tmp_path):
+    """.cdq tile records unpacked on the GPU (256-tile spans from host
+    checkpoints) give the host decoder's arrays: the CLI golden files and a
+    written file with ragged spans, adjacent residuals and both lattices; and
+    read_device_packs on a CUDA device builds the host path's packs byte for byte."""
+    from pathlib import Path
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200 import pack_file as PF
+    gold = Path(__file__).parent / "golden"
+    files = [gold / "cli_26.cdq", gold / "cli_16.cdq"]
+    for ns in (26, 16):
+        tensors = {}
+        for i, (r, c) in enumerate([(200, 2080), (45, 96), (33, 1088)]):
+            q, sc, ri, rv = _random_reference(r, c, ns, seed=900 + i + ns)
+            tensors[f"w{i}"] = {"rows": r, "cols": c, "quant_indices": q, "scales_f8": sc,
+                                "residual_indices": ri, "residual_values": rv}
+        p = tmp_path / f"rand{ns}.cdq"
+        PF.write_cdq(p, tensors, n_states=ns)
+        files.append(p)
+    for path in files:
+        data = path.read_bytes()
+        ns, tabs = PF.scan_cdq(data)
+        for t in tabs:
+            h = PF.decode_tensor(data, ns, t)
+            d = PF.decode_tensor_device(data, ns, t, "cuda")
+            assert np.array_equal(d["quant_indices"].cpu().numpy(), h["quant_indices"])
+            assert np.array_equal(d["scales_f8"].cpu().numpy(), h["scales_f8"])
+            assert np.array_equal(d["residual_indices"].cpu().numpy(), h["residual_indices"])
+            assert np.array_equal(d["residual_values"].cpu().numpy().view(np.uint16), h["residual_values"])
+        dev = PF.read_device_packs(path, device="cuda")
+        for t in tabs:
+            h = PF.decode_tensor(data, ns, t)
+            hp = ops.DevicePack.from_reference(h["quant_indices"], h["scales_f8"], h["residual_indices"],
+                                               h["residual_values"], int(t.rows), int(t.cols), ns, device="cpu")
+            dp = dev[t.name.decode()]
+            assert torch.equal(dp.units.cpu(), hp.units) and torch.equal(dp.res_ptr.cpu(), hp.res_ptr)
+
+
+def test_device_file_decode_rejects_bad_index():
+    """A 26-state index of 26 or more in a record is refused by the device decoder."""
+    from pathlib import Path
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200 import pack_file as PF
+    data = bytearray((Path(__file__).parent / "golden" / "cli_26.cdq").read_bytes())
+    ns, tabs = PF.scan_cdq(bytes(data))
+    t = tabs[0]
+    data[t.record_offset + 2] |= 0x1F  # first index of the first tile: 31
+    with pytest.raises(L.CdqError):
+        PF.decode_tensor_device(bytes(data), ns, t, "cuda")
