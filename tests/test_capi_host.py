@@ -201,3 +201,35 @@ def test_device_ingest_argument_checks():
     assert lib.cdq_pack_from_reference_device(4, 32, 26, None, P, None, None, 0, C.byref(st), P, None) == 3
     assert lib.cdq_pack_from_reference_device(4, 32, 26, P, P, None, None, 0, C.byref(st), None, None) == 3
     assert lib.cdq_pack_from_reference_device(4, 32, 26, P, P, None, None, 5, C.byref(st), P, None) == 3
+
+
+def test_file_checkpoints_match_record_walk(L):
+    """cdq_file_checkpoints gives, for every span of tiles, the byte offset and
+    first residual index that a walk over the records finds; truncated records
+    are refused."""
+    import ctypes as C
+    from cdq_lrr_b200 import pack_file as PF
+    data = (GOLD / "cli_26.cdq").read_bytes()
+    ns, tabs = PF.scan_cdq(data)
+    buf = np.frombuffer(data, dtype=np.uint8)
+    for every in (1, 3, 256):
+        for t in tabs:
+            spans = -(-int(t.n_tiles) // every)
+            bo = np.empty(spans, np.int64)
+            ro = np.empty(spans, np.int64)
+            assert L.lib().cdq_file_checkpoints(buf.ctypes.data_as(C.c_void_p), buf.size, ns, C.byref(t), every,
+                                                bo.ctypes.data_as(C.c_void_p), ro.ctypes.data_as(C.c_void_p)) == 0
+            pos, n = 0, 0
+            for k in range(int(t.n_tiles)):
+                if k % every == 0:
+                    assert bo[k // every] == pos and ro[k // every] == n
+                tc = data[t.record_offset + pos + 1]
+                pos += 2 + 20 + (tc * 21 + 7) // 8
+                n += tc
+            assert pos == t.record_bytes and n == t.n_res
+    t = tabs[0]
+    short = buf[: t.record_offset + t.record_bytes - 1].copy()
+    bo = np.empty(int(t.n_tiles), np.int64)
+    ro = np.empty(int(t.n_tiles), np.int64)
+    assert L.lib().cdq_file_checkpoints(short.ctypes.data_as(C.c_void_p), short.size, ns, C.byref(t), 1,
+                                        bo.ctypes.data_as(C.c_void_p), ro.ctypes.data_as(C.c_void_p)) == 5
