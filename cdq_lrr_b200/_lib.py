@@ -87,6 +87,7 @@ _SIGS = {
     "cdq_file_checkpoints": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), C.c_int32, _P, _P]),
     "cdq_file_decode_device": (C.c_int, [_P, C.c_int64, C.c_int32, C.c_int64, C.c_int64, C.c_int32, _P, _P,
                                          _P, _P, _P, _P, _P, _P]),
+    "cdq_compare_stats": (C.c_int, [_P, _P, C.c_int64, C.c_int32, _P, _P, C.c_int64, _P]),
     "cdq_add_rmsnorm": (C.c_int, [_P, _P, _P, C.c_float, _P, C.c_int32, _P]),
     "cdq_attn_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                   C.c_float, _P, _P]),

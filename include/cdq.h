@@ -249,6 +249,17 @@ CDQ_API cdq_status cdq_pack_from_reference_device(int32_t rows, int32_t cols, in
                                                   cdq_packed* out, int32_t* error, void* stream);
 
 /*
+ * Quality statistics on the device (the reference's report after quantizing,
+ * code/run_any_model.py:89-110): out[0..3] (device float64) = sum (a-b)^2,
+ * sum a*b, sum a^2, sum b^2 over n values of a and b (dtype 0: bf16 bits,
+ * 1: float32), from which the caller forms MSE and cosine (weights vs w_hat,
+ * or baseline vs quantized logits). workspace: >= 32 KiB of device memory for
+ * the block partial sums, added in block order (deterministic).
+ */
+CDQ_API cdq_status cdq_compare_stats(const void* a, const void* b, int64_t n, int32_t dtype, double* out,
+                                     double* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Batch-1 decode-step kernels around the fused linear, for a Qwen2-style
  * decoder layer (the reference runs HF's Qwen2 modules around CDQLinear,
  * code/cdq_lrr_qwen05.py:300-330; these replace Qwen2RMSNorm, the rotary

@@ -233,3 +233,13 @@ def test_file_checkpoints_match_record_walk(L):
     ro = np.empty(int(t.n_tiles), np.int64)
     assert L.lib().cdq_file_checkpoints(short.ctypes.data_as(C.c_void_p), short.size, ns, C.byref(t), 1,
                                         bo.ctypes.data_as(C.c_void_p), ro.ctypes.data_as(C.c_void_p)) == 5
+
+
+def test_compare_stats_argument_checks(L):
+    """The quality reduction rejects bad arguments before any device work."""
+    import ctypes as C
+    P = C.c_void_p(64)
+    assert L.lib().cdq_compare_stats(None, P, 10, 0, P, P, 1 << 20, None) == 3
+    assert L.lib().cdq_compare_stats(P, P, 10, 2, P, P, 1 << 20, None) == 3
+    assert L.lib().cdq_compare_stats(P, P, 0, 0, P, P, 1 << 20, None) == 3
+    assert L.lib().cdq_compare_stats(P, P, 10, 0, P, P, 1024, None) == 7

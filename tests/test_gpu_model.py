@@ -218,3 +218,31 @@ def test_fused_decode_full_model(cdq_model):
     cos = torch.nn.functional.cosine_similarity(fd.logits.float(), ref, dim=-1).item()
     assert cos >= 0.998, cos
     assert L.kernel_error() == 0
+
+
+def test_quality_report_matches_torch():
+    """The on-device quality sums against torch float64 (bf16 and float32
+    inputs), bit-identical on repeat, and the quantize-and-report loop over a
+    one-layer model against torch's MSE / cosine of each weight and its w_hat."""
+    from cdq_lrr_b200 import decode, ops, quality
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for dt in (torch.bfloat16, torch.float32):
+        a = torch.randn(1_000_003, generator=g, device="cuda").to(dt)
+        b = (a.float() + 0.01 * torch.randn(a.numel(), generator=g, device="cuda")).to(dt)
+        r = quality.compare(a, b)
+        a64, b64 = a.double(), b.double()
+        mse = (a64 - b64).pow(2).mean().item()
+        cos = (a64 @ b64 / (a64.norm() * b64.norm())).item()
+        assert abs(r["mse"] - mse) <= 1e-9 * mse and abs(r["cos"] - cos) <= 1e-12
+        assert quality.compare(a, b) == r
+    m = decode.build_model(seed=0, device="cuda", layers=1)
+    orig = {n: mod.weight.detach().clone() for n, mod in m.named_modules() if isinstance(mod, nn.Linear)}
+    rep = quality.quantize_with_report(m)
+    assert rep["linears"] == 7 and 0.99 < rep["weight_cos"] <= 1.0
+    for name, r in rep["per_linear"].items():
+        w = orig[name].double().reshape(-1)
+        wh = ops.dequant(m.get_submodule(name).device_pack).double().reshape(-1)
+        assert abs(r["cos"] - (w @ wh / (w.norm() * wh.norm())).item()) <= 1e-10
+        assert abs(r["mse"] - (w - wh).pow(2).mean().item()) <= 1e-9 * max(r["mse"], 1e-30)
+    lr = quality.logit_report(torch.ones(4, 8, device="cuda"), torch.ones(4, 8, device="cuda"))
+    assert lr["logits_mse"] == 0.0 and abs(lr["logits_cos"] - 1.0) < 1e-12
