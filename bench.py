@@ -284,6 +284,14 @@ def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
     r = decode.fused_greedy_decode(model, ids, new_tokens)
     decode.greedy_decode(model, ids, 8)
     h = decode.greedy_decode(model, ids, new_tokens)
+    # the 16-state draft tier (README's draft/verify tiers): same model, 16-state packs
+    from cdq_lrr_b200.quant import CAMKII_LATTICE_16
+    del model
+    torch.cuda.empty_cache()
+    model = decode.build_model(seed=0, device="cuda")
+    decode.patch_cdq(model, lattice=CAMKII_LATTICE_16)
+    decode.fused_greedy_decode(model, ids, 8)
+    d16 = decode.fused_greedy_decode(model, ids, new_tokens)
     out = {"tokens_per_s": round(r["tokens_per_s"], 2),
            "ms_per_token": round(r["decode_ms_per_token"], 4),
            "prefill_ms": round(r["prefill_ms"], 3), "prompt_tokens": prompt_len,
@@ -292,6 +300,7 @@ def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
                    "kernels around grouped CDQ projections; torch embedding, lm_head GEMV, argmax), "
                    "token and position advanced on the device, one CUDA graph per token",
            "hf_step_tokens_per_s": round(h["tokens_per_s"], 2),
+           "draft_tier_16_state_tokens_per_s": round(d16["tokens_per_s"], 2),
            "hf_step": "the same model through HF's Qwen2 forward (CDQ projections patched in), CUDA graph",
            "model": "Qwen2.5-0.5B architecture, random init, 168 CDQ-26 projections, bf16 tied lm_head",
            "timing": "CUDA events around the decode loop (device time incl. host launch gaps)"}
