@@ -132,11 +132,6 @@ __device__ __forceinline__ uint4 ldg_x4(const uint16_t* p) {
                  : "l"(p));
     return v;
 }
-__device__ __forceinline__ uint32_t ldg_stream(const void* p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
 
 __device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
     uint32_t d;
