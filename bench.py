@@ -316,8 +316,8 @@ def run_ours(args) -> None:
     from cdq_lrr_b200.synth import synth_activation, synth_weight
 
     ws_, rank, local = dist_setup(args.gpus)
-    kernel_name = ("gemv_kernel<26,1,192> (bulk-copy quad ring + mma.sync) then fixup_kernel<1,192>; "
-                   "one grouped launch pair per step")
+    kernel_name = ("res_sum_kernel<192> (residual pre-pass) then stream_kernel<26,1,192> (bulk-copy quad "
+                   "ring + mma.sync, group sums finished in the kernel); one grouped call = two launches per step")
     dev = torch.device("cuda", torch.cuda.current_device())
 
     # weights: generated and quantised on the GPU, one at a time

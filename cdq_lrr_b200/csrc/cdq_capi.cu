@@ -75,10 +75,13 @@ cdq_status fill_job(const cdq_packed* w, const uint16_t* x, int64_t m, void* y, 
     J->reserved_ptr = nullptr;
     J->rb_begin = 0;
     J->reserved0 = 0;
-    // the per-group partial sums of the streaming pass live in the caller's workspace
+    // the caller's workspace: the row-block arrival counters, then the
+    // streaming path's per-group sums or the tile path's prepared activations
     const int64_t need = linear_workspace_need(g, m);
     if (!ws || (int64_t)ws_bytes < need || !aligned(ws, 256)) return CDQ_ERR_WORKSPACE;
-    J->partial = reinterpret_cast<float*>(ws);
+    J->counters = reinterpret_cast<uint32_t*>(ws);
+    J->partial = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + gemv_counter_bytes(g));
+    J->unit_begin = 0;
     return CDQ_OK;
 }
 

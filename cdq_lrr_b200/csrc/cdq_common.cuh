@@ -144,23 +144,31 @@ CDQ_HD Geometry geometry(int64_t rows, int64_t cols, int n_states) {
     return g;
 }
 
-// Workspace of one fused-linear call with batch m (bytes). The streaming path
-// keeps float32 sums per (batch row, residual group, padded row); the tcgen05
-// tile path keeps the call's prepared activations: the B-operand stages of
-// every quad (batch padded to N = 16, 32 or 64, 512 bytes per batch row per
-// quad) and x^T (64 * kp columns x the batch padded to 8, bf16).
+// Workspace of one fused-linear call with batch m (bytes). It starts with one
+// uint32 arrival counter per row block (the streaming kernel's split-K
+// hand-off; zero before the first call, every call leaves them zero), then
+// the path's own data: the streaming path's float32 sums per (batch row,
+// residual group, padded row), or the tcgen05 tile path's prepared
+// activations: the B-operand stages of every quad (batch padded to N = 16, 32
+// or 64, 512 bytes per batch row per quad) and x^T (64 * kp columns x the
+// batch padded to 8, bf16).
 CDQ_HD int64_t ws_align256(int64_t b) { return (b + 255) / 256 * 256; }
 CDQ_HD int tile_nb(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
 CDQ_HD int64_t tile_xperm_bytes(const Geometry& g, int64_t m) { return (g.kp + 3) / 4 * tile_nb(m) * 512; }
 CDQ_HD int64_t tile_prep_bytes(const Geometry& g, int64_t m) {
     return ws_align256(tile_xperm_bytes(g, m)) + ws_align256(g.kp * 64 * ((m + 7) / 8 * 8) * 2);
 }
-CDQ_HD int64_t gemv_partial_bytes(const Geometry& g, int64_t m) {
+CDQ_HD int64_t gemv_counter_bytes(const Geometry& g) { return ws_align256(g.r16 * 4); }
+CDQ_HD int64_t gemv_sums_bytes(const Geometry& g, int64_t m) {
     return ws_align256(m * g.kg * g.r16 * 16 * 4);
 }
+// the streaming path alone (counters + sums)
+CDQ_HD int64_t gemv_partial_bytes(const Geometry& g, int64_t m) {
+    return gemv_counter_bytes(g) + gemv_sums_bytes(g, m);
+}
 CDQ_HD int64_t linear_workspace_need(const Geometry& g, int64_t m) {
-    const int64_t a = gemv_partial_bytes(g, m), b = tile_prep_bytes(g, m);
-    return a > b ? a : b;
+    const int64_t a = gemv_sums_bytes(g, m), b = tile_prep_bytes(g, m);
+    return gemv_counter_bytes(g) + (a > b ? a : b);
 }
 
 // Quad holding unit (b16, cp): byte offset of the quad, its unit count u and

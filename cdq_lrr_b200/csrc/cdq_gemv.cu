@@ -1,22 +1,19 @@
-// Fused dequant linear for the CDQ-LRR device pack: the streaming pass (batch
-// M <= 64, n-tiles of 8 above 8), the fix-up pass and the launchers of both
-// paths.
+// Fused dequant linear for the CDQ-LRR device pack: the shared decode pieces
+// (bulk-copy ring, pair tables, unit decode into mma.sync), the wide streaming
+// pass for batches 9 to 64 and its fix-up pass, and the launchers of every
+// path (batches up to 8: cdq_stream.cuh; tcgen05 tile path: cdq_tile.cuh).
 //
 // y[m, row] = sum_col w_hat[row, col] * x[m, col] (+ bias[row]) where
 // w_hat = bf16(LATTICE[q] * sigma) is rebuilt in registers from the packed
 // tiles and never written to memory (the reference materialises w_hat and
 // calls F.linear: code/cdq_lrr_qwen05.py:188-198, code/cdq_loader.py:53-58).
 //
-// Work decomposition. A work item is (job, 16-row block, residual group of
-// up to 32 tile columns = 16 units = 4 quads). Items of every job of a launch
-// are dealt round-robin to the warps of the grid (grouped launch).
-//
-// Memory pipeline. Each warp streams its items' quads (2688 or 2176
-// contiguous bytes; the last quad of a row block may be shorter) into a
-// private two-slot ring in shared memory with bulk copies (cp.async.bulk,
-// completion counted on one mbarrier per slot), so two quads are in flight
-// per warp while it decodes the previous one; lane 0 issues the copy of the
-// warp's next quad, across item boundaries, as soon as a slot is consumed.
+// Memory pipeline (both streaming kernels). Each warp streams its quads
+// (2688 or 2176 contiguous bytes; the last quad of a row block may be
+// shorter) into a private two-slot ring in shared memory with bulk copies
+// (cp.async.bulk, completion counted on one mbarrier per slot), so two quads
+// are in flight per warp while it decodes the previous one; lane 0 issues the
+// copy of the warp's next quad as soon as a slot is consumed.
 //
 // Dequantisation. Lane l = 4g + c reads from the slot exactly the 16 pair
 // codes of its m16n8k16 A fragments (rows g and g+8 of the block over 16
@@ -27,19 +24,14 @@
 // single rounding of the exact product, as torch's bf16 multiply), which is
 // the A operand of a tensor-core mma (bf16 inputs, fp32 accumulators); the
 // activations form the B operand (batch = the mma's N dimension). Residual
-// positions carry the zero symbol; their bf16 values are added by the fix-up
-// pass from the CSR buckets of each row.
+// positions carry the zero symbol; their bf16 values enter through the
+// residual pre-pass (cdq_stream.cuh), whose per-group sums are added to the
+// mma sums group by group.
 //
-// Two passes. The streaming pass writes each item's fp32 sums to a per-group
-// slot of the workspace (no residuals, fences or atomics on its path); the
-// fix-up pass adds, per output, the group slots in group order, the row's
-// residual entries (bf16 value x activation in fp32) and the bias, and
-// rounds once. Both passes are deterministic. In a launch with at most one
-// item per warp (the projections of a decode step), the streaming warp itself
-// finishes the rows of single-group jobs with the same arithmetic in the same
-// order, and the fix-up pass runs only for the multi-group jobs. Batches of
-// 16 and more go to the tcgen05 tile path (cdq_tile.cuh) when the launch has
-// enough 128-row tiles.
+// Arithmetic of one output (every streaming path, any batch, any grouping):
+//     y = sum over the row's residual groups, in group order and starting
+//         from zero, of (mma sum of the group + residual sum of the group),
+//         + bias, rounded once.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -89,9 +81,7 @@ constexpr uint32_t kSpinLimit = 1u << 22; // mbarrier polls before a wait gives 
 //                       (binary-search keys), the scale table (fp8 code b ->
 //                       (sigma, sigma) at 4b) and one mbarrier per (warp, slot)
 //   [128K, ...)         rings of warps kLowWarps .. kWarps-1
-// A ring is kSlots slots; a slot holds one quad (its units' bytes as stored)
-// followed, for batch M <= kXSlotBatch, by the quad's activation columns of
-// every batch row (128 bytes per unit per row).
+// A ring is kSlots slots; a slot holds one quad (its units' bytes as stored).
 constexpr uint32_t kLowStage = 1024;
 constexpr int kLowWarps = 4;
 constexpr uint32_t kLat26Xor = 0x300u << 7;
@@ -100,27 +90,22 @@ constexpr uint32_t kBeginAddr = 61u << 10;
 constexpr uint32_t kSigAddr = 62u << 10;
 constexpr uint32_t kBarAddr = 63u << 10;
 constexpr uint32_t kHighStage = 128u << 10;
-constexpr int kXSlotBatch = 2;
 
-template <int NS, int M>
+template <int NS>
 struct SlotTraits {
     static constexpr uint32_t kQuadBytes = 4 * PackTraits<NS>::kUnit;
-    static constexpr bool kX = M <= kXSlotBatch;
-    static constexpr uint32_t kSlot = kQuadBytes + (kX ? M * 512 : 0);
-    static constexpr uint32_t kRing = kSlots * kSlot;
+    static constexpr uint32_t kRing = kSlots * kQuadBytes;
     static constexpr uint32_t kTop = kHighStage + (kWarps - kLowWarps) * kRing;
 };
-static_assert(kLowStage + kLowWarps * SlotTraits<26, kXSlotBatch>::kRing <= (32u << 10),
-              "low rings overlap the table");
-static_assert(SlotTraits<26, kXSlotBatch>::kTop <= 232448 && SlotTraits<26, 8>::kTop <= 232448,
-              "rings exceed the window");
+static_assert(kLowStage + kLowWarps * SlotTraits<26>::kRing <= (32u << 10), "low rings overlap the table");
+static_assert(SlotTraits<26>::kTop <= 232448, "rings exceed the window");
 static_assert(kBeginAddr >= (473u << 7) && kBeginAddr + 4 * kMaxJobs <= kSigAddr &&
                   kSigAddr + 1024 <= kBarAddr && kBarAddr + kWarps * kSlots * 8 <= (512u << 7),
               "keys, scale table and barriers must sit in the 26-state table's unused entries 473..511");
 
-template <int NS, int M>
+template <int NS>
 __device__ __forceinline__ uint32_t slot_base(int warp) {
-    constexpr uint32_t kRing = SlotTraits<NS, M>::kRing;
+    constexpr uint32_t kRing = SlotTraits<NS>::kRing;
     return warp < kLowWarps ? kLowStage + warp * kRing : kHighStage + (warp - kLowWarps) * kRing;
 }
 
@@ -362,11 +347,18 @@ __device__ __forceinline__ ItemInfo item_info(const GemvBatch<MAXJ>& batch, int6
     return I;
 }
 
+// The wide streaming pass (batches 9 to 64): each unit is decoded once into
+// w_hat pair registers that multiply NT n-tiles of 8 batch rows (activations
+// from the L1 cache). Items are (job, 16-row block, residual group), dealt
+// round-robin to the warps of the grid; each item's sums, added over the
+// group's residual sums from the pre-pass, are written to the workspace and
+// the fix-up pass adds the groups.
 template <int NS, int M, int MAXJ>
 __global__ void __launch_bounds__(kThreads, 1)
-gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+wide_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    static_assert(M > 8, "batches up to 8 take the stream kernel");
     using Tr = PackTraits<NS>;
-    using Sl = SlotTraits<NS, M>;
+    using Sl = SlotTraits<NS>;
     constexpr uint32_t kU = Tr::kUnit;
     constexpr uint32_t kQuad = Sl::kQuadBytes;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -401,7 +393,7 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             if (lane == 0) *reinterpret_cast<int32_t*>(base + kBeginAddr + 4 * i) = v;
         }
     }
-    const uint32_t ring = slot_base<NS, M>(warp);
+    const uint32_t ring = slot_base<NS>(warp);
     const uint32_t bars = kBarAddr + warp * kSlots * 8;
     if (lane == 0) {
         for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
@@ -414,18 +406,14 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     const int64_t total = batch.total_items;
     const int64_t stride = (int64_t)gridDim.x * kWarps;
     const int64_t first = (int64_t)blockIdx.x * kWarps + warp;
-    // lanes of batch columns >= M read row 0: their mma output columns are
-    // never stored, so any finite or non-finite value there is harmless
-    const int xrow = g < M ? g : 0;
-    constexpr int NT = (M + 7) / 8;             // n-tiles of 8 batch rows
-    const int m_rt = M <= 8 ? M : batch.m;      // batch rows of this launch
+    constexpr int NT = (M + 7) / 8;  // n-tiles of 8 batch rows
+    const int m_rt = batch.m;        // batch rows of this launch
 
     // Producer cursor (lane 0 issues; every lane keeps the same values): the
     // next quad of this warp's stream of items.
     int64_t p_item = first;
-    int p_q = 0, p_nq = 0, p_units = 0, p_cols = 0, p_xleft = 0;
+    int p_q = 0, p_nq = 0, p_units = 0;
     const uint8_t* p_base = nullptr;
-    const uint16_t* p_x = nullptr;
     uint32_t p_slot = 0;
     auto p_load = [&]() {
         if (p_item < total) {
@@ -435,9 +423,6 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             p_units = I.n_units;
             p_nq = (I.n_units + 3) >> 2;
             p_q = 0;
-            p_x = J.x + 64 * I.cp0;
-            p_cols = J.cols;
-            p_xleft = 2 * (J.cols - 64 * I.cp0);  // activation bytes of a row from the item's first column
         }
     };
     auto produce = [&]() {
@@ -446,19 +431,9 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const int u = left < 4 ? left : 4;
         const uint32_t bytes = (uint32_t)u * kU;
         if (lane == 0) {
-            const uint32_t slot = ring + p_slot * Sl::kSlot, bar = bars + 8 * p_slot;
-            if constexpr (Sl::kX) {
-                // the quad's activation columns, cut at the row's end (a phantom tile)
-                const int xb = min(128 * u, p_xleft - 512 * p_q);
-                slot_arm(bar, bytes + (uint32_t)(M * xb));
-                bulk_copy(slot, p_base + (int64_t)p_q * kQuad, bytes, bar);
-#pragma unroll
-                for (int m = 0; m < M; ++m)
-                    bulk_copy(slot + kQuad + 512 * m, p_x + (int64_t)m * p_cols + 256 * p_q, (uint32_t)xb, bar);
-            } else {
-                slot_arm(bar, bytes);
-                bulk_copy(slot, p_base + (int64_t)p_q * kQuad, bytes, bar);
-            }
+            const uint32_t bar = bars + 8 * p_slot;
+            slot_arm(bar, bytes);
+            bulk_copy(ring + p_slot * kQuad, p_base + (int64_t)p_q * kQuad, bytes, bar);
         }
         p_slot ^= 1u;
         if (++p_q == p_nq) {
@@ -478,195 +453,65 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const int n_units = I.n_units, nq = (n_units + 3) >> 2;
         // a phantom second tile (odd tile count) sits in the row's last unit
         const int phantom_u = (J.kt & 1) && I.cp0 + n_units == J.kp ? n_units - 1 : -1;
-        const bool phantom_item = phantom_u >= 0;
-        const uint16_t* xp = J.x + (int64_t)xrow * J.cols + 64 * I.cp0 + 16 * c;
-        const uint16_t* xw = J.x + 64 * I.cp0 + 16 * c;  // batch row 0 (wide batches)
+        const uint16_t* xw = J.x + 64 * I.cp0 + 16 * c;  // batch row 0
         float d[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
-        // A job of one residual group (every row's K in this item), in a launch
-        // small enough that the fix-up launch would cost more than the rows'
-        // residual tail stalls this warp: the warp finishes its 16 rows itself,
-        // with the fix-up pass's arithmetic in the fix-up pass's order. Lane
-        // (row rr, half rh) reads the row's residual bounds now and warms L2
-        // with its entries after the first quad.
-        const bool direct = NT == 1 && J.kg == 1 && batch.finish_single;
-        const int rr = I.b16 * 16 + (lane >> 1), rh = lane & 1;
-        uint32_t reb = 0, ree = 0;
-        if (direct) {
-            reb = __ldg(J.res_ptr + rr) + rh;
-            ree = min(__ldg(J.res_ptr + rr + 1), J.n_res);
-        }
-        // unit i of quad q: the narrow path (one n-tile) or the wide one
-        auto run_unit = [&](const uint4& A, uint32_t w4, uint32_t sw, bool hi_half, const uint4& xa,
-                            const uint4& xb, int unit) {
-            if constexpr (NT == 1) {
-                if (hi_half) unit_mma<NS, 16>(A, w4, sw, xa, xb, lane_base, sig_base, d[0]);
-                else unit_mma<NS, 0>(A, w4, sw, xa, xb, lane_base, sig_base, d[0]);
-            } else {
-                const bool zx = unit == phantom_u && c >= 2;
-                if (hi_half) unit_mma_wide<NS, 16, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
-                else unit_mma_wide<NS, 0, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
-            }
+        // unit i of quad q (the phantom tile's lanes take zero activations)
+        auto run_unit = [&](const uint4& A, uint32_t w4, uint32_t sw, bool hi_half, int unit) {
+            const bool zx = unit == phantom_u && c >= 2;
+            if (hi_half) unit_mma_wide<NS, 16, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
+            else unit_mma_wide<NS, 0, NT>(A, w4, sw, xw + 64 * unit, J.cols, g, m_rt, zx, lane_base, sig_base, d);
         };
         for (int q = 0; q < nq; ++q) {
             if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
                 failed = true;
                 break;
             }
-            const uint32_t slot = ring + c_slot * Sl::kSlot;
+            const uint32_t slot = ring + c_slot * kQuad;
             const int uq = min(4, n_units - 4 * q);
-            const uint16_t* xq = xp + 256 * q;
-            if (uq == 4 && !phantom_item) {
-                // a full quad without a phantom tile: no per-unit checks
-                uint4 A[4], X[4][2];
+            uint4 A[4];
+            uint4 W;
+            uint2 S;
+            if (uq == 4) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                const uint4 W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
-                const uint2 S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
-                uint32_t dep = W.x ^ S.x;
-                if constexpr (Sl::kX) {
-                    const uint32_t xa = slot + kQuad + 512 * xrow + 32 * c;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        X[i][0] = lds_slot4(xa + 128 * i);
-                        X[i][1] = lds_slot4(xa + 128 * i + 16);
-                        dep ^= X[i][0].x ^ X[i][1].x;
-                    }
-                }
-                // one register of every slot read: each read has landed before the slot is reused
-                dep ^= A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
-                asm volatile("" ::"r"(dep));
-                __syncwarp();
-                produce();
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
-                    if constexpr (Sl::kX) {
-                        xa = X[i][0];
-                        xb = X[i][1];
-                    } else if constexpr (NT == 1) {
-                        xa = ldg_x4(xq + 64 * i);
-                        xb = ldg_x4(xq + 64 * i + 8);
-                    }
-                    const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
-                    run_unit(A[i], w4, i < 2 ? S.x : S.y, (i & 1) != 0, xa, xb, 4 * q + i);
-                }
+                W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
             } else {
-                // a short last quad (1..3 units, compact) or the quad holding a phantom tile
-                uint4 A[4], X[4][2];
-                uint4 W;
-                uint2 S;
-                if (uq == 4) {
+                // a short last quad (1..3 units, compact)
+                uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                    W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
-                    S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
-                } else {
-                    uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) {
-                        A[i] = make_uint4(0u, 0u, 0u, 0u);
-                        if (i < uq) {
-                            A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                            if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
-                            h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
-                        }
-                    }
-                    A[3] = make_uint4(0u, 0u, 0u, 0u);
-                    W = make_uint4(w4[0], w4[1], w4[2], 0u);
-                    S = make_uint2(h[0] | (h[1] << 16), h[2]);
-                }
-                uint32_t dep = W.x ^ W.y ^ W.z ^ S.x ^ S.y;
-                if constexpr (Sl::kX) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        X[i][0] = make_uint4(0u, 0u, 0u, 0u);
-                        X[i][1] = X[i][0];
-                        // the phantom tile's lanes (c >= 2) keep zeros: that part of the slot is stale
-                        if (i < uq && (4 * q + i != phantom_u || c < 2)) {
-                            const uint32_t xa = slot + kQuad + 512 * xrow + 128 * i + 32 * c;
-                            X[i][0] = lds_slot4(xa);
-                            X[i][1] = lds_slot4(xa + 16);
-                        }
-                        dep ^= X[i][0].x ^ X[i][1].x;
-                    }
-                }
-                dep ^= A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
-                asm volatile("" ::"r"(dep));
-                __syncwarp();
-                produce();
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < 3; ++i) {
+                    A[i] = make_uint4(0u, 0u, 0u, 0u);
                     if (i < uq) {
-                        uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
-                        if constexpr (Sl::kX) {
-                            xa = X[i][0];
-                            xb = X[i][1];
-                        } else if constexpr (NT == 1) {
-                            load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
-                        }
-                        const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
-                        run_unit(A[i], w4, i < 2 ? S.x : S.y, (i & 1) != 0, xa, xb, 4 * q + i);
+                        A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                        if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
+                        h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
                     }
+                }
+                A[3] = make_uint4(0u, 0u, 0u, 0u);
+                W = make_uint4(w4[0], w4[1], w4[2], 0u);
+                S = make_uint2(h[0] | (h[1] << 16), h[2]);
+            }
+            // one register of every slot read: each read has landed before the slot is reused
+            uint32_t dep = W.x ^ W.y ^ W.z ^ S.x ^ S.y ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+            asm volatile("" ::"r"(dep));
+            __syncwarp();
+            produce();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (i < uq) {
+                    const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
+                    run_unit(A[i], w4, i < 2 ? S.x : S.y, (i & 1) != 0, 4 * q + i);
                 }
             }
             c_slot ^= 1u;
             c_phase ^= c_slot == 0 ? 1u : 0u;
-            if (direct && q == 0 && reb < ree) {
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(J.res_ent + reb));
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(J.res_ent + ree - 1));
-            }
         }
         if (failed) break;
-        if constexpr (NT == 1) {
-            if (direct) {
-                // y = (this group's sum) + (the row's residual entries, bf16 value x
-                // activation in fp32, entry order, split over the lane pair) + bias
-                float acc[M];
-#pragma unroll
-                for (int n = 0; n < M; ++n) acc[n] = 0.f;
-                for (uint32_t e0 = reb; e0 < ree; e0 += 16) {
-                    uint32_t en[8];
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) en[t] = e0 + 2 * t < ree ? __ldg(J.res_ent + e0 + 2 * t) : 0u;
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        const uint32_t col = en[t] >> 16;
-                        if (e0 + 2 * t < ree && col < (uint32_t)J.cols) {
-                            const float v = __uint_as_float(en[t] << 16);
-#pragma unroll
-                            for (int n = 0; n < M; ++n)
-                                acc[n] = fmaf(v, bf16_to_f32(__ldg(J.x + (int64_t)n * J.cols + col)), acc[n]);
-                        }
-                    }
-                }
-                float R[4] = {0.f, 0.f, 0.f, 0.f};  // (row g, 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
-#pragma unroll
-                for (int n = 0; n < M; ++n) {
-                    acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
-                    const float a = __shfl_sync(0xFFFFFFFFu, acc[n], 2 * g);
-                    const float b = __shfl_sync(0xFFFFFFFFu, acc[n], 2 * g + 16);
-                    if (n == 2 * c) {
-                        R[0] = a;
-                        R[2] = b;
-                    }
-                    if (n == 2 * c + 1) {
-                        R[1] = a;
-                        R[3] = b;
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = I.b16 * 16 + g + 8 * h;
-#pragma unroll
-                    for (int j = 0; j < 2; ++j)
-                        if (row < J.rows && 2 * c + j < M) store_out(J, 2 * c + j, row, d[0][2 * h + j] + R[2 * h + j]);
-                }
-                continue;
-            }
-        }
-        // this group's partial sums of rows g and g + 8 (batch columns 8t + 2c, 8t + 2c + 1)
+        // this group's sums of rows g and g + 8 (batch columns 8t + 2c, 8t + 2c + 1),
+        // added over the group's residual sums from the pre-pass: the group's value
         const int64_t rpad = (int64_t)J.r16 * 16;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -674,8 +519,14 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int64_t row = I.b16 * 16 + g + 8 * h;
-                if (n0 < m_rt) J.partial[((int64_t)n0 * J.kg + I.grp) * rpad + row] = d[t][2 * h];
-                if (n0 + 1 < m_rt) J.partial[((int64_t)(n0 + 1) * J.kg + I.grp) * rpad + row] = d[t][2 * h + 1];
+                if (n0 < m_rt) {
+                    float* p = J.partial + ((int64_t)n0 * J.kg + I.grp) * rpad + row;
+                    *p = d[t][2 * h] + __ldcg(p);
+                }
+                if (n0 + 1 < m_rt) {
+                    float* p = J.partial + ((int64_t)(n0 + 1) * J.kg + I.grp) * rpad + row;
+                    *p = d[t][2 * h + 1] + __ldcg(p);
+                }
             }
         }
     }
@@ -691,18 +542,16 @@ gemv_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     }
 }
 
-// Fix-up pass: y[m, row] = sum over groups (in group order) of the partial
-// sums + the residual entries of the row (bf16 value x activation, fp32) +
-// bias, rounded once to bf16 (or stored as float32). One warp per (job,
-// 16-row block); lane l = 2 * (row in block) + half, the two halves of a row
-// taking alternate residual entries and meeting in one shuffle. Grid row y
-// is job y; the job's fields are uniform reads of the launch record.
+// Fix-up pass of the wide (batch > 8) streaming kernel: y[m, row] = sum over
+// the row's residual groups, in group order and starting from zero, of the
+// group's value (its mma sum plus its residual sum from the pre-pass), + bias,
+// rounded once to bf16 (or stored as float32): the arithmetic of the batch
+// <= 8 kernel, so a row's result does not depend on the batch it is computed
+// in. One thread per (job, padded row, batch row); grid row y is job y.
 constexpr int kFixThreads = 256;
-constexpr int kFixGroups = 4;  // residual groups whose bucket bounds are fetched together
 
-template <int M, int MAXJ>
-__global__ void __launch_bounds__(kFixThreads, M == 1 ? 8 : 2)
-fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+template <int MAXJ>
+__global__ void __launch_bounds__(kFixThreads) fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     // block -> job: rb_begin holds each job's first block (uniform search of the launch record)
     int j = 0;
     if constexpr (MAXJ > 1) {
@@ -714,120 +563,39 @@ fixup_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         j = lo;
     }
     const GemvJob& J = batch.jobs[j];
-    const int b16 = ((int)blockIdx.x - J.rb_begin) * (kFixThreads / 32) + (int)(threadIdx.x >> 5);
-    if (b16 >= J.r16) return;
-    const uint32_t* const res_ptr = J.res_ptr;
-    const uint32_t* const res_ent = J.res_ent;
-    const uint16_t* const x = J.x;
-    const float* const partial = J.partial;
-    const int kg = J.kg, cols = J.cols, rows = J.rows;
-    const uint32_t n_res = J.n_res;
     const int64_t rpad = (int64_t)J.r16 * 16;
-    const int lane = threadIdx.x & 31, ri = lane >> 1, half = lane & 1;
-    const int row = b16 * 16 + ri;
-    const bool live = row < rows;
-    // batch rows in chunks of M (one chunk unless the launch is wider than 8)
-    const int m_total = M < 8 ? M : batch.m;
-    constexpr int kMH = (M + 1) / 2;
-    for (int n0 = 0; n0 < m_total; n0 += M) {
-        const int mc = min(M, m_total - n0);  // rows of this chunk
-        const uint16_t* const xc = x + (int64_t)n0 * cols;
-        const float* const pc = partial + (int64_t)n0 * kg * rpad;
-        // the group partial sums do not depend on the residuals: fetch them first
-        // (half 0 holds even batch columns of the chunk, half 1 odd ones)
-        float psum[kMH];
-#pragma unroll
-        for (int k = 0; k < kMH; ++k) psum[k] = 0.f;
-        float acc[M];
-#pragma unroll
-        for (int n = 0; n < M; ++n) acc[n] = 0.f;
-        auto add_entries = [&](uint32_t eb, uint32_t ee) {
-            constexpr int kBatch = M <= 2 ? 8 : 4;  // entries of this half in flight at once
-            for (uint32_t e0 = eb; e0 < ee; e0 += 2 * kBatch) {
-                uint32_t en[kBatch];
-#pragma unroll
-                for (int t = 0; t < kBatch; ++t) en[t] = e0 + 2 * t < ee ? __ldg(res_ent + e0 + 2 * t) : 0u;
-#pragma unroll
-                for (int t = 0; t < kBatch; ++t) {
-                    const uint32_t col = en[t] >> 16;
-                    if (e0 + 2 * t < ee && col < (uint32_t)cols) {
-                        const float v = __uint_as_float(en[t] << 16);
-#pragma unroll
-                        for (int n = 0; n < M; ++n)
-                            if (n < mc) acc[n] = fmaf(v, bf16_to_f32(__ldg(xc + (int64_t)n * cols + col)), acc[n]);
-                    }
-                }
-            }
-        };
-        // the row's residual bounds (its buckets are consecutive: one range)
-        const uint32_t reb = __ldg(res_ptr + (int64_t)row * kg) + half;
-        const uint32_t ree = min(__ldg(res_ptr + (int64_t)(row + 1) * kg), n_res);
-        for (int g0 = 0; g0 < kg; g0 += kFixGroups) {
-            float pv[kMH][kFixGroups];
-#pragma unroll
-            for (int k = 0; k < kFixGroups; ++k) {
-#pragma unroll
-                for (int t = 0; t < kMH; ++t) {
-                    const int n = 2 * t + half;
-                    pv[t][k] = n < mc && live && g0 + k < kg
-                                   ? __ldcg(pc + ((int64_t)n * kg + g0 + k) * rpad + row)
-                                   : 0.f;
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kFixGroups; ++k)
-#pragma unroll
-                for (int t = 0; t < kMH; ++t) psum[t] += pv[t][k];  // group order
-        }
-        add_entries(reb, ree);
-#pragma unroll
-        for (int n = 0; n < M; ++n) acc[n] += __shfl_xor_sync(0xFFFFFFFFu, acc[n], 1);
-        if (live) {
-#pragma unroll
-            for (int t = 0; t < kMH; ++t) {
-                const int n = 2 * t + half;
-                if (n < mc) store_out(J, n0 + n, row, psum[t] + acc[n]);
-            }
-        }
-    }
+    const int64_t i = ((int64_t)blockIdx.x - J.rb_begin) * kFixThreads + threadIdx.x;
+    if (i >= rpad * batch.m) return;
+    const int n = (int)(i / rpad), row = (int)(i - n * rpad);
+    if (row >= J.rows) return;
+    const int kg = J.kg;
+    const float* p = J.partial + (int64_t)n * kg * rpad + row;
+    float s = 0.f;
+    for (int k = 0; k < kg; ++k) s += __ldcg(p + (int64_t)k * rpad);
+    store_out(J, n, row, s);
 }
 
 #include "cdq_tile.cuh"
+#include "cdq_stream.cuh"
 
-// The fix-up pass over every job's row blocks (kFixThreads / 32 per block, jobs
-// back to back); batches above 8 are fixed up in chunks of 8 batch rows.
-// single_done: the streaming pass finished the jobs of one residual group
-// (batch <= 8), which the fix-up pass then leaves out (no launch if none is left).
+// The fix-up pass over every job (one thread per padded row and batch row).
 template <int MAXJ>
-cudaError_t launch_fixup(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream, bool single_done = false) {
+cudaError_t launch_fixup(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream) {
     GemvBatch<MAXJ> fb = b;
-    int blocks = 0, n = 0;
+    int64_t blocks = 0;
     for (int j = 0; j < b.n; ++j) {
-        if (single_done && b.jobs[j].kg == 1) continue;
-        fb.jobs[n] = b.jobs[j];
-        fb.jobs[n].rb_begin = blocks;
-        blocks += (b.jobs[j].r16 + kFixThreads / 32 - 1) / (kFixThreads / 32);
-        ++n;
+        fb.jobs[j].rb_begin = (int32_t)blocks;
+        blocks += ((int64_t)b.jobs[j].r16 * 16 * m + kFixThreads - 1) / kFixThreads;
     }
-    fb.n = n;
-    if (n == 0) return cudaSuccess;
-    const int grid = std::max(blocks, 1);
-    switch (m) {
-        case 1: fixup_kernel<1, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 2: fixup_kernel<2, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 3: fixup_kernel<3, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 4: fixup_kernel<4, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 5: fixup_kernel<5, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 6: fixup_kernel<6, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        case 7: fixup_kernel<7, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-        default: fixup_kernel<8, MAXJ><<<grid, kFixThreads, 0, stream>>>(fb); break;
-    }
+    if (blocks >= INT32_MAX) return cudaErrorInvalidValue;
+    fb.m = m;
+    fixup_kernel<MAXJ><<<(int)std::max<int64_t>(blocks, 1), kFixThreads, 0, stream>>>(fb);
     return cudaGetLastError();
 }
 
 template <int NS, int M, int MAXJ>
 cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
-    auto kern = gemv_kernel<NS, M, MAXJ>;
+    auto kern = wide_kernel<NS, M, MAXJ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     const int64_t want = (b.total_items + kWarps - 1) / kWarps;
@@ -837,11 +605,13 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     // launch; larger launches keep the two passes (the rows' residual tail
     // would stall warps that have more items to stream)
     GemvBatch<MAXJ> sb = b;
-    sb.finish_single = M <= 8 && b.total_items <= (int64_t)kWarps * num_sms ? 1 : 0;
+    sb.finish_single = 0;
+    e = stream::launch_res(b, b.m, stream);
+    if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, kSmemBytes, stream>>>(sb);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_fixup(b, b.m, stream, sb.finish_single != 0);
+    return launch_fixup(b, b.m, stream);
 }
 
 // The tile path: a launch that lays out the activations (once per distinct x
@@ -904,9 +674,9 @@ cudaError_t dispatch(const GemvBatch<MAXJ>& b, int ns, int m, cudaStream_t s, in
         if (m <= 32) return ns == 26 ? launch_tile<26, 32, MAXJ>(b, s, sms) : launch_tile<16, 32, MAXJ>(b, s, sms);
         return ns == 26 ? launch_tile<26, 64, MAXJ>(b, s, sms) : launch_tile<16, 64, MAXJ>(b, s, sms);
     }
-#define CDQ_M_CASE(MM)                                                  \
-    case MM:                                                            \
-        return ns == 26 ? launch_one<26, MM, MAXJ>(b, s, sms) : launch_one<16, MM, MAXJ>(b, s, sms);
+#define CDQ_M_CASE(MM)                                                                      \
+    case MM:                                                                                \
+        return ns == 26 ? stream::launch<26, MM, MAXJ>(b, s, sms) : stream::launch<16, MM, MAXJ>(b, s, sms);
     switch (m) {
         CDQ_M_CASE(1)
         CDQ_M_CASE(2)
@@ -961,12 +731,15 @@ cudaError_t gemv_read_error(int* out) {
 
 // ---------------------------------------------------------------------------
 // cdq_linear_noalloc: the fused linear for callers that cannot allocate device
-// memory. Its split-K scratch (per-group partial sums and per-row-block arrival
-// counters, the same layout as cdq_linear's workspace) lives in the file-scope
+// memory. Its scratch (one arrival counter per row block, then the per-group
+// sums, the same layout as cdq_linear's workspace) lives in the file-scope
 // array below, which every GPU that loads this library holds until the process
-// exits. Host code never touches the array by name: the array's host-side
-// symbol is only a stand-in, so set-up asks the runtime for its device address
-// once per device (with that device current) and passes that address on.
+// exits. The array starts zeroed and every completed call leaves its counters
+// at zero again. Host code never touches the array by name: the array's
+// host-side symbol is only a stand-in, so set-up asks the runtime for its
+// device address once per device (with that device current) and passes that
+// address on. The address is cached per device ordinal, so it does not survive
+// a cudaDeviceReset of that device.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -1043,17 +816,18 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     J.out_f32 = 0;
     J.n_res = (uint32_t)w->n_res;
     J.item_begin = 0;
+    J.unit_begin = 0;
     J.rb_begin = 0;
     J.reserved0 = 0;
     J.reserved_ptr = nullptr;
-    // the streaming pass writes every partial slot before the fix-up pass
-    // reads it, so the array's previous contents never matter
-    J.partial = static_cast<float*>(scratch);
+    // counters first (zero), then the sums: each sum is written before it is read
+    J.counters = static_cast<uint32_t*>(scratch);
+    J.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + gemv_counter_bytes(g));
     b.total_items = (int64_t)J.r16 * J.kg;
     b.total_row_blocks = J.r16;
     b.m = (int32_t)m;
     b.finish_single = 0;
-    // the streaming path only: its scratch is sized for the group sums
+    // the streaming paths only: the scratch holds counters and group sums, no prepared activations
     return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms, false) == cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;

@@ -20,15 +20,17 @@ struct GemvJob {
     float* partial;       // per-group partial sums [m][kg][r16*16] (workspace)
     void* reserved_ptr;
     int64_t item_begin;   // first work item (row block x residual group) of this job
+    int64_t unit_begin;   // first unit of this job in the launch's unit sequence (streaming kernel)
+    uint32_t* counters;   // per-row-block arrival counters after the partial sums (streaming kernel)
     int32_t rows, cols, r16, kt, kp, kg;
     int32_t out_f32;
     uint32_t n_res;       // residual entries; bucket pointers are clamped to it
     int32_t rb_begin;     // first fix-up block of this job (set by the launcher)
     int32_t reserved0;
 };
-static_assert(sizeof(GemvJob) == 112, "GemvJob layout");
+static_assert(sizeof(GemvJob) == 128, "GemvJob layout");
 
-constexpr int kMaxJobs = 192;  // 192 x 112-byte jobs fit the 32 KB kernel-parameter space
+constexpr int kMaxJobs = 192;  // 192 x 128-byte jobs fit the 32 KB kernel-parameter space
 
 template <int MAXJ>
 struct GemvBatch {
@@ -37,6 +39,7 @@ struct GemvBatch {
     int32_t total_row_blocks;  // fix-up pass work
     int32_t m;                 // batch rows of every job of the launch
     int32_t finish_single;     // streaming pass finishes single-group jobs itself (small launches)
+    int64_t total_units;       // units of every job of the launch (streaming kernel)
     GemvJob jobs[MAXJ];
 };
 

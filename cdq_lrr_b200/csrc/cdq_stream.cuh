@@ -1,0 +1,536 @@
+// The streaming fused linear for batches of 1 to 8 rows, and the residual
+// pre-pass shared by both streaming paths. Included by cdq_gemv.cu (it shares
+// that file's bulk-copy ring, pair tables and unit decode).
+//
+// Residual pre-pass (res_sum_kernel). One thread per CSR bucket (row, group
+// of 32 tile columns) of every job of the launch:
+//     R[n][group][row] = sum over the bucket's entries, in order, starting
+//                        from zero, of bf16 value x activation (fp32 fma),
+// written to the job's per-group sums in the workspace. The buckets of a row
+// are consecutive, so a warp reads one stretch of the entry array; a thread's
+// loads are issued in batches so that several are in flight.
+//
+// Streaming kernel (stream_kernel). The units of every job of a launch form
+// one sequence: job by job, row block by row block, which is also the order
+// of the units buffers in memory. A work item is (job, 16-row block, residual
+// group of up to 16 units, i.e. 32 tile columns). Warp w of the W warps of
+// the grid owns the items whose first unit lies in [U*w/W, U*(w+1)/W) (U =
+// units of the launch), so each warp walks one contiguous stretch of the
+// units buffers: its producer lane copies quad after quad into the warp's
+// two-slot ring, and the cursor moves from item to item without a search.
+// Per item the quads are decoded into exact w_hat pairs and fed to mma.sync
+// (as in the wide kernel), and the group's value is the mma sum plus the
+// group's residual sum from the pre-pass (read at the item's start, used at
+// its end). An output is
+//     y = sum over the row's groups, in group order and starting from zero,
+//         of (mma sum of the group + residual sum of the group), + bias,
+// rounded once. A row block whose groups all lie in one warp's stretch is
+// summed in registers. A row block cut by a stretch boundary writes each
+// group's value to the workspace (over the group's residual sum, which its
+// own lane has read); the warp that brings the row block's arrival counter to
+// its group count adds the values in group order, stores y and resets the
+// counter to zero. Either way the arithmetic is the same, so y does not
+// depend on how a launch is cut into stretches (or grouped with other jobs),
+// and the output is deterministic. The wide kernel (batches above 8) and its
+// fix-up pass use the same per-group values.
+namespace stream {
+
+#ifndef CDQ_STREAM_WARPS
+#define CDQ_STREAM_WARPS 16
+#endif
+constexpr int kSWarps = CDQ_STREAM_WARPS;
+constexpr int kSThreads = 32 * kSWarps;
+constexpr int kSLowWarps = 5;  // rings below the pair table, in [1K, 32K)
+
+// A slot holds one quad (the activations come through the L1 cache).
+template <int NS>
+struct Ring {
+    static constexpr uint32_t kQuad = 4 * PackTraits<NS>::kUnit;
+    static constexpr uint32_t kBytes = kSlots * kQuad;
+    static constexpr uint32_t kTop = kHighStage + (kSWarps - kSLowWarps) * kBytes;
+};
+static_assert(kLowStage + kSLowWarps * Ring<26>::kBytes <= (32u << 10), "low rings overlap the table");
+static_assert(Ring<26>::kTop <= kSmemBytes && Ring<16>::kTop <= kSmemBytes, "rings exceed the window");
+static_assert(kBarAddr + kSWarps * kSlots * 8 <= (512u << 7), "barriers overlap the table");
+
+template <int NS>
+__device__ __forceinline__ uint32_t ring_of(int warp) {
+    return warp < kSLowWarps ? kLowStage + warp * Ring<NS>::kBytes
+                             : kHighStage + (warp - kSLowWarps) * Ring<NS>::kBytes;
+}
+
+// A work item: job, 16-row block, residual group.
+struct Cursor {
+    int j, b16, grp;
+};
+
+// First unit of the item (the launch's unit count once past the last job).
+template <int MAXJ>
+__device__ __forceinline__ int item_start(const GemvBatch<MAXJ>& b, const Cursor& c) {
+    if (c.j >= b.n) return (int)b.total_units;
+    const GemvJob& J = b.jobs[c.j];
+    return (int)J.unit_begin + c.b16 * J.kp + 16 * c.grp;
+}
+
+template <int MAXJ>
+__device__ __forceinline__ void advance(const GemvBatch<MAXJ>& b, Cursor& c) {
+    const GemvJob& J = b.jobs[c.j];
+    if (++c.grp == J.kg) {
+        c.grp = 0;
+        if (++c.b16 == J.r16) {
+            c.b16 = 0;
+            ++c.j;
+        }
+    }
+}
+
+// The first item whose first unit is >= u (u in [0, total_units]).
+template <int MAXJ>
+__device__ __forceinline__ Cursor first_at(const GemvBatch<MAXJ>& b, int u) {
+    int lo = 0, hi = b.n - 1;
+    while (lo < hi) {  // last job with unit_begin <= u (uniform reads of the launch record)
+        const int mid = (lo + hi + 1) >> 1;
+        if (b.jobs[mid].unit_begin <= u) lo = mid; else hi = mid - 1;
+    }
+    const GemvJob& J = b.jobs[lo];
+    const uint32_t rel = (uint32_t)(u - J.unit_begin);  // launches hold fewer than 2^31 units
+    Cursor c;
+    c.j = lo;
+    c.b16 = (int)(rel / (uint32_t)J.kp);
+    c.grp = ((int)(rel - (uint32_t)c.b16 * (uint32_t)J.kp) + 15) >> 4;
+    if (c.grp >= J.kg) {
+        c.grp = 0;
+        ++c.b16;
+    }
+    if (c.b16 >= J.r16) {
+        c.b16 = 0;
+        ++c.j;
+    }
+    return c;
+}
+
+// Residual pre-pass: a block takes 256 consecutive buckets of one job (one
+// thread per bucket). Their entries are one contiguous stretch of the entry
+// array: thread 0 bulk-copies it into shared memory (the 16-byte-aligned
+// part; a ragged edge of up to three entries at either end is read with
+// plain loads) together with the activation row, then each thread adds its
+// bucket's entries in order, activations read from shared memory. A stretch
+// longer than the entry buffer goes in chunks (the thread's sum carries
+// over); batches of several rows repeat the pass per row. The one wait on the
+// copies is bounded (error code 4 of the fused linear on timeout). Block ->
+// job through rb_begin (set by the launcher).
+constexpr int kResThreads = 256;
+constexpr int kResCap = 4096;  // entries staged per chunk (16 KB)
+
+__host__ __device__ constexpr int res_smem_bytes(int cols) { return 16 + (kResCap + 4) * 4 + cols * 2; }
+
+template <int MAXJ>
+__global__ void __launch_bounds__(kResThreads) res_sum_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    extern __shared__ __align__(16) uint8_t rsm[];
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(rsm);
+    uint32_t* const ent = reinterpret_cast<uint32_t*>(rsm + 16);  // entry e of a chunk at e - (c0 & ~3)
+    uint16_t* const xs = reinterpret_cast<uint16_t*>(rsm + 16 + (kResCap + 4) * 4);
+    int j = 0;
+    if constexpr (MAXJ > 1) {
+        int lo = 0, hi = batch.n - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (batch.jobs[mid].rb_begin <= (int)blockIdx.x) lo = mid; else hi = mid - 1;
+        }
+        j = lo;
+    }
+    const GemvJob& J = batch.jobs[j];
+    const int kg = J.kg, cols = J.cols, tid = threadIdx.x;
+    const uint32_t buckets = (uint32_t)J.r16 * 16u * (uint32_t)kg;
+    const uint32_t bb = ((uint32_t)blockIdx.x - (uint32_t)J.rb_begin) * kResThreads;
+    const uint32_t b = bb + tid;
+    const bool live = b < buckets;
+    const uint32_t n_res = J.n_res;
+    const uint32_t last = min(bb + kResThreads, buckets);  // one past the block's last bucket
+    const bool bulk = ((uintptr_t)J.res_ent & 15u) == 0;   // entries 16-byte aligned: copy in bulk
+    if (tid == 0) {
+        mbar_init(bar);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // the block's stretch [E0, E1) and this thread's bucket [s, t) (the CSR is ascending)
+    const uint32_t E0 = min(__ldg(J.res_ptr + bb), n_res);
+    const uint32_t E1 = max(min(__ldg(J.res_ptr + last), n_res), E0);
+    const uint32_t s = live ? min(max(__ldg(J.res_ptr + b), E0), E1) : E1;
+    const uint32_t t = live ? min(max(__ldg(J.res_ptr + b + 1), s), E1) : E1;
+    const uint32_t row = b / (uint32_t)kg, grp = b - row * (uint32_t)kg;
+    const int64_t rpad = (int64_t)J.r16 * 16;
+    const int m = batch.m;
+    __syncthreads();
+    uint32_t phase = 0;
+    for (int n = 0; n < m; ++n) {
+        float acc = 0.f;
+        for (uint32_t c0 = E0; c0 < E1; c0 += kResCap) {
+            const uint32_t c1 = min(c0 + (uint32_t)kResCap, E1), base = c0 & ~3u;
+            // [a0, a1): the chunk's 16-byte-aligned entries (bulk-copied); [c0, a0)
+            // and [a1, c1) hold at most three entries each (plain loads)
+            const uint32_t a0 = bulk ? min((c0 + 3u) & ~3u, c1) : c1, a1 = bulk ? max(c1 & ~3u, a0) : c1;
+            __syncthreads();  // the previous chunk's (or row's) readers are done
+            if (tid == 0) {
+                const uint32_t xbytes = c0 == E0 ? (uint32_t)cols * 2 : 0u;
+                slot_arm(bar, xbytes + (a1 - a0) * 4);
+                if (xbytes) bulk_copy(bar + 16 + (kResCap + 4) * 4, J.x + (int64_t)n * cols, xbytes, bar);
+                if (a1 > a0) bulk_copy(bar + 16 + (a0 - base) * 4, J.res_ent + a0, (a1 - a0) * 4, bar);
+            }
+            for (uint32_t e = c0 + tid; e < a0; e += kResThreads) ent[e - base] = __ldg(J.res_ent + e);
+            for (uint32_t e = a1 + tid; e < c1; e += kResThreads) ent[e - base] = __ldg(J.res_ent + e);
+            const bool landed = mbar_wait(bar, phase);
+            phase ^= 1u;
+            if (!__syncthreads_and(landed)) {
+                if (tid == 0) atomicExch(&g_gemv_error, 4);
+                return;
+            }
+            const uint32_t lo = max(s, c0), hi = min(t, c1);
+            for (uint32_t e = lo; e < hi; ++e) {
+                const uint32_t en = ent[e - base];
+                const uint32_t col = en >> 16;
+                if (col < (uint32_t)cols)
+                    acc = fmaf(__uint_as_float(en << 16), __uint_as_float((uint32_t)xs[col] << 16), acc);
+            }
+        }
+        if (live) J.partial[((int64_t)n * kg + grp) * rpad + row] = acc;
+    }
+}
+
+// The pre-pass over every job of the launch (a batch of m rows).
+template <int MAXJ>
+cudaError_t launch_res(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream) {
+    GemvBatch<MAXJ> rb = b;
+    int64_t blocks = 0;
+    int max_cols = 32;
+    for (int j = 0; j < b.n; ++j) {
+        rb.jobs[j].rb_begin = (int32_t)blocks;
+        blocks += ((int64_t)b.jobs[j].r16 * 16 * b.jobs[j].kg + kResThreads - 1) / kResThreads;
+        max_cols = std::max(max_cols, (int)b.jobs[j].cols);
+    }
+    if (blocks >= INT32_MAX) return cudaErrorInvalidValue;
+    rb.m = m;
+    const int smem = res_smem_bytes(max_cols);  // at most 160 KB
+    auto kern = res_sum_kernel<MAXJ>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, res_smem_bytes(CDQ_MAX_COLS));
+    if (e != cudaSuccess) return e;
+    kern<<<(int)std::max<int64_t>(blocks, 1), kResThreads, smem, stream>>>(rb);
+    return cudaGetLastError();
+}
+
+// floor(U * k / n) for U < 2^31 and k <= n < 2^16, without a 64-bit division:
+// the double quotient is within one of the answer, then fixed exactly.
+__device__ __forceinline__ int64_t stretch_bound(int64_t U, int64_t k, int64_t n) {
+    const int64_t num = U * k;
+    int64_t q = (int64_t)((double)num / (double)n);
+    if (q * n > num) --q;
+    if ((q + 1) * n <= num) ++q;
+    return q;
+}
+
+// A group of a row block cut by a stretch boundary: store the group's value;
+// the warp's last group of the row block reports its `done` groups on the
+// row block's counter, and the warp that completes the count adds the groups
+// in order, stores y and resets the counter. Kept out of line: it runs for at
+// most two row blocks per warp.
+template <int M>
+__device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const float (&v)[4], bool report,
+                                       int done, int g, int c, int lane) {
+    const int kg = J.kg;
+    const int64_t rpad = (int64_t)J.r16 * 16;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int64_t row = b16 * 16 + g + 8 * h;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const int n = 2 * c + jj;
+            if (n < M) J.partial[((int64_t)n * kg + grp) * rpad + row] = v[2 * h + jj];
+        }
+    }
+    if (!report) return;
+    __threadfence();
+    __syncwarp();
+    uint32_t before = 0;
+    if (lane == 0) before = atomicAdd(J.counters + b16, (uint32_t)done);
+    before = __shfl_sync(0xFFFFFFFFu, before, 0);
+    if (before + (uint32_t)done != (uint32_t)kg) return;
+    // every group has arrived: add them in group order
+    __threadfence();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = b16 * 16 + g + 8 * h;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+            const int n = 2 * c + jj;
+            if (n < M) {
+                const float* sp = J.partial + (int64_t)n * kg * rpad + row;
+                float s = 0.f;
+                for (int k = 0; k < kg; ++k) s += __ldcg(sp + (int64_t)k * rpad);
+                if (row < J.rows) store_out(J, n, row, s);
+            }
+        }
+    }
+    if (lane == 0) J.counters[b16] = 0u;
+}
+
+template <int NS, int M, int MAXJ>
+__global__ void __launch_bounds__(kSThreads, 1)
+stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    using Tr = PackTraits<NS>;
+    constexpr uint32_t kU = Tr::kUnit;
+    using Rg = Ring<NS>;
+    constexpr uint32_t kQuad = Rg::kQuad;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+    if (s0 > kLowStage || s0 + kSmemBytes < Rg::kTop) {
+        if (threadIdx.x == 0) atomicExch(&g_gemv_error, 1);
+        return;
+    }
+    uint8_t* const base = smem - s0;  // generic pointer of shared address 0
+    for (int i = threadIdx.x; i < Tr::kPairs * 32; i += blockDim.x) {
+        const uint32_t p = (uint32_t)i >> 5, l = (uint32_t)i & 31;
+        uint32_t lo, hi, addr;
+        if constexpr (NS == 26) {
+            lo = c_lat26[p / 27];
+            hi = c_lat26[p % 27];
+            addr = ((p << 7) ^ kLat26Xor) + 4 * l;
+        } else {
+            lo = c_lat16[p & 15];
+            hi = c_lat16[p >> 4];
+            addr = kLat16Base + (p << 8) + 4 * l;
+        }
+        *reinterpret_cast<uint32_t*>(base + addr) = lo | (hi << 16);
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        const uint32_t s = fp8_to_bf16((uint8_t)i);
+        *reinterpret_cast<uint32_t*>(base + kSigAddr + 4 * i) = s | (s << 16);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const uint32_t ring = ring_of<NS>(warp);
+    const uint32_t bars = kBarAddr + warp * kSlots * 8;
+    if (lane == 0) {
+        for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    // this warp's stretch of the unit sequence
+    const int64_t U = batch.total_units;
+    const int64_t nw = (int64_t)gridDim.x * kSWarps;
+    const int64_t gw = (int64_t)blockIdx.x * kSWarps + warp;
+    const int u_lo = (int)stretch_bound(U, gw, nw), u_hi = (int)stretch_bound(U, gw + 1, nw);
+    Cursor cur = first_at(batch, u_lo);
+    const int u_first = item_start(batch, cur);
+    if (u_first >= u_hi) return;  // no item starts in this stretch
+    const int u_end = item_start(batch, first_at(batch, u_hi));
+    const int grp_first = cur.grp;  // first group of a row block cut at the stretch's start
+
+    const uint32_t lane_base = NS == 26 ? (kLat26Xor | (4u * lane)) : (kLat16Base + 4u * lane);
+    const uint32_t sig_base = kSigAddr;
+    const int xrow = g < M ? g : 0;  // batch rows >= M: their mma columns are never stored
+
+    // Producer (lane 0 issues; every lane keeps the same cursor): the quads of
+    // [u_first, u_end), which are consecutive in each job's units buffer.
+    int pj = cur.j;
+    int p_left = (int)(u_end - u_first);
+    int p_kp, p_r, p_rb;
+    const uint8_t* p_ptr;
+    {
+        const GemvJob& J = batch.jobs[pj];
+        p_kp = J.kp;
+        p_r = 16 * cur.grp;
+        p_rb = J.r16 - cur.b16;
+        p_ptr = J.units + ((int64_t)cur.b16 * J.kp + p_r) * kU;
+    }
+    // into `slot`: the slot the consumer has just read (two copies run ahead)
+    auto produce = [&](uint32_t slot) {
+        if (p_left <= 0) return;
+        const int u = min(4, p_kp - p_r);
+        const uint32_t bytes = (uint32_t)u * kU;
+        if (lane == 0) {
+            const uint32_t bar = bars + 8 * slot;
+            slot_arm(bar, bytes);
+            bulk_copy(ring + slot * kQuad, p_ptr, bytes, bar);
+        }
+        p_ptr += bytes;
+        p_left -= u;
+        p_r += u;
+        if (p_r == p_kp) {
+            p_r = 0;
+            if (--p_rb == 0 && p_left > 0) {
+                const GemvJob& J = batch.jobs[++pj];
+                p_kp = J.kp;
+                p_rb = J.r16;
+                p_ptr = J.units;
+            }
+        }
+    };
+    produce(0);
+    produce(1);
+
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t c_slot = 0, c_phase = 0;
+    bool failed = false;
+    for (;;) {
+        const int ustart = item_start(batch, cur);
+        if (ustart >= u_hi) break;
+        const GemvJob& J = batch.jobs[cur.j];
+        const int kg = J.kg, kp = J.kp, cols = J.cols;
+        const int cp0 = 16 * cur.grp;
+        const int n_units = min(16, kp - cp0), nq = (n_units + 3) >> 2;
+        // a phantom second tile (odd tile count) sits in the row block's last unit
+        const int phantom_u = (J.kt & 1) && cp0 + n_units == kp ? n_units - 1 : -1;
+        const bool phantom_item = phantom_u >= 0;
+        const uint16_t* xp = J.x + (int64_t)xrow * cols + 64 * cp0 + 16 * c;
+
+        // the group's residual sums of rows g and g + 8 (batch columns 2c, 2c + 1),
+        // from the pre-pass: in flight while the quads stream
+        const int64_t rpad = (int64_t)J.r16 * 16;
+        float R[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj)
+                if (2 * c + jj < M)
+                    R[2 * h + jj] = __ldcg(J.partial + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
+                                           cur.b16 * 16 + g + 8 * h);
+
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < nq; ++q) {
+            if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
+                failed = true;
+                break;
+            }
+            const uint32_t slot = ring + c_slot * kQuad;
+            const int uq = min(4, n_units - 4 * q);
+            const uint16_t* xq = xp + 256 * q;
+            if (uq == 4 && !phantom_item) {
+                // a full quad without a phantom tile: no per-unit checks
+                uint4 A[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                const uint4 W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                const uint2 S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+                // one register of every slot read: each read has landed before the slot is reused
+                uint32_t dep = W.x ^ S.x ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+                asm volatile("" ::"r"(dep));
+                __syncwarp();
+                produce(c_slot);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 xa = ldg_x4(xq + 64 * i), xb = ldg_x4(xq + 64 * i + 8);
+                    const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
+                    if (i & 1) unit_mma<NS, 16>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
+                    else unit_mma<NS, 0>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
+                }
+            } else {
+                // a short last quad (1..3 units, compact) or the quad holding a phantom tile
+                uint4 A[4];
+                uint4 W;
+                uint2 S;
+                if (uq == 4) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                    W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+                    S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+                } else {
+                    uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) {
+                        A[i] = make_uint4(0u, 0u, 0u, 0u);
+                        if (i < uq) {
+                            A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+                            if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
+                            h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
+                        }
+                    }
+                    A[3] = make_uint4(0u, 0u, 0u, 0u);
+                    W = make_uint4(w4[0], w4[1], w4[2], 0u);
+                    S = make_uint2(h[0] | (h[1] << 16), h[2]);
+                }
+                uint32_t dep = W.x ^ W.y ^ W.z ^ S.x ^ S.y ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+                asm volatile("" ::"r"(dep));
+                __syncwarp();
+                produce(c_slot);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (i < uq) {
+                        uint4 xa, xb;
+                        load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
+                        const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
+                        if (i & 1) unit_mma<NS, 16>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
+                        else unit_mma<NS, 0>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
+                    }
+                }
+            }
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
+        }
+        if (failed) break;
+
+        // (row g + 8h, batch column 2c + j) of this lane's mma fragment: e = 2h + j
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = d[e] + R[e];
+
+        const int rb0 = ustart - cp0;  // first unit of the row block
+        Cursor nxt = cur;
+        advance(batch, nxt);
+        const bool has_next = item_start(batch, nxt) < u_hi;
+        const bool cut = kg > 1 && (rb0 < u_lo || rb0 + 16 * (kg - 1) >= u_hi);
+        if (!cut) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tot[e] += v[e];
+            if (cur.grp == kg - 1) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = cur.b16 * 16 + g + 8 * h;
+#pragma unroll
+                    for (int jj = 0; jj < 2; ++jj)
+                        if (row < J.rows && 2 * c + jj < M) store_out(J, 2 * c + jj, row, tot[2 * h + jj]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) tot[e] = 0.f;
+            }
+        } else {
+            cut_group<M>(J, cur.b16, cur.grp, v, cur.grp == kg - 1 || !has_next,
+                         cur.grp - (rb0 < u_lo ? grp_first : 0) + 1, g, c, lane);
+        }
+        cur = nxt;
+    }
+    if (failed) {
+        // a copy that never landed: record it, give the copies still in
+        // flight a bounded chance to land, and leave
+        if (lane == 0) atomicExch(&g_gemv_error, 2);
+        for (int k = 0; k < kSlots; ++k) {
+            (void)mbar_wait(bars + 8 * c_slot, c_phase);
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
+        }
+    }
+}
+
+// Two launches: the residual pre-pass, then the streaming kernel (the jobs'
+// unit offsets laid out on the host; one CTA per SM at most, none beyond the
+// number of work items).
+template <int NS, int M, int MAXJ>
+cudaError_t launch(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
+    auto kern = stream_kernel<NS, M, MAXJ>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    GemvBatch<MAXJ> sb = b;
+    int64_t units = 0, items = 0;
+    for (int j = 0; j < b.n; ++j) {
+        sb.jobs[j].unit_begin = units;
+        units += (int64_t)b.jobs[j].r16 * b.jobs[j].kp;
+        items += (int64_t)b.jobs[j].r16 * b.jobs[j].kg;
+    }
+    if (units >= INT32_MAX) return cudaErrorInvalidValue;
+    sb.total_units = units;
+    e = launch_res(b, M, stream);
+    if (e != cudaSuccess) return e;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms));
+    kern<<<grid, kSThreads, kSmemBytes, stream>>>(sb);
+    return cudaGetLastError();
+}
+
+}  // namespace stream

@@ -187,7 +187,9 @@ class DevicePack:
         tc = torch.bincount(tile, minlength=self.n_tiles)
         return int(self.n_tiles * (2 + ib) + ((tc * 21 + 7) // 8).sum().item())
 
-    # ---- workspace of cdq_linear (float32 group sums, kept by the pack) ----
+    # ---- workspace of cdq_linear, kept by the pack: row-block arrival counters
+    # (zero before the first call; every call leaves them zero), then float32
+    # group sums or the tile path's prepared activations ----
     def linear_workspace(self, m: int) -> torch.Tensor:
         dev = self.device
         key = (dev, m)
@@ -254,7 +256,7 @@ def _job_workspace(pack: DevicePack, m: int, seen: set, keep: list) -> torch.Ten
         seen.add(id(pack))
         return pack.linear_workspace(m)
     s = L.sizes(pack.rows, pack.cols, pack.n_states, max_batch=m)
-    ws = torch.empty(max(s.linear_workspace_bytes, 256), dtype=torch.uint8, device=pack.device)
+    ws = torch.zeros(max(s.linear_workspace_bytes, 256), dtype=torch.uint8, device=pack.device)
     keep.append(ws)
     return ws
 
@@ -310,11 +312,15 @@ class GroupedLinear:
             j.workspace_bytes = ws.numel()
             j.out_f32 = 1 if t.y.dtype == torch.float32 else 0
         self.device = self.tasks[0].x.device if self.tasks else None
-        # per lattice size, per batch of at most L.MAX_JOBS jobs: a streaming pass and a fix-up pass
+        # per lattice size, per batch of at most L.MAX_JOBS jobs: the residual
+        # pre-pass and the streaming kernel for m <= 8; above, the pre-pass,
+        # the wide streaming kernel and its fix-up (or, on the tcgen05 tile
+        # path, the activation layout and the tile kernel)
         per_ns = {}
         for t in self.tasks:
             per_ns[t.pack.n_states] = per_ns.get(t.pack.n_states, 0) + 1
-        self.launches = sum(2 * -(-n // L.MAX_JOBS) for n in per_ns.values())
+        per = 2 if m <= 8 else 3
+        self.launches = sum(per * -(-n // L.MAX_JOBS) for n in per_ns.values())
 
     def __call__(self) -> None:
         if self.tasks:

@@ -149,6 +149,43 @@ def test_linear_split_k_and_ragged(shape, ns, m):
     _check_gemv(y1, O.linear_f64(O.dequantize(p), _bits(x)))
 
 
+@pytest.mark.parametrize("m", [1, 2, 5, 8])
+def test_stream_cut_row_blocks_and_counters(m):
+    """Long rows (several residual groups) in launches of every size: the row
+    blocks that a warp's stretch boundary cuts are finished through the
+    workspace's arrival counters. The result is bit-identical whether the job
+    runs alone or among other jobs (different cuts), and every call leaves the
+    counters at zero."""
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200 import ops
+    from cdq_lrr_b200.synth import synth_activation, synth_weight
+    shapes = [(896, 4864), (64, 18944), (1000, 2080), (16, 65504 // 32 * 32)]
+    packs = [ops.quantize(synth_weight(r, c, seed=r + c).cuda(), n_states=26)[0] for r, c in shapes]
+    xs = [synth_activation(m, c, seed=c).cuda() for _, c in shapes]
+    singles = [ops.linear(p, x, out_f32=True) for p, x in zip(packs, xs)]
+    filler = [ops.quantize(synth_weight(4864, 896, seed=i).cuda(), n_states=26)[0] for i in range(3)]
+    for order in (0, 1):
+        tasks = []
+        jobs = list(zip(packs, xs))
+        if order:
+            jobs = jobs[::-1]
+        for f in filler:
+            tasks.append(ops.GemvTask(f, synth_activation(m, 896, seed=9).cuda(),
+                                      torch.empty(m, 4864, dtype=torch.float32, device="cuda")))
+        for p, x in jobs:
+            tasks.append(ops.GemvTask(p, x, torch.empty(m, p.rows, dtype=torch.float32, device="cuda")))
+        ops.linear_grouped(tasks, m)
+        torch.cuda.synchronize()
+        got = {id(t.pack): t.y for t in tasks}
+        for p, s in zip(packs, singles):
+            assert torch.equal(got[id(p)], s)
+    for p, (r, c), x, s in zip(packs, shapes, xs, singles):
+        ws = p.linear_workspace(m)
+        nbytes = (r + 15) // 16 * 4
+        assert int(ws[:nbytes].count_nonzero()) == 0
+        _check_gemv(s, O.linear_f64(_bits(ops.dequant(p)), _bits(x)))
+
+
 def test_linear_batch_above_8_splits():
     from cdq_lrr_b200 import ops
     from cdq_lrr_b200.synth import synth_activation, synth_weight
