@@ -70,6 +70,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp7b", type=int, default=1,
+                    help="1: add the tensor-parallel Qwen2.5-7B-shape stack over all ranks to the default "
+                         "line (0: skip)")
     ap.add_argument("--decode-tokens", type=int, default=256,
                     help="greedy tokens decoded after a 128-token prompt by the full "
                          "Qwen2.5-0.5B-architecture model (0: skip the decode measurement)")
@@ -215,23 +218,41 @@ def sum_over_ranks(ws, v: float) -> float:
 # --------------------------------------------------------------- CPU baseline
 
 
-def cpu_baseline(seconds: float, use_product_quantizer_packs=None) -> dict:
-    """The reference CPU forward on layer 0's seven projections, repeated."""
+def oracle_workload():
+    """The benchmark workload for the reference's CPU forward: all 168
+    projections as reference-format packs (seeded random valid indices, fp8
+    scales in [2^-6, 2^-2) and round(0.0156 * numel) residuals at random
+    positions, the sizes of the quantized workload: the forward's cost does
+    not depend on the values) and the GPU arm's activations. Returns the
+    modules, the activations and the algorithmic bytes of one pass."""
     import numpy as np
-    import torch
     from oracle import cdq_oracle as O
     from oracle.cdq_oracle_torch import OracleCDQLinear
-    from cdq_lrr_b200.synth import QWEN05, layer_shapes, synth_activation, synth_weight
+    from cdq_lrr_b200.synth import synth_activation
+    mods, xs = [], []
+    for i, (_, rows, cols) in enumerate(layer_list()):
+        rng = np.random.default_rng(i)
+        n = rows * cols
+        k = int(round(n * 0.0156))
+        sc = rng.integers(0x08, 0x28, n // 32, dtype=np.uint8)
+        p = {"quant_indices": rng.integers(0, 26, (n // 32, 32), dtype=np.uint8),
+             "scales_bf16": O.f32_to_bf16_bits(O.fp8_e4m3fn_decode(sc)),
+             "residual_indices": np.sort(rng.choice(n, k, replace=False)).astype(np.int64),
+             "residual_values": rng.integers(0x3C00, 0x3F00, k, dtype=np.uint16),
+             "lattice": O.lattice_bits(26), "orig_shape": (rows, cols)}
+        mods.append(OracleCDQLinear(p))
+        xs.append(synth_activation(1, cols, seed=10000 + i))
+    step_bytes = sum(m.reference_bytes() + x.numel() * 2 + m.orig_shape[0] * 2 for m, x in zip(mods, xs))
+    return mods, xs, step_bytes
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The reference CPU forward over the whole workload (all 168 projections),
+    repeated for about `seconds`, on every host thread."""
+    import torch
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    mods, xs = [], []
-    for i, (name, rows, cols) in enumerate(layer_shapes(QWEN05)):
-        w = synth_weight(rows, cols, std=0.02, seed=1000 + i)
-        p = O.quantize(w.view(torch.int16).numpy().view(np.uint16), n_states=26)
-        mods.append(OracleCDQLinear(p))
-        xs.append(synth_activation(1, cols, seed=2000 + i))
-    step_bytes = sum(m.reference_bytes() + x.numel() * 2 + m.orig_shape[0] * 2
-                     for m, x in zip(mods, xs))
+    mods, xs, step_bytes = oracle_workload()
     with torch.no_grad():
         for m, x in zip(mods, xs):
             m(x)  # warm-up
@@ -244,10 +265,10 @@ def cpu_baseline(seconds: float, use_product_quantizer_packs=None) -> dict:
             times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": step_bytes / med / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"layer-0 projections of the workload (7 weights, {step_bytes / 1e6:.2f} MB "
-                      f"algorithmic), {len(times)} passes, median {med * 1e3:.2f} ms/pass; "
-                      f"reference forward = lattice gather, bf16 scale multiply, residual "
-                      f"scatter, F.linear (torch CPU)",
+            "sample": f"the whole workload (168 projections, {step_bytes / 1e6:.2f} MB algorithmic) per pass, "
+                      f"{len(times)} passes, median {med * 1e3:.1f} ms/pass; reference forward = lattice gather, "
+                      f"bf16 scale multiply, residual scatter, F.linear (torch CPU, restated in "
+                      f"oracle/cdq_oracle_torch.py)",
             "ms_per_pass": med * 1e3}
 
 
@@ -443,16 +464,47 @@ def run_ours(args) -> None:
     ok = torch.equal(ys_host[last].to(dev), torch.cat([t.y.view(-1) for t in tasks]))
 
     peak, peak_kind = measured_peak()
-    # DRAM bytes per step from the committed ncu summary of this workload (both passes)
+    # DRAM bytes of one step (both launches) from the ncu capture of this
+    # workload with these kernels, summarised in profiles/ (ncu cannot run
+    # inside a timed run)
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "gemv_streaming_and_fixup_qwen05_168proj.md")
+    traffic_src = os.path.join("profiles", "stream_kernel_qwen05_168proj.md")
     try:
-        with open(tp) as f:
+        with open(os.path.join(ROOT, traffic_src)) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_step:"):
                     traffic = int(line.split(":", 1)[1])
     except OSError:
         traffic = None
+
+    # the Qwen2.5-7B-shape stack tensor-parallel over every rank of this run
+    # (one-shot all-reduce, and NCCL beside it), in every line
+    tp7 = None
+    if args.tp7b:
+        from cdq_lrr_b200.synth import QWEN7B, layer_shapes
+        import torch.distributed as dist
+        kinds = {"q_proj": "col", "k_proj": "col", "v_proj": "col", "o_proj": "row",
+                 "gate_proj": "col", "up_proj": "col", "down_proj": "row"}
+        s7 = [(n, r, c, kinds[n]) for n, r, c in layer_shapes(QWEN7B)]
+        grp = dist.group.WORLD if ws_ > 1 else None
+        tp_args = argparse.Namespace(steps=max(args.steps // 4, 10), warmup=max(args.warmup, 3))
+        one = tp_measure(tp_args, s7, QWEN7B["layers"], 26, 1, "oneshot", grp, ws_, rank, local, check=True)
+        nccl = tp_measure(tp_args, s7, QWEN7B["layers"], 26, 1, "nccl", grp, ws_, rank, local) if ws_ > 1 else None
+        if rank == 0:
+            def brief(r):
+                return {"ms_per_step": r["ms_per_step"], "aggregate_gb_s": r["value"],
+                        "per_gpu_gb_s": r["roofline"]["achieved_per_gpu"],
+                        "per_gpu_roofline_frac": r["roofline"]["frac"], "allreduce_error": r["allreduce_error"],
+                        "clocks": r["clocks"]}
+            tp7 = {"workload": "Qwen2.5-7B-shape projection stack (28 layers x 7, 26-state, seeded random packs), "
+                               f"batch 1, tensor-parallel x{ws_}: q/k/v/gate/up split by output rows, o/down "
+                               "split along K with a float32 all-reduce of their partial outputs",
+                   "n_gpus": ws_, "steps": tp_args.steps, "algorithmic_gb_all_ranks": one["algorithmic_gb_all_ranks"],
+                   "oneshot": brief(one), "nccl": brief(nccl) if nccl else None,
+                   "allreduce_match": one.get("allreduce_match", True if ws_ == 1 else None),
+                   "allreduce_match_rule": "one-shot sums == rank-order float32 sums of the NCCL-all-gathered "
+                                           "partials, bit for bit, on every rank (trivially true at one GPU)",
+                   "nccl_max_rel_diff": one.get("nccl_max_rel_diff")}
 
     cpu = None
     if rank == 0 and ws_ == 1 and not args.no_cpu_baseline:
@@ -475,6 +527,9 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(kernel_gbs / peak, 4),
                          "peak_kind": f"of {peak_kind}", "traffic": traffic,
+                         "traffic_over_algorithmic": round(traffic / alg_bytes, 4) if traffic else None,
+                         "traffic_source": f"{traffic_src}: ncu dram__bytes_read.sum + dram__bytes_write.sum of "
+                                           f"both launches of one step" if traffic else None,
                          "kernel": kernel_name},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": int(xs_host.numel() * 2),
@@ -489,6 +544,7 @@ def run_ours(args) -> None:
             "clocks": sampler.summary(t0, t1),
             "cpu_baseline": cpu,
             "decode": dec,
+            "tp7b": tp7,
         }
         print(json.dumps(line), flush=True)
     if ws_ > 1:
@@ -505,18 +561,7 @@ def run_reference(args) -> None:
     import torch
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    import numpy as np
-    from oracle import cdq_oracle as O
-    from oracle.cdq_oracle_torch import OracleCDQLinear
-    from cdq_lrr_b200.synth import QWEN05, layer_shapes, synth_activation, synth_weight
-    mods, xs = [], []
-    for i, (name, rows, cols) in enumerate(layer_shapes(QWEN05)):
-        w = synth_weight(rows, cols, std=0.02, seed=i)
-        p = O.quantize(w.view(torch.int16).numpy().view(np.uint16), n_states=26)
-        mods.append(OracleCDQLinear(p))
-        xs.append(synth_activation(1, cols, seed=10000 + i))
-    step_bytes = sum(m.reference_bytes() + x.numel() * 2 + m.orig_shape[0] * 2
-                     for m, x in zip(mods, xs))
+    mods, xs, step_bytes = oracle_workload()
     with torch.no_grad():
         for _ in range(args.warmup):
             for m, x in zip(mods, xs):
@@ -527,8 +572,8 @@ def run_reference(args) -> None:
                 m(x)
         dt = (time.perf_counter() - t0) / args.steps
     value = step_bytes / dt / 1e9
-    sample = (f"each step = the reference CPU forward over layer 0's 7 projections of the "
-              f"workload ({step_bytes / 1e6:.2f} MB algorithmic); GB/s is size-independent")
+    sample = (f"each step = the reference CPU forward (restated with the same torch CPU ops) over the whole "
+              f"workload: all 168 projections, {step_bytes / 1e6:.2f} MB algorithmic, batch 1")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
@@ -619,8 +664,38 @@ def run_tp70b(args) -> None:
            f"{args.states}-state")
 
 
+def tp_allreduce_check(layers, oar, group, world: int) -> dict:
+    """One step's row-parallel reductions, checked across ranks: the one-shot
+    all-reduce's sums must equal, bit for bit, the float32 sums in rank order
+    (starting from zero) of the partials gathered from every rank by NCCL, and
+    are compared with NCCL's own all-reduce of the same partials (whose
+    summation order is NCCL's). Every rank takes the same collective steps."""
+    import torch
+    import torch.distributed as dist
+    match, worst = True, 0.0
+    for g, ys in layers[:2]:
+        g()
+        parts = [y.clone() for y in ys]
+        for y in ys:
+            oar(y)
+        for y, p in zip(ys, parts):
+            gathered = [torch.empty_like(p) for _ in range(world)]
+            dist.all_gather(gathered, p, group=group)
+            ref = torch.zeros_like(p)
+            for q in gathered:
+                ref = ref + q
+            match = match and bool(torch.equal(y, ref))
+            nc = p.clone()
+            dist.all_reduce(nc, group=group)
+            worst = max(worst, float((nc - y).abs().max() / (y.abs().max() + 1e-30)))
+    torch.cuda.synchronize()
+    t = torch.tensor([1.0 if match else 0.0], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return {"allreduce_match": bool(t.item() == 1.0), "nccl_max_rel_diff": worst}
+
+
 def tp_measure(args, shapes, n_layers: int, n_states: int, batch: int, allreduce: str, group,
-               world: int, rank: int, local: int) -> dict | None:
+               world: int, rank: int, local: int, check: bool = False) -> dict | None:
     """Tensor-parallel GEMV stack on the ranks of `group` (world ranks): per
     layer, q/k/v/gate/up split by output rows (no collective) and o/down split
     along K with a float32 all-reduce of their partial outputs, by the
@@ -663,6 +738,7 @@ def tp_measure(args, shapes, n_layers: int, n_states: int, batch: int, allreduce
             alg_bytes += pack.reference_bytes() + x.numel() * 2 + y.numel() * (2 if y.dtype == torch.bfloat16 else 4)
         layers.append((ops.GroupedLinear(tasks, m=m), reduce_ys))
     oar = tp.OneShotAllReduce(max_red, group=group) if world > 1 and allreduce == "oneshot" else None
+    checked = tp_allreduce_check(layers, oar, group, world) if check and oar is not None else None
 
     def step():
         for g, ys in layers:
@@ -734,7 +810,7 @@ def tp_measure(args, shapes, n_layers: int, n_states: int, batch: int, allreduce
             "algorithmic_gb_all_ranks": round(total / 1e9, 3),
             "roofline": {"bound": "hbm", "achieved_per_gpu": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu / peak, 4), "peak_kind": f"of {peak_kind}"},
-            "allreduce_error": err, "clocks": sampler.summary(t0, t1)}
+            "allreduce_error": err, **(checked or {}), "clocks": sampler.summary(t0, t1)}
 
 
 def tp_line(label: str, r: dict, steps: int, warmup: int) -> dict:

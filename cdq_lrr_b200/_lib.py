@@ -20,6 +20,7 @@ STATUS = {
 MAX_BATCH = 64
 MAX_COLS = 65536
 MAX_JOBS = 192  # jobs per grouped launch (the launch record fits the kernel-parameter space)
+QUANT_NO_TOPK_GUARD = 1  # CDQ_QUANT_NO_TOPK_GUARD
 
 
 class CdqError(RuntimeError):
@@ -82,6 +83,8 @@ _SIGS = {
     "cdq_allreduce_f32": (C.c_int, [C.POINTER(C.c_void_p), C.c_int32, C.c_int32, C.c_int64, C.c_void_p,
                                     C.c_int64, C.c_void_p]),
     "cdq_ar_error": (C.c_int, [C.POINTER(C.c_int32)]),
+    "cdq_ar_clear_error": (C.c_int, []),
+    "cdq_ar_set_spin_limit": (C.c_int, [C.c_int64]),
     "cdq_pack_from_reference_device": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, C.c_int64,
                                                  C.POINTER(cdq_packed), _P, _P]),
     "cdq_file_checkpoints": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), C.c_int32, _P, _P]),
@@ -97,6 +100,12 @@ _SIGS = {
     "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                C.POINTER(cdq_packed), _P, _P, C.c_size_t, _P]),
+    "cdq_quantize_ex": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double, C.c_int32, C.c_int64,
+                                  C.POINTER(cdq_packed), _P, _P, C.c_size_t, _P]),
+    "cdq_pack_tile_indices": (C.c_int, [_P, C.c_int64, C.c_int32, _P]),
+    "cdq_unpack_tile_indices": (C.c_int, [_P, C.c_int64, C.c_int32, _P]),
+    "cdq_pack_residual_stream": (C.c_int, [_P, _P, C.c_int64, _P]),
+    "cdq_unpack_residual_stream": (C.c_int, [_P, C.c_int64, _P, _P]),
     "cdq_host_from_reference": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P,
                                           C.c_int64, C.POINTER(cdq_packed)]),
     "cdq_host_to_reference": (C.c_int, [C.POINTER(cdq_packed), _P, _P, _P, _P]),

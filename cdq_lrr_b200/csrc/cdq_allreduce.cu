@@ -30,9 +30,10 @@ namespace {
 constexpr int kArBlocks = CDQ_AR_BLOCKS;
 constexpr int kArMaxRanks = CDQ_AR_MAX_RANKS;
 constexpr int kArThreads = 512;
-constexpr uint32_t kArSpinLimit = 1u << 24;  // polls of a flag before a wait gives up
+constexpr uint32_t kArSpinLimit = 1u << 24;  // default polls of a flag before a wait gives up
 
 __device__ int g_ar_error;
+uint32_t g_ar_spin_limit = kArSpinLimit;  // process-wide, set by cdq_ar_set_spin_limit
 
 struct ArArgs {
     float* stage[kArMaxRanks];     // each rank's staging buffers (2 x cap floats)
@@ -40,6 +41,7 @@ struct ArArgs {
     uint32_t* epoch;               // this rank's epoch counters [block]
     int64_t cap;
     int world, rank;
+    uint32_t spin_limit;
 };
 
 // Region layout: staging 2 * cap floats | pad kArBlocks * kArMaxRanks words | epochs kArBlocks words
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(kArThreads) ar_kernel(const ArArgs a, float* _
         const uint32_t* flag = a.pad[a.rank] + c * kArMaxRanks + tid;
         uint32_t spin = 0;
         while ((int32_t)(ld_acquire_sys(flag) - e) < 0) {
-            if (++spin == kArSpinLimit) {
+            if (++spin >= a.spin_limit) {
                 s_ok = 0;
                 atomicExch(&g_ar_error, 1);
                 break;
@@ -171,6 +173,7 @@ cdq_status cdq_allreduce_f32(void* const* regions, int32_t world, int32_t rank, 
     a.cap = cap;
     a.world = world;
     a.rank = rank;
+    a.spin_limit = g_ar_spin_limit;
     // always kArBlocks blocks: the blocks' epochs advance together, so one call
     // uses one staging parity throughout, whatever slice a block covers
     ar_kernel<<<kArBlocks, kArThreads, 0, (cudaStream_t)stream>>>(a, data, n);
@@ -182,6 +185,17 @@ cdq_status cdq_ar_error(int32_t* code) {
     int v = 0;
     if (cdq::ar_read_error(&v) != cudaSuccess) return CDQ_ERR_CUDA;
     *code = v;
+    return CDQ_OK;
+}
+
+cdq_status cdq_ar_clear_error(void) {
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_ar_error, &zero, sizeof zero) == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_ar_set_spin_limit(int64_t polls) {
+    if (polls < 1 || polls > (int64_t)UINT32_MAX) return CDQ_ERR_ARG;
+    g_ar_spin_limit = (uint32_t)polls;
     return CDQ_OK;
 }
 

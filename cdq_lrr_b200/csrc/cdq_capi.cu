@@ -103,6 +103,42 @@ cdq_status linear_common(const cdq_packed* w, const uint16_t* x, int64_t m, void
     return e == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }
 
+cdq_status quantize_common(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states, double stc_frac,
+                           int32_t flags, int64_t res_capacity, cdq_packed* out, cdq_quant_info* info,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    int sms = 0;
+    cdq_status st = device_setup(&sms);
+    if (st) return st;
+    cdq_sizes sz;
+    st = cdq_get_sizes(rows, cols, n_states, stc_frac, 1, &sz);
+    if (st) return st;
+    if (flags & ~CDQ_QUANT_NO_TOPK_GUARD) return CDQ_ERR_ARG;
+    if (!w || !aligned(w, 16) || !out || !info || !out->units || !out->res_ptr || !out->res_ent ||
+        !out->res_q || !aligned(out->units, 16) || !aligned(out->res_ptr, 4) ||
+        !aligned(out->res_ent, 4) || !aligned(info, 8) || res_capacity < 0)
+        return CDQ_ERR_ARG;
+    if (!workspace || (int64_t)workspace_bytes < sz.quantize_workspace_bytes ||
+        !aligned(workspace, 256))
+        return CDQ_ERR_WORKSPACE;
+    QuantArgs a;
+    a.w = w;
+    a.rows = rows;
+    a.cols = cols;
+    a.n_states = n_states;
+    a.stc_frac = stc_frac;
+    a.no_guard = (flags & CDQ_QUANT_NO_TOPK_GUARD) ? 1 : 0;
+    a.res_cap = res_capacity;
+    a.out = *out;
+    a.out.rows = rows;
+    a.out.cols = cols;
+    a.out.n_states = n_states;
+    a.info = info;
+    a.ws = reinterpret_cast<uint8_t*>(workspace);
+    a.ws_bytes = workspace_bytes;
+    cudaError_t e = quantize_launch(a, (cudaStream_t)stream, sms);
+    return e == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
 }  // namespace
 
 extern "C" {
@@ -173,38 +209,18 @@ cdq_status cdq_dequant(const cdq_packed* w, uint16_t* w_hat, void* stream) {
 cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
                         double stc_frac, cdq_packed* out, cdq_quant_info* info, void* workspace,
                         size_t workspace_bytes, void* stream) {
-    int sms = 0;
-    cdq_status st = device_setup(&sms);
-    if (st) return st;
     cdq_sizes sz;
-    st = cdq_get_sizes(rows, cols, n_states, stc_frac, 1, &sz);
+    cdq_status st = cdq_get_sizes(rows, cols, n_states, stc_frac, 1, &sz);
     if (st) return st;
-    if (!w || !aligned(w, 16) || !out || !info || !out->units || !out->res_ptr || !out->res_ent ||
-        !out->res_q || !aligned(out->units, 16) || !aligned(out->res_ptr, 4) ||
-        !aligned(out->res_ent, 4) || !aligned(info, 8))
-        return CDQ_ERR_ARG;
-    if (!workspace || (int64_t)workspace_bytes < sz.quantize_workspace_bytes ||
-        !aligned(workspace, 256))
-        return CDQ_ERR_WORKSPACE;
-    QuantArgs a;
-    a.w = w;
-    a.rows = rows;
-    a.cols = cols;
-    a.n_states = n_states;
-    a.stc_frac = stc_frac;
-    a.out = *out;
-    a.out.rows = rows;
-    a.out.cols = cols;
-    a.out.n_states = n_states;
-    a.info = info;
-    a.ws = reinterpret_cast<uint8_t*>(workspace);
-    a.ws_bytes = workspace_bytes;
-    cudaError_t e = quantize_launch(a, (cudaStream_t)stream, sms);
-    if (e != cudaSuccess) return CDQ_ERR_CUDA;
-    out->rows = rows;
-    out->cols = cols;
-    out->n_states = n_states;
-    return CDQ_OK;
+    return quantize_common(w, rows, cols, n_states, stc_frac, 0, sz.max_res, out, info, workspace,
+                           workspace_bytes, stream);
+}
+
+cdq_status cdq_quantize_ex(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
+                           double stc_frac, int32_t flags, int64_t res_capacity, cdq_packed* out,
+                           cdq_quant_info* info, void* workspace, size_t workspace_bytes, void* stream) {
+    return quantize_common(w, rows, cols, n_states, stc_frac, flags, res_capacity, out, info, workspace,
+                           workspace_bytes, stream);
 }
 
 cdq_status cdq_set_tile_min_batch(int32_t m) {

@@ -402,6 +402,42 @@ cdq_status cdq_file_decode(const uint8_t* data, int64_t len, int32_t n_states,
     return n == t->n_res ? CDQ_OK : CDQ_ERR_FORMAT;
 }
 
+cdq_status cdq_pack_tile_indices(const uint8_t* q, int64_t n_tiles, int32_t n_states, uint8_t* out) {
+    if (n_states != 26 && n_states != 16) return CDQ_ERR_STATES;
+    if (n_tiles < 0 || (n_tiles && (!q || !out))) return CDQ_ERR_ARG;
+    const int ib = idx_bytes(n_states);
+    for (int64_t t = 0; t < n_tiles; ++t) pack_indices(q + t * 32, n_states, out + t * ib);
+    return CDQ_OK;
+}
+
+cdq_status cdq_unpack_tile_indices(const uint8_t* packed, int64_t n_tiles, int32_t n_states, uint8_t* q) {
+    if (n_states != 26 && n_states != 16) return CDQ_ERR_STATES;
+    if (n_tiles < 0 || (n_tiles && (!q || !packed))) return CDQ_ERR_ARG;
+    const int ib = idx_bytes(n_states);
+    for (int64_t t = 0; t < n_tiles; ++t) unpack_indices(packed + t * ib, n_states, q + t * 32);
+    return CDQ_OK;
+}
+
+cdq_status cdq_pack_residual_stream(const uint8_t* offsets, const uint16_t* values, int64_t count, uint8_t* out) {
+    if (count < 0 || (count && (!offsets || !values || !out))) return CDQ_ERR_ARG;
+    memset(out, 0, (size_t)blob_bytes(count));
+    for (int64_t i = 0; i < count; ++i) {
+        put_bits(out, 21 * i, offsets[i] & 0x1Fu, 5);
+        put_bits(out, 21 * i + 5, values[i], 16);
+    }
+    return CDQ_OK;
+}
+
+cdq_status cdq_unpack_residual_stream(const uint8_t* packed, int64_t count, uint8_t* offsets, uint16_t* values) {
+    if (count < 0 || (count && (!offsets || !values || !packed))) return CDQ_ERR_ARG;
+    const int64_t nb = blob_bytes(count);
+    for (int64_t i = 0; i < count; ++i) {
+        offsets[i] = (uint8_t)get_bits(packed, nb, 21 * i, 5);
+        values[i] = (uint16_t)get_bits(packed, nb, 21 * i + 5, 16);
+    }
+    return CDQ_OK;
+}
+
 cdq_status cdq_file_encode_header(int32_t n_states, int32_t n_tensors, uint8_t* out, int64_t cap,
                                   int64_t* written) {
     if (!written || n_tensors < 0 || n_tensors > 0xFFFF) return CDQ_ERR_ARG;

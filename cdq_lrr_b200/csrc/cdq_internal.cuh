@@ -61,6 +61,8 @@ struct QuantArgs {
     const uint16_t* w;
     int32_t rows, cols, n_states;
     double stc_frac;
+    int32_t no_guard;  // 1: no top-k tie guard (the packer CLI's quantizer)
+    int64_t res_cap;   // residual entries the output buffers hold
     cdq_packed out;
     cdq_quant_info* info;
     uint8_t* ws;

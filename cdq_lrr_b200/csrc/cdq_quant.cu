@@ -308,9 +308,9 @@ __global__ void k_count(const uint16_t* __restrict__ w, int32_t rows, int32_t co
     if (!fallback_pass && total) atomicAdd(&ws.st->mask_count, total);
 }
 
-__global__ void k_decide(WS ws, unsigned long long n, unsigned long long k) {
+__global__ void k_decide(WS ws, unsigned long long n, unsigned long long k, int guard) {
     QState* st = ws.st;
-    if (st->mask_count > 2ull * k) {
+    if (guard && st->mask_count > 2ull * k) {
         st->fallback = 1u;
         st->rank[2] = n - k;  // ascending rank of the k-th largest
     }
@@ -439,7 +439,7 @@ __global__ void k_pack_codes(const uint16_t* __restrict__ w, int32_t rows, int32
 // 6b. residual entries: one thread per bucket, columns in ascending order.
 template <int NS>
 __global__ void k_pack_res(const uint16_t* __restrict__ w, int32_t rows, int32_t cols,
-                           cdq_packed out, WS ws) {
+                           cdq_packed out, WS ws, int64_t res_cap) {
     const Geometry g = geometry(rows, cols, NS);
     const int64_t nb = g.r16 * g.kg * 16;
     const Rule rule = make_rule(ws.st);
@@ -461,8 +461,10 @@ __global__ void k_pack_res(const uint16_t* __restrict__ w, int32_t rows, int32_t
             while (m) {
                 const int e = __ffs(m) - 1;
                 m &= m - 1;
-                out.res_ent[pos] = ((uint32_t)(c * 32 + e) << 16) | wt[e];
-                out.res_q[pos] = (uint8_t)snap<NS>(x[e], sq);
+                if ((int64_t)pos < res_cap) {  // beyond it only the count is reported
+                    out.res_ent[pos] = ((uint32_t)(c * 32 + e) << 16) | wt[e];
+                    out.res_q[pos] = (uint8_t)snap<NS>(x[e], sq);
+                }
                 ++pos;
             }
         }
@@ -524,7 +526,7 @@ cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
     k_find<2><<<1, 256, 0, s>>>(3u, 0, ws);
     k_threshold<<<1, 1, 0, s>>>(ws, weight);
     k_count<<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.n_states, a.out.res_ptr, ws, 0);
-    k_decide<<<1, 1, 0, s>>>(ws, (unsigned long long)numel, k);
+    k_decide<<<1, 1, 0, s>>>(ws, (unsigned long long)numel, k, a.no_guard ? 0 : 1);
     // top-k fallback (each kernel returns at once unless the tie guard fired)
     k_hist<0><<<tile_blocks, threads, 0, s>>>(a.w, n_tiles, 4u, 1, ws);
     k_find<0><<<1, 256, 0, s>>>(4u, 1, ws);
@@ -542,10 +544,10 @@ cudaError_t quantize_launch(const QuantArgs& a, cudaStream_t s, int sms) {
     const int code_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((lanes + threads - 1) / threads, (int64_t)sms * 16));
     if (a.n_states == 26) {
         k_pack_codes<26><<<code_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
-        k_pack_res<26><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+        k_pack_res<26><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws, a.res_cap);
     } else {
         k_pack_codes<16><<<code_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
-        k_pack_res<16><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws);
+        k_pack_res<16><<<bucket_blocks, threads, 0, s>>>(a.w, a.rows, a.cols, a.out, ws, a.res_cap);
     }
     k_info<<<1, 1, 0, s>>>(ws, a.out.res_ptr, nb, a.info, k);
     return cudaGetLastError();

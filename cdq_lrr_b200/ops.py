@@ -338,24 +338,32 @@ def dequant(pack: DevicePack) -> torch.Tensor:
     return out
 
 
-def quantize(w: torch.Tensor, n_states: int = 26, stc_frac: float = 0.0156
-             ) -> tuple[DevicePack, dict]:
-    """GPU tile quantizer: bf16 [rows, cols] CUDA tensor -> (device pack, info)."""
+def quantize(w: torch.Tensor, n_states: int = 26, stc_frac: float = 0.0156,
+             topk_guard: bool = True) -> tuple[DevicePack, dict]:
+    """GPU tile quantizer: bf16 [rows, cols] CUDA tensor -> (device pack, info).
+
+    topk_guard=False quantizes as the reference packer CLI does
+    (code/cdq_pack.py:279-291, no top-k tie guard): up to every weight can
+    become a residual, so the residual buffers are sized for rows * cols."""
     _require_cuda(w, "cdq quantize")
     if w.dim() != 2:
         raise ValueError(f"expected 2D, got {tuple(w.shape)}")
     rows, cols = w.shape
     w = w.detach().to(torch.bfloat16).contiguous()
     s = L.sizes(rows, cols, n_states, stc_frac)
-    pack = DevicePack.empty(rows, cols, n_states, s.max_res, w.device)
+    cap = s.max_res if topk_guard else rows * cols
+    pack = DevicePack.empty(rows, cols, n_states, cap, w.device)
     ws = torch.empty(s.quantize_workspace_bytes, dtype=torch.uint8, device=w.device)
     info_t = torch.zeros(C.sizeof(L.cdq_quant_info), dtype=torch.uint8, device=w.device)
     st = pack.struct()
-    L.check(L.lib().cdq_quantize(_vp(w), rows, cols, n_states, stc_frac, C.byref(st), _vp(info_t),
-                                 _vp(ws), ws.numel(), _stream(w.device)), "cdq_quantize")
+    flags = 0 if topk_guard else L.QUANT_NO_TOPK_GUARD
+    L.check(L.lib().cdq_quantize_ex(_vp(w), rows, cols, n_states, stc_frac, flags, cap, C.byref(st),
+                                    _vp(info_t), _vp(ws), ws.numel(), _stream(w.device)), "cdq_quantize_ex")
     raw = bytes(info_t.cpu().numpy().tobytes())
     info = L.cdq_quant_info.from_buffer_copy(raw)
     pack.n_res = int(info.n_res)
+    if pack.n_res > cap:
+        raise L.CdqError(6, "cdq_quantize_ex: residual buffers too small")
     # release the unused residual capacity
     pack.res_ent = pack.res_ent[: pack.n_res].clone()
     pack.res_q = pack.res_q[: pack.n_res].clone()

@@ -12,8 +12,9 @@ accepts tensors given as flat residual lists (``residual_indices`` /
 Python loop, and ``read_device_packs`` returns device packs directly.
 
 The CLI quantises on the GPU with the top-k tie guard of
-quantize_cdq_lrr; the reference CLI's inline quantiser (:283-291) has no
-guard, so the two differ only on tensors where the guard fires.
+quantize_cdq_lrr by default; ``--no-topk-guard`` quantises exactly as the
+reference CLI's inline quantiser (:279-291), which has no guard (the two
+differ only on tensors where the guard fires).
 """
 from __future__ import annotations
 
@@ -34,63 +35,86 @@ IDX_BYTES_PER_TILE = 20
 NIBBLE_BYTES_PER_TILE = 16
 
 
+def _c_u8(a) -> np.ndarray:
+    if isinstance(a, torch.Tensor):
+        a = a.detach().cpu().numpy()
+    return np.ascontiguousarray(np.asarray(a)).astype(np.uint8, copy=False).reshape(-1)
+
+
+def _tile_indices(q32, n_states: int) -> bytes:
+    q = _c_u8(q32)
+    assert q.size == 32
+    out = np.empty(20 if n_states == 26 else 16, dtype=np.uint8)
+    L.check(L.lib().cdq_pack_tile_indices(q.ctypes.data_as(C.c_void_p), 1, n_states,
+                                          out.ctypes.data_as(C.c_void_p)), "cdq_pack_tile_indices")
+    return out.tobytes()
+
+
+def _tile_unpack(buf: bytes, n_states: int) -> torch.Tensor:
+    assert len(buf) == (20 if n_states == 26 else 16)
+    src = np.frombuffer(bytes(buf), dtype=np.uint8)
+    q = np.empty(32, dtype=np.uint8)
+    L.check(L.lib().cdq_unpack_tile_indices(src.ctypes.data_as(C.c_void_p), 1, n_states,
+                                            q.ctypes.data_as(C.c_void_p)), "cdq_unpack_tile_indices")
+    return torch.from_numpy(q)
+
+
 def pack_5bit_row(q32) -> bytes:
-    q = [int(v) for v in (q32.tolist() if hasattr(q32, "tolist") else q32)]
-    assert len(q) == 32
-    acc = 0
-    for i, v in enumerate(q):
-        acc |= (v & 0x1F) << (5 * i)
-    return acc.to_bytes(20, "little")
+    """32 indices (0..25) -> 20 bytes, 5 bits each, LSB first (code/cdq_pack.py:50-56)."""
+    return _tile_indices(q32, 26)
 
 
 def unpack_5bit_row(buf: bytes) -> torch.Tensor:
-    assert len(buf) == 20
-    acc = int.from_bytes(buf, "little")
-    return torch.tensor([(acc >> (5 * i)) & 0x1F for i in range(32)], dtype=torch.uint8)
+    """20 bytes -> 32 indices (code/cdq_pack.py:59-64)."""
+    return _tile_unpack(buf, 26)
 
 
 def pack_indices_nibble(indices_32) -> bytes:
-    q = torch.as_tensor(indices_32).to(torch.uint8)
-    assert q.numel() == 32
-    return bytes((((q[1::2] & 0x0F) << 4) | (q[0::2] & 0x0F)).tolist())
+    """32 indices (0..15) -> 16 bytes, even index in the low nibble (code/cdq_pack.py:67-78)."""
+    return _tile_indices(indices_32, 16)
 
 
 def unpack_nibble_row(buf: bytes) -> torch.Tensor:
-    assert len(buf) == 16
-    out = torch.empty(32, dtype=torch.uint8)
-    for i, b in enumerate(buf):
-        out[2 * i] = b & 0x0F
-        out[2 * i + 1] = (b >> 4) & 0x0F
-    return out
+    """16 bytes -> 32 indices (code/cdq_pack.py:81-88)."""
+    return _tile_unpack(buf, 16)
+
+
+def _bf16_bits(values) -> np.ndarray:
+    if isinstance(values, torch.Tensor):
+        v = values.detach().cpu()
+        if v.dtype != torch.bfloat16:
+            v = v.to(torch.bfloat16)
+        return np.ascontiguousarray(v.view(torch.int16).numpy().view(np.uint16)).reshape(-1)
+    return np.ascontiguousarray(np.asarray(values, dtype=np.uint16)).reshape(-1)
 
 
 def pack_residuals(offsets, values_bf16) -> bytes:
-    offs = torch.as_tensor(offsets).tolist()
-    if len(offs) == 0:
+    """Residuals of one tile -> ceil(21 R / 8) bytes: per residual a 5-bit
+    offset then the 16 bf16 bits, LSB first (code/cdq_pack.py:91-105)."""
+    offs = _c_u8(offsets)
+    vals = _bf16_bits(values_bf16)
+    assert offs.size == vals.size
+    if offs.size == 0:
         return b""
-    vals = torch.as_tensor(values_bf16).to(torch.bfloat16).view(torch.int16).tolist()
-    acc, pos = 0, 0
-    for o, v in zip(offs, vals):
-        acc |= (int(o) & 0x1F) << pos
-        pos += 5
-        acc |= (int(v) & 0xFFFF) << pos
-        pos += 16
-    return acc.to_bytes((pos + 7) // 8, "little")
+    out = np.empty((21 * offs.size + 7) // 8, dtype=np.uint8)
+    L.check(L.lib().cdq_pack_residual_stream(offs.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p),
+                                             offs.size, out.ctypes.data_as(C.c_void_p)), "cdq_pack_residual_stream")
+    return out.tobytes()
 
 
 def unpack_residuals(buf: bytes, tag_count: int):
+    """(offsets uint8 [R], values bf16 [R]) of one tile's residual stream
+    (code/cdq_pack.py:108-119)."""
     if tag_count == 0:
         return torch.empty(0, dtype=torch.uint8), torch.empty(0, dtype=torch.bfloat16)
-    acc = int.from_bytes(buf, "little")
-    offs = torch.empty(tag_count, dtype=torch.uint8)
-    raw = torch.empty(tag_count, dtype=torch.int32)
-    pos = 0
-    for i in range(tag_count):
-        offs[i] = (acc >> pos) & 0x1F
-        pos += 5
-        raw[i] = (acc >> pos) & 0xFFFF
-        pos += 16
-    return offs, raw.to(torch.int16).view(torch.bfloat16)
+    src = np.frombuffer(bytes(buf), dtype=np.uint8)
+    assert src.size >= (21 * tag_count + 7) // 8
+    offs = np.empty(tag_count, dtype=np.uint8)
+    vals = np.empty(tag_count, dtype=np.uint16)
+    L.check(L.lib().cdq_unpack_residual_stream(src.ctypes.data_as(C.c_void_p), tag_count,
+                                               offs.ctypes.data_as(C.c_void_p), vals.ctypes.data_as(C.c_void_p)),
+            "cdq_unpack_residual_stream")
+    return torch.from_numpy(offs), torch.from_numpy(vals.view(np.int16)).view(torch.bfloat16)
 
 
 def _u8(a) -> np.ndarray:
@@ -118,15 +142,14 @@ def _flat_residuals(t: dict) -> tuple[np.ndarray, np.ndarray]:
     ri, rv = [], []
     for ti, (tc, blob) in enumerate(zip(tags.tolist(), t["res_blobs"])):
         if tc:
-            acc = int.from_bytes(blob, "little")
-            pos = 0
-            for _ in range(tc):
-                ri.append(ti * TILE + ((acc >> pos) & 0x1F))
-                pos += 5
-                rv.append((acc >> pos) & 0xFFFF)
-                pos += 16
-    order = np.argsort(np.asarray(ri, dtype=np.int64), kind="stable")
-    return (np.asarray(ri, dtype=np.int64)[order], np.asarray(rv, dtype=np.uint16)[order])
+            o, v = unpack_residuals(blob, tc)
+            ri.append(ti * TILE + o.numpy().astype(np.int64))
+            rv.append(v.view(torch.int16).numpy().view(np.uint16))
+    if not ri:
+        return np.empty(0, dtype=np.int64), np.empty(0, dtype=np.uint16)
+    ri_a, rv_a = np.concatenate(ri), np.concatenate(rv)
+    order = np.argsort(ri_a, kind="stable")
+    return ri_a[order], rv_a[order]
 
 
 def encode_cdq(tensors: dict, n_states: int = 26) -> bytes:
@@ -292,7 +315,7 @@ def dequant_tile(q32, scale_bf16, res_blob, tag_count, lattice=None):
     return w
 
 
-def main():
+def main(argv=None):
     import argparse
     import os
     import time
@@ -303,7 +326,10 @@ def main():
     ap.add_argument("--max-tensors", type=int, default=-1, help="-1 = all")
     ap.add_argument("--states", type=int, choices=(26, 16), default=16)
     ap.add_argument("--stc-frac", type=float, default=0.0156)
-    args = ap.parse_args()
+    ap.add_argument("--no-topk-guard", action="store_true",
+                    help="quantize exactly as the reference packer CLI (no top-k tie guard, "
+                         "code/cdq_pack.py:279-291); by default the guard of quantize_cdq_lrr applies")
+    args = ap.parse_args(argv)
     from safetensors import safe_open
     f = safe_open(os.path.join(args.model, "model.safetensors"), framework="pt")
     keys = [k for k in f.keys() if k.endswith(".weight") and any(
@@ -316,7 +342,8 @@ def main():
     tensors, tot_w, tot_res = {}, 0, 0
     for k in keys:
         w = f.get_tensor(k).to(torch.bfloat16).cuda()
-        pack, info = quantize(w, n_states=args.states, stc_frac=args.stc_frac)
+        pack, info = quantize(w, n_states=args.states, stc_frac=args.stc_frac,
+                              topk_guard=not args.no_topk_guard)
         ref = pack.to_reference()
         rows, cols = w.shape
         tensors[k] = {"rows": rows, "cols": cols, "q": ref["quant_indices"],

@@ -18,8 +18,9 @@ materialises w_hat. Differences from the reference, all deliberate:
 
 * only the two built-in lattices are accepted (the kernels carry their bf16
   tables); any other ``lattice`` raises ValueError;
-* the returned dict also carries ``"device_pack"``, the packed weight in the
-  device layout, so CDQLinear does not repack it;
+* the returned dict has exactly the reference's keys; the packed weight in
+  the device layout it was built from is remembered alongside (keyed by the
+  dict's quant_indices tensor), so CDQLinear does not repack it;
 * CDQLinear stores the device pack as its buffers (``units``,
   ``res_ptr``, ``res_ent``, ``res_q``); the reference buffer names
   (``quant_indices``, ``scales_f8``, ``scales_bf16``, ``residual_indices``,
@@ -88,9 +89,9 @@ def quantize_cdq_lrr(weight: torch.Tensor, chunk_tiles: int = 8192, lattice=None
                      stc_frac: float | None = None) -> dict:
     """Full CDQ-LRR quantisation of a 2-D weight on the GPU.
 
-    Returns the reference's dict (CPU tensors, code/cdq_lrr_qwen05.py:121-133)
-    plus ``device_pack``. ``chunk_tiles`` is accepted for signature
-    compatibility; the GPU quantizer needs no chunking.
+    Returns the reference's dict (CPU tensors, code/cdq_lrr_qwen05.py:121-133:
+    the same keys, types, dtypes and shapes). ``chunk_tiles`` is accepted for
+    signature compatibility; the GPU quantizer needs no chunking.
     """
     assert weight.dim() == 2, f"expected 2D, got {weight.shape}"
     n_states = _n_states_of(lattice)
@@ -104,7 +105,7 @@ def quantize_cdq_lrr(weight: torch.Tensor, chunk_tiles: int = 8192, lattice=None
     n_tiles = pack.n_tiles
     scales_u8 = torch.from_numpy(ref["scales_f8"]).view(n_tiles, 1)
     scales_f8 = scales_u8.view(FP8_DTYPE)
-    return {
+    out = {
         "quant_indices": torch.from_numpy(ref["quant_indices"]),
         "scales_f8": scales_f8,
         "scales_bf16": scales_f8.to(torch.bfloat16),
@@ -116,12 +117,28 @@ def quantize_cdq_lrr(weight: torch.Tensor, chunk_tiles: int = 8192, lattice=None
         "n_tiles": int(n_tiles),
         "lattice": _lattice_of(n_states).clone(),
         "n_states": n_states,
-        "device_pack": pack,
     }
+    _remember(out["quant_indices"], pack)
+    return out
+
+
+# The device pack a quantize_cdq_lrr dict was built from, keyed by the dict's
+# quant_indices tensor (held weakly), so that CDQLinear(pack, ...) and
+# dequantize(pack) reuse it instead of uploading the arrays again. The dict
+# itself keeps exactly the reference's keys.
+_PACKS: dict[int, tuple] = {}
+
+
+def _remember(key: torch.Tensor, dp: ops.DevicePack) -> None:
+    import weakref
+    k = id(key)
+    _PACKS[k] = (weakref.ref(key), dp)
+    weakref.finalize(key, _PACKS.pop, k, None)
 
 
 def _device_pack_of(pack: dict, device=None) -> ops.DevicePack:
-    dp = pack.get("device_pack")
+    entry = _PACKS.get(id(pack["quant_indices"]))
+    dp = entry[1] if entry is not None and entry[0]() is pack["quant_indices"] else None
     if dp is None:
         rows, cols = pack["orig_shape"]
         n_states = _n_states_of(pack.get("lattice"))

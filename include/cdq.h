@@ -118,16 +118,26 @@ CDQ_API const char* cdq_version(void);
  * y[M, rows] = x[M, cols] * w_hat^T (+ bias), fused: the packed weight is
  * streamed from HBM and dequantized in registers (bit-exact w_hat pairs fed
  * to the tensor cores), FP32 accumulation, result rounded once to bf16.
- * M <= CDQ_MAX_BATCH.
- * workspace: linear_workspace_bytes of device memory; no zeroing needed, every
- * call writes what it reads. Streaming path (M below the tile threshold, or a
- * launch with too few 128-row tiles to fill the GPU): two launches, the
- * streaming pass writes float32 sums per residual group to the workspace and
- * a fix-up pass adds the groups, the residual entries and the bias. tcgen05
- * tile path: two launches, a small one that lays out the activations in the
- * workspace, then the tile kernel, whose epilogue adds the residual entries
- * and the bias. Calls that share one workspace must not overlap on the GPU.
- * bias may be NULL. x, y, bias: bf16 bit patterns, row-major.
+ * M <= CDQ_MAX_BATCH. bias may be NULL. x, y, bias: bf16 bit patterns,
+ * row-major.
+ * workspace: linear_workspace_bytes of device memory. Its first
+ * ceil(R16 * 4 / 256) * 256 bytes hold one arrival counter per 16-row block:
+ * they must be zero before the first call (zero-fill a new workspace once),
+ * and every completed call leaves them zero again; the rest needs no
+ * initialisation. After a call that recorded a kernel error
+ * (cdq_kernel_error), zero the workspace again. Calls that share one
+ * workspace must not overlap on the GPU.
+ * Paths: M <= 8, two launches: a residual pre-pass (the sum of every
+ * (row, residual group) bucket, bf16 value x activation in fp32, entries in
+ * order) and the streaming kernel, which adds each group's mma sum to its
+ * residual sum, sums the groups of a row in order (in registers, or through
+ * the workspace and the counters where a warp's work boundary cuts a row
+ * block) and adds the bias. M = 9..64 on the streaming path: the pre-pass,
+ * the wide streaming kernel and a fix-up launch that adds the groups; same
+ * arithmetic per output, so a row's result does not depend on the batch it
+ * is computed in. M >= the tile threshold with enough 128-row tiles: the
+ * tcgen05 tile path, two launches (activation layout, tile kernel whose
+ * epilogue adds the residual entries and the bias).
  * Replaces CDQLinear.forward, code/cdq_lrr_qwen05.py:196-198, and the
  * loader's CDQLinear.forward, code/cdq_loader.py:53-58.
  */
@@ -144,14 +154,18 @@ CDQ_API cdq_status cdq_linear_f32(const cdq_packed* w, const uint16_t* x, int64_
  * As cdq_linear (bf16 output), for callers that cannot allocate device
  * memory: a plugin whose host process owns all device memory through its own
  * pool, or a path where a cudaMalloc, which may synchronise the device, is
- * not allowed. It allocates nothing and takes no workspace: its partial-sum
- * scratch is a 4 MiB array that the library holds on every GPU that loads it,
- * until the process exits. Weights whose scratch would exceed 4 MiB
- * (m * ceil(cols/1024) * ceil(rows/16) * 64 bytes, rounded up to 256) are
- * rejected with CDQ_ERR_WORKSPACE. All calls share the one array: calls that overlap on the
- * GPU race, so issue them on one stream. The first call on a device sets up
- * the scratch address and lattice tables (host-side runtime calls); make it
- * before any stream capture.
+ * not allowed. It allocates nothing and takes no workspace: its scratch (the
+ * row-block counters and per-group sums of the streaming paths) is a 4 MiB
+ * array that the library holds on every GPU that loads it, until the process
+ * exits. Weights whose scratch would exceed 4 MiB (ceil(rows/16) * 4 bytes
+ * rounded up to 256, plus m * ceil(cols/1024) * ceil(rows/16) * 64 bytes
+ * rounded up to 256) are rejected with CDQ_ERR_WORKSPACE. Always the
+ * streaming paths (no tcgen05 tile path), any m <= CDQ_MAX_BATCH. All calls
+ * share the one array: calls that overlap on the GPU race, so issue them on
+ * one stream. The first call on a device sets up the scratch address and
+ * lattice tables (host-side runtime calls); make it before any stream
+ * capture. The address is remembered per device ordinal, so it does not
+ * survive a cudaDeviceReset of that device within the process.
  * No counterpart in the reference.
  */
 CDQ_API cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x, int64_t m,
@@ -184,16 +198,19 @@ CDQ_API cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64
  * M = 128 side of a tensor-core mma with tensor-memory accumulators, the
  * batch its N side, padded to 16, 32 or 64); smaller batches take the
  * streaming mma.sync path. Default 16; a value above CDQ_MAX_BATCH turns the
- * tile path off. Both paths write the same per-group sums and share the
- * fix-up pass. Not thread-safe against concurrent calls of the linear entry
- * points. No counterpart in the reference.
+ * tile path off. The tile path adds a row's products in its own order (one
+ * tensor-memory accumulator over the whole row, then the row's residual
+ * entries), so its outputs differ from the streaming path's in the last
+ * bits. Not thread-safe against concurrent calls of the linear entry points.
+ * No counterpart in the reference.
  */
 CDQ_API cdq_status cdq_set_tile_min_batch(int32_t m);
 
 /*
  * The sticky in-kernel error code of the fused linear on the current device
  * (0: none; 1: shared-memory window misplaced; 2: a weight copy never landed
- * within the wait limit; 3: a tile-path pipeline wait gave up). A kernel that
+ * within the wait limit; 3: a tile-path pipeline wait gave up; 4: a residual
+ * pre-pass copy never landed within the wait limit). A kernel that
  * records an error leaves its outputs incomplete but returns normally, so the
  * context stays usable. Reads after a device synchronisation; does not reset.
  */
@@ -227,8 +244,17 @@ CDQ_API cdq_status cdq_ar_destroy(void* region);
 CDQ_API cdq_status cdq_allreduce_f32(void* const* regions, int32_t world, int32_t rank, int64_t cap,
                                      float* data, int64_t n, void* stream);
 /* Sticky error code of the all-reduce on the current device (0: none; 1: a
- * peer's flag did not arrive within the wait limit). Does not reset. */
+ * peer's flag did not arrive within the wait limit). Reading does not reset
+ * it; cdq_ar_clear_error does. After error 1 the ranks' epochs and staging
+ * parities are out of step: every rank must destroy its region and create a
+ * new one (zeroed pads and epochs) and exchange handles again before the
+ * next cdq_allreduce_f32. */
 CDQ_API cdq_status cdq_ar_error(int32_t* code);
+CDQ_API cdq_status cdq_ar_clear_error(void);
+/* Polls of a peer's flag before a wait gives up (process-wide, read at each
+ * cdq_allreduce_f32 call; default 2^24, 1 <= polls < 2^32). A short limit
+ * lets a test see the give-up path without a peer. */
+CDQ_API cdq_status cdq_ar_set_spin_limit(int64_t polls);
 
 /*
  * Device-side ingest of a reference-format pack: q [rows*cols/32][32] lattice
@@ -316,6 +342,45 @@ typedef struct cdq_quant_info {
 CDQ_API cdq_status cdq_quantize(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
                                 double stc_frac, cdq_packed* out, cdq_quant_info* info,
                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * cdq_quantize with options. flags: 0, or CDQ_QUANT_NO_TOPK_GUARD to quantize
+ * as the reference packer CLI does (code/cdq_pack.py:279-291: the same steps
+ * without the top-k tie guard of code/cdq_lrr_qwen05.py:93-96, so every weight
+ * whose saliency reaches the threshold becomes a residual; that can be every
+ * weight, e.g. an all-zero tensor). res_capacity: the residual entries
+ * out->res_ent / out->res_q hold (cdq_get_sizes' max_res suffices with the
+ * guard; rows * cols always suffices). Entries beyond the capacity are not
+ * written; info->n_res always reports the full count, so n_res > res_capacity
+ * means the pack is incomplete and the call must be repeated with larger
+ * buffers.
+ */
+#define CDQ_QUANT_NO_TOPK_GUARD 1
+CDQ_API cdq_status cdq_quantize_ex(const uint16_t* w, int32_t rows, int32_t cols, int32_t n_states,
+                                   double stc_frac, int32_t flags, int64_t res_capacity, cdq_packed* out,
+                                   cdq_quant_info* info, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/*
+ * Bit packers of the .cdq tile records (host memory, n_tiles tiles or count
+ * residuals per call), byte-exact with the reference's:
+ *   cdq_pack_tile_indices / cdq_unpack_tile_indices: q [n_tiles][32] <-> 20
+ *     bytes per tile (26 states: 5 bits per index, LSB first; pack_5bit_row /
+ *     unpack_5bit_row, code/cdq_pack.py:50-64) or 16 (16 states: two indices
+ *     per byte, the even one in the low nibble; pack_indices_nibble /
+ *     unpack_nibble_row, code/cdq_pack.py:67-81). Indices are masked to 5 or
+ *     4 bits.
+ *   cdq_pack_residual_stream / cdq_unpack_residual_stream: count residuals of
+ *     one tile <-> ceil(21 * count / 8) bytes, each a 5-bit offset then the
+ *     16 bf16 bits, LSB first (pack_residuals / unpack_residuals,
+ *     code/cdq_pack.py:84-119).
+ */
+CDQ_API cdq_status cdq_pack_tile_indices(const uint8_t* q, int64_t n_tiles, int32_t n_states, uint8_t* out);
+CDQ_API cdq_status cdq_unpack_tile_indices(const uint8_t* packed, int64_t n_tiles, int32_t n_states, uint8_t* q);
+CDQ_API cdq_status cdq_pack_residual_stream(const uint8_t* offsets, const uint16_t* values, int64_t count,
+                                            uint8_t* out);
+CDQ_API cdq_status cdq_unpack_residual_stream(const uint8_t* packed, int64_t count, uint8_t* offsets,
+                                              uint16_t* values);
 
 /*
  * Host-side conversions between the reference's pack tensors and the device

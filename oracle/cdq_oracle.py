@@ -206,8 +206,12 @@ def quantile_linear(values: np.ndarray, q: float) -> np.float32:
 
 
 def quantize(w_bits: np.ndarray, n_states: int = 26, stc_frac: float | None = None,
-             chunk_tiles: int = 16384) -> dict:
+             chunk_tiles: int = 16384, topk_guard: bool = True) -> dict:
     """Restates quantize_cdq_lrr (code/cdq_lrr_qwen05.py:63-133).
+
+    ``topk_guard=False`` restates the packer CLI's inline quantizer instead
+    (code/cdq_pack.py:279-291): the same steps without the top-k tie guard,
+    so every weight whose saliency reaches the threshold is a residual.
 
     ``w_bits``: uint16 bf16 bits [rows, cols], cols % 32 == 0. Returns numpy
     arrays with the reference pack's keys (bf16 tensors as uint16 bits, fp8 as
@@ -244,7 +248,7 @@ def quantize(w_bits: np.ndarray, n_states: int = 26, stc_frac: float | None = No
     thr = quantile_linear(sal, 1.0 - stc_frac)
     mask = sal >= thr
     topk_fallback = False
-    if int(mask.sum()) > 2 * k:
+    if topk_guard and int(mask.sum()) > 2 * k:
         # torch.topk's choice among equal values is implementation defined;
         # torch 2.11 on CPU takes the lowest flat indices, restated here.
         topk_fallback = True

@@ -1,8 +1,8 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a container where the reference source tree is mounted (default
-/root/reference, override with CDQ_REFERENCE). It imports the reference's own
-Python modules and records what they return:
+Run where the reference source tree is available, with CDQ_REFERENCE set to
+its root (the directory holding code/). It imports the reference's own Python
+modules and records what they return:
 
 * code/cdq_lrr_qwen05.py: CAMKII_LATTICE / CAMKII_LATTICE_16,
   fp8_quantize_scale, quantize_cdq_lrr, dequantize, CDQLinear.forward;
@@ -15,7 +15,12 @@ digests of the reference's arrays plus a few scalars. Outputs go next to this
 script: golden.npz, digests.json and *.cdq files. The weights come from
 cdq_lrr_b200.synth (torch CPU generator, deterministic across machines).
 
-    python tests/golden/make_golden.py
+    CDQ_REFERENCE=<reference root> python tests/golden/make_golden.py [--extras]
+
+``--extras`` only adds to the existing fixtures: the packer CLI's file for a
+checkpoint on which quantize_cdq_lrr's top-k tie guard fires (the CLI has no
+guard: cli_noguard_26.cdq) and the key / type / dtype / shape record of the
+quantize_cdq_lrr dict ("pack_dict" in digests.json).
 """
 from __future__ import annotations
 
@@ -33,7 +38,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
-REF = Path(os.environ.get("CDQ_REFERENCE", "/root/reference")) / "code"
+if not os.environ.get("CDQ_REFERENCE"):
+    raise SystemExit("set CDQ_REFERENCE to the reference source tree (the directory holding code/)")
+REF = Path(os.environ["CDQ_REFERENCE"]) / "code"
 sys.path.insert(0, str(REF))
 
 import cdq_lrr_qwen05 as R  # noqa: E402
@@ -260,5 +267,35 @@ def main() -> None:
     print("wrote", HERE / "golden.npz", sum(v.nbytes for v in out.values()), "raw bytes")
 
 
+def extras() -> None:
+    """The packer CLI on tensors where the top-k tie guard fires, and the pack
+    dict's structure, added to the existing fixtures."""
+    meta = json.loads((HERE / "digests.json").read_text())
+    with tempfile.TemporaryDirectory() as td:
+        from safetensors.torch import save_file
+        tensors, names = {}, []
+        for i, nm in enumerate(["zeros", "constant", "small26"]):
+            w, _, _ = weight_case(nm)
+            key = f"model.layers.{i}.mlp.up_proj.weight"
+            tensors[key] = w.contiguous()
+            names.append((key, nm))
+        save_file(tensors, os.path.join(td, "model.safetensors"))
+        dst = HERE / "cli_noguard_26.cdq"
+        subprocess.run([sys.executable, str(REF / "cdq_pack.py"), "--model", td, "--out", str(dst),
+                        "--states", "26"], check=True, capture_output=True)
+        meta["cli_noguard_tensors"] = names
+    w, ns, frac = weight_case("small26")
+    pack = R.quantize_cdq_lrr(w, lattice=lattice_of(ns), stc_frac=frac)
+    spec = {}
+    for k, v in pack.items():
+        if isinstance(v, torch.Tensor):
+            spec[k] = {"type": "tensor", "dtype": str(v.dtype).replace("torch.", ""), "shape": list(v.shape)}
+        else:
+            spec[k] = {"type": type(v).__name__, "value": list(v) if isinstance(v, (tuple, torch.Size)) else v}
+    meta["pack_dict"] = {"case": "small26", "keys": spec}
+    (HERE / "digests.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
+    print("wrote", dst, "and pack_dict")
+
+
 if __name__ == "__main__":
-    main()
+    extras() if "--extras" in sys.argv else main()

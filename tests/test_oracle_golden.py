@@ -155,3 +155,22 @@ def test_projection_4864x896_digests(golden, golden_meta, ns):
     y64 = O.linear_f64(what, x)
     yref = O.bf16_bits_to_f32(golden[f"cfg1_{ns}.y1"]).astype(np.float64)
     assert np.all(np.abs(y64 - yref) <= 2.0 ** -7 * np.abs(y64) + 1e-30)
+
+
+def test_oracle_without_guard_reproduces_reference_cli(golden, golden_meta):
+    """The packer CLI quantizes without quantize_cdq_lrr's top-k tie guard
+    (code/cdq_pack.py:279-291). On a checkpoint where the guard would fire (an
+    all-zero and a constant tensor: every saliency ties), the oracle's
+    guard-free restatement plus its writer reproduce the reference CLI's file
+    byte for byte; with the guard the zero and constant tensors differ."""
+    from pathlib import Path
+    data = (Path(__file__).parent / "golden" / "cli_noguard_26.cdq").read_bytes()
+    tensors, differs = [], []
+    for key, nm in golden_meta["cli_noguard_tensors"]:
+        w = golden[f"{nm}.weight"]
+        p = O.quantize(w, n_states=26, stc_frac=0.0156, topk_guard=False)
+        tensors.append((key, p))
+        g = O.quantize(w, n_states=26, stc_frac=0.0156)
+        differs.append(bool(g["topk_fallback"]) and g["outlier_count"] != p["outlier_count"])
+    assert O.write_cdq(tensors, 26) == data
+    assert differs == [True, True, False]

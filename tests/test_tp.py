@@ -199,12 +199,19 @@ def test_oneshot_allreduce_two_ranks():
     for pr in procs:
         pr.start()
     res = {}
-    for _ in range(world):
-        rank, outs, err = q.get(timeout=240)
-        res[rank] = (outs, err)
-    for pr in procs:
-        pr.join(timeout=60)
-        assert pr.exitcode == 0
+    try:
+        for _ in range(world):
+            rank, outs, err = q.get(timeout=240)
+            res[rank] = (outs, err)
+        for pr in procs:
+            pr.join(timeout=60)
+            assert pr.exitcode == 0
+    finally:
+        # a rank that died or hangs must not outlive the test holding GPU IPC regions
+        for pr in procs:
+            if pr.is_alive():
+                pr.terminate()
+                pr.join(timeout=30)
     for it, n in enumerate((7, 3584, 65536, 3584, 1)):
         parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * it + r)).numpy() for r in range(world)]
         ref = np.float32(0) + parts[0]
@@ -215,3 +222,38 @@ def test_oneshot_allreduce_two_ranks():
     for r in range(world):
         assert np.all(res[r][0][-1] == sum(range(1, world + 1)))
         assert res[r][1] == 0
+
+
+@pytest.mark.gpu
+def test_oneshot_allreduce_peer_wait_gives_up():
+    """Failure detection without a fault: rank 0 of a two-rank all-reduce whose
+    peer never arrives (the second region is never driven by anyone). With a
+    short poll limit the flag wait gives up, the call records error 1 and the
+    data keeps this rank's own partial; the context stays usable."""
+    import ctypes as C
+    from cdq_lrr_b200 import _lib as L
+    lib = L.lib()
+    cap = 4096
+    regions = (C.c_void_p * 2)()
+    handles = [L.cdq_ipc_handle(), L.cdq_ipc_handle()]
+    for i in range(2):
+        p = C.c_void_p()
+        L.check(lib.cdq_ar_create(cap, C.byref(p), C.byref(handles[i])), "cdq_ar_create")
+        regions[i] = p.value
+    L.check(lib.cdq_ar_clear_error(), "cdq_ar_clear_error")
+    L.check(lib.cdq_ar_set_spin_limit(1 << 12), "cdq_ar_set_spin_limit")
+    try:
+        y = torch.randn(cap, device="cuda")
+        ref = y.clone()
+        L.check(lib.cdq_allreduce_f32(regions, 2, 0, cap, C.c_void_p(y.data_ptr()), cap,
+                                      C.c_void_p(torch.cuda.current_stream().cuda_stream)), "cdq_allreduce_f32")
+        torch.cuda.synchronize()
+        assert L.ar_error() == 1
+        assert torch.equal(y, ref)
+        z = torch.ones(8, device="cuda") * 2  # the context still works
+        assert float(z.sum()) == 16.0
+    finally:
+        L.check(lib.cdq_ar_set_spin_limit(1 << 24), "cdq_ar_set_spin_limit")
+        L.check(lib.cdq_ar_clear_error(), "cdq_ar_clear_error")
+        for i in range(2):
+            L.check(lib.cdq_ar_destroy(C.c_void_p(regions[i])), "cdq_ar_destroy")
