@@ -291,11 +291,14 @@ def random_pack(rows: int, cols: int, seed: int, device, stc_frac: float = 0.015
     return ops.DevicePack.from_reference(q, scales, ridx, rval, rows, cols, n_states, device=device)
 
 
-def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
+def run_decode(new_tokens: int, prompt_len: int = 128, alg_per_weight: float | None = None) -> dict:
     """Batch-1 greedy decode of the full Qwen2.5-0.5B-architecture model
     (random init, 168 CDQ-26 projections through the fused GEMV, bf16 tied
-    lm_head), static KV cache, one-token step replayed from a CUDA graph."""
+    lm_head), static KV cache, one-token step replayed from a CUDA graph; and
+    the bytes a token reads (alg_per_weight: the workload's algorithmic bytes
+    per projection weight, from the GEMV measurement)."""
     import torch
+    from cdq_lrr_b200.synth import QWEN05
     from cdq_lrr_b200 import decode
     model = decode.build_model(seed=0, device="cuda")
     decode.patch_cdq(model)
@@ -313,13 +316,30 @@ def run_decode(new_tokens: int, prompt_len: int = 128) -> dict:
     decode.patch_cdq(model, lattice=CAMKII_LATTICE_16)
     decode.fused_greedy_decode(model, ids, 8)
     d16 = decode.fused_greedy_decode(model, ids, new_tokens)
+    # bytes a token must read: the 168 projections' reference records (and their
+    # activations and outputs), the tied bf16 lm_head, the KV cache at the mean
+    # position of the run, one embedding row
+    cfg = QWEN05
+    proj = sum(rows * cols for _, rows, cols in layer_list())
+    proj_bytes = int(round(proj * alg_per_weight)) if alg_per_weight else None
+    lm_bytes = cfg["vocab"] * cfg["hidden"] * 2
+    mean_pos = prompt_len + new_tokens / 2
+    kv_bytes = int(cfg["layers"] * cfg["kv_heads"] * cfg["head_dim"] * 2 * 2 * mean_pos)
+    tok_bytes = (proj_bytes or 0) + lm_bytes + kv_bytes + cfg["hidden"] * 2
+    peak, peak_kind = measured_peak()
     out = {"tokens_per_s": round(r["tokens_per_s"], 2),
            "ms_per_token": round(r["decode_ms_per_token"], 4),
+           "bytes_per_token": tok_bytes,
+           "bytes_per_token_parts": {"projections": proj_bytes, "lm_head_bf16": lm_bytes, "kv_cache": kv_bytes},
+           "roofline": {"bound": "hbm", "achieved_gb_s": round(tok_bytes * r["tokens_per_s"] / 1e9, 2),
+                        "peak": peak, "frac": round(tok_bytes * r["tokens_per_s"] / 1e9 / peak, 4),
+                        "peak_kind": f"of {peak_kind}"},
            "prefill_ms": round(r["prefill_ms"], 3), "prompt_tokens": prompt_len,
            "new_tokens": new_tokens, "cuda_graph": r["graphed"],
-           "step": "fused decode step (library RMSNorm, rotary + cache append + GQA attention, SiLU-mul "
-                   "kernels around grouped CDQ projections; torch embedding, lm_head GEMV, argmax), "
-                   "token and position advanced on the device, one CUDA graph per token",
+           "step": "fused decode step, library kernels only: embedding + RMSNorm, per layer add + RMSNorm, "
+                   "grouped CDQ projections, rotary + cache append + GQA attention, SiLU-mul; lm_head GEMV "
+                   "with fused argmax; token and position advanced on the device; one CUDA graph per token, "
+                   "launches programmatically dependent",
            "hf_step_tokens_per_s": round(h["tokens_per_s"], 2),
            "draft_tier_16_state_tokens_per_s": round(d16["tokens_per_s"], 2),
            "hf_step": "the same model through HF's Qwen2 forward (CDQ projections patched in), CUDA graph",
@@ -512,7 +532,9 @@ def run_ours(args) -> None:
 
     dec = None
     if rank == 0 and ws_ == 1 and args.decode_tokens > 0:
-        dec = run_decode(args.decode_tokens)
+        n_weights = sum(r * c for _, r, c in layer_list())
+        dec = run_decode(args.decode_tokens, alg_per_weight=(alg_bytes - sum(t.x.numel() * 2 + t.y.numel() * 2
+                                                                             for t in tasks)) / n_weights)
 
     if rank == 0:
         line = {

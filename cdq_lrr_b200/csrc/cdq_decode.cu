@@ -11,13 +11,29 @@
 //                positions 0..pos (fp32 scores, softmax and weighted sum, one
 //                bf16 rounding of the output);
 //   silu_mul     out = bf16(bf16(silu(g)) * u) (Qwen2MLP's act_fn(gate) * up);
+//   embed_rmsnorm  h = embedding row of the step's token, then add_rmsnorm's
+//                norm (the first layer's input norm);
+//   lm_head_argmax  logits = bf16(x . w_row) for every vocabulary row (the tied
+//                bf16 lm_head GEMV, fp32 accumulation) and their argmax (first
+//                index among equal values, NaN above everything, torch.argmax's
+//                rule) folded into one 64-bit key per step;
 //   advance      the step's greedy token becomes the next step's input, is
 //                recorded, and the position moves on, all on the device, so a
 //                CUDA graph of the whole step replays without the host.
+// Every kernel is launched programmatically dependent on its predecessor: it
+// waits for the predecessor's completion before touching data, then lets its
+// own successor be scheduled, so launch latencies overlap execution.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "cdq.h"
+#include "cdq_internal.cuh"
+
+using cdq::launch_pdl;
+using cdq::pdl_release;
+using cdq::pdl_wait;
 
 namespace {
 
@@ -32,6 +48,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __r
                                                                    const uint16_t* __restrict__ w, float eps,
                                                                    uint16_t* __restrict__ out, int n) {
     __shared__ float red[kNormThreads / 32];
+    pdl_wait();
+    pdl_release();
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += kNormThreads) {
         float v = bf(h[i]);
@@ -64,6 +82,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     extern __shared__ float scores[];
     __shared__ float qe[kHd], ke[kHd], ve[kHd], red[kAttnThreads / 32], part[kHd];
     const int h = blockIdx.x, tid = threadIdx.x;
+    pdl_wait();
+    pdl_release();
     const int group = n_heads / n_kv, kvh = h / group;
     const int P = *pos_p;
     if (P < 0 || P >= max_len || P >= cap) return;  // the host sizes the cache; nothing to attend otherwise
@@ -140,6 +160,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
 
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
                                 uint16_t* __restrict__ out, int n) {
+    pdl_wait();
+    pdl_release();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float x = bf(g[i]);
         out[i] = tobf(rbf(x / (1.f + expf(-x))) * bf(u[i]));
@@ -149,11 +171,117 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* 
 __global__ void advance_kernel(const int64_t* __restrict__ next, int64_t* __restrict__ ids,
                                int64_t* __restrict__ tokens, int32_t* __restrict__ pos, int32_t* __restrict__ count,
                                int cap) {
+    pdl_wait();
+    pdl_release();
     const int c = *count;
     if (c < cap) tokens[c] = *next;
     *ids = *next;
     *pos += 1;
     *count = c + 1;
+}
+
+// The argmax key of a bf16 logit: orderable bits of the value (NaN above
+// every number) above the complemented index (the first index wins ties).
+__device__ __forceinline__ unsigned long long argmax_key(uint16_t v, uint32_t idx) {
+    uint32_t b = v == 0x8000u ? 0u : v;                 // -0 equals +0
+    if ((b & 0x7FFFu) > 0x7F80u) b = 0xFFFFu;           // every NaN: the largest key
+    else b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - idx);
+}
+
+__global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int64_t* __restrict__ ids,
+                                                                     const uint16_t* __restrict__ table,
+                                                                     int64_t vocab, uint16_t* __restrict__ h,
+                                                                     const uint16_t* __restrict__ w, float eps,
+                                                                     uint16_t* __restrict__ out, int n) {
+    __shared__ float red[kNormThreads / 32];
+    pdl_wait();
+    pdl_release();
+    const int64_t id = *ids;
+    const bool ok = id >= 0 && id < vocab;  // an out-of-range id gives a zero row
+    const uint16_t* row = table + (ok ? id : 0) * (int64_t)n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += kNormThreads) {
+        const uint16_t v = ok ? row[i] : (uint16_t)0;
+        h[i] = v;
+        ss = fmaf(bf(v), bf(v), ss);
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int k = 0; k < kNormThreads / 32; ++k) tot += red[k];
+    const float r = rsqrtf(tot / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += kNormThreads) out[i] = tobf(bf(w[i]) * rbf(bf(h[i]) * r));
+}
+
+constexpr int kLmThreads = 256;
+constexpr int kLmRows = 4;  // rows per warp step (loads in flight)
+
+// logits[r] = bf16(sum_k x[k] * w[r][k]) (fp32, lane-chunk order then a warp
+// reduction), and the step's argmax key (atomicMax of argmax_key, which the
+// advance kernel reads and clears). x is staged in shared memory as fp32.
+__global__ void __launch_bounds__(kLmThreads) lm_head_argmax_kernel(const uint16_t* __restrict__ w,
+                                                                    const uint16_t* __restrict__ x, int vocab,
+                                                                    int n, uint16_t* __restrict__ logits,
+                                                                    unsigned long long* __restrict__ best) {
+    extern __shared__ float xs[];
+    pdl_wait();
+    pdl_release();
+    for (int i = threadIdx.x; i < n; i += kLmThreads) xs[i] = bf(x[i]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nch = n / 8;  // 16-byte chunks per row
+    const int64_t nw = (int64_t)gridDim.x * (kLmThreads / 32);
+    unsigned long long key = 0ull;
+    for (int64_t r0 = ((int64_t)blockIdx.x * (kLmThreads / 32) + warp) * kLmRows; r0 < vocab; r0 += nw * kLmRows) {
+        float acc[kLmRows];
+#pragma unroll
+        for (int t = 0; t < kLmRows; ++t) acc[t] = 0.f;
+        for (int ch = lane; ch < nch; ch += 32) {
+            uint4 u[kLmRows];
+#pragma unroll
+            for (int t = 0; t < kLmRows; ++t)
+                u[t] = r0 + t < vocab ? __ldcs(reinterpret_cast<const uint4*>(w + (r0 + t) * (int64_t)n) + ch)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+            const float4 xa = *reinterpret_cast<const float4*>(xs + 8 * ch);
+            const float4 xb = *reinterpret_cast<const float4*>(xs + 8 * ch + 4);
+#pragma unroll
+            for (int t = 0; t < kLmRows; ++t) {
+                float a = acc[t];
+                a = fmaf(__uint_as_float(u[t].x << 16), xa.x, a);
+                a = fmaf(__uint_as_float(u[t].x & 0xFFFF0000u), xa.y, a);
+                a = fmaf(__uint_as_float(u[t].y << 16), xa.z, a);
+                a = fmaf(__uint_as_float(u[t].y & 0xFFFF0000u), xa.w, a);
+                a = fmaf(__uint_as_float(u[t].z << 16), xb.x, a);
+                a = fmaf(__uint_as_float(u[t].z & 0xFFFF0000u), xb.y, a);
+                a = fmaf(__uint_as_float(u[t].w << 16), xb.z, a);
+                a = fmaf(__uint_as_float(u[t].w & 0xFFFF0000u), xb.w, a);
+                acc[t] = a;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kLmRows; ++t) {
+            float a = acc[t];
+            for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+            if (r0 + t < vocab) {
+                const uint16_t v = tobf(a);
+                if (lane == 0 && logits) logits[r0 + t] = v;
+                const unsigned long long k = argmax_key(v, (uint32_t)(r0 + t));
+                key = k > key ? k : key;
+            }
+        }
+    }
+    if (lane == 0 && key) atomicMax(best, key);
+}
+
+// The argmax key -> the step's token, then the key is cleared for the next step.
+__global__ void argmax_token_kernel(unsigned long long* __restrict__ best, int64_t* __restrict__ next) {
+    pdl_wait();
+    pdl_release();
+    const unsigned long long k = *best;
+    *next = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    *best = 0ull;
 }
 
 }  // namespace
@@ -163,8 +291,10 @@ extern "C" {
 cdq_status cdq_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps, uint16_t* out,
                            int32_t n, void* stream) {
     if (!h || !w || !out || n < 1) return CDQ_ERR_ARG;
-    add_rmsnorm_kernel<<<1, kNormThreads, 0, (cudaStream_t)stream>>>(h, delta, w, eps, out, n);
-    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    return launch_pdl(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, (cudaStream_t)stream, h, delta, w, eps,
+                      out, n) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
 }
 
 cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* cos_t,
@@ -179,23 +309,58 @@ cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const uint16_t*
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return CDQ_ERR_CUDA;
-    attn_decode_kernel<<<n_heads, kAttnThreads, smem, (cudaStream_t)stream>>>(
-        q, k, v, cos_t, sin_t, pos, k_cache, v_cache, max_len, n_heads, n_kv, scale, out, max_len);
-    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    return launch_pdl(attn_decode_kernel, dim3(n_heads), dim3(kAttnThreads), (size_t)smem, (cudaStream_t)stream, q,
+                      k, v, cos_t, sin_t, pos, k_cache, v_cache, (int)max_len, (int)n_heads, (int)n_kv, scale, out,
+                      (int)max_len) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
 }
 
 cdq_status cdq_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n, void* stream) {
     if (!g || !u || !out || n < 1 || n > ((int64_t)1 << 30)) return CDQ_ERR_ARG;
     const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
-    silu_mul_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(g, u, out, (int)n);
-    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    return launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, g, u, out, (int)n) ==
+                   cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
 }
 
 cdq_status cdq_decode_advance(const int64_t* next, int64_t* ids, int64_t* tokens, int32_t* pos, int32_t* count,
                               int32_t cap, void* stream) {
     if (!next || !ids || !tokens || !pos || !count || cap < 1) return CDQ_ERR_ARG;
-    advance_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(next, ids, tokens, pos, count, cap);
-    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    return launch_pdl(advance_kernel, dim3(1), dim3(1), 0, (cudaStream_t)stream, next, ids, tokens, pos, count,
+                      (int)cap) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_embed_rmsnorm(const int64_t* ids, const uint16_t* table, int64_t vocab, uint16_t* h,
+                             const uint16_t* w, float eps, uint16_t* out, int32_t n, void* stream) {
+    if (!ids || !table || vocab < 1 || !h || !w || !out || n < 1) return CDQ_ERR_ARG;
+    return launch_pdl(embed_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, (cudaStream_t)stream, ids, table, vocab,
+                      h, w, eps, out, (int)n) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_lm_head_argmax(const uint16_t* w, const uint16_t* x, int32_t vocab, int32_t n, uint16_t* logits,
+                              uint64_t* best, int64_t* next, void* stream) {
+    if (!w || !x || !best || !next || vocab < 1 || n < 8 || n % 8 || n > 16384) return CDQ_ERR_ARG;
+    if ((uintptr_t)w % 16 || (uintptr_t)best % 8) return CDQ_ERR_ARG;
+    int sms = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return CDQ_ERR_CUDA;
+    const int64_t rows_per_block = (kLmThreads / 32) * kLmRows;
+    const int blocks = (int)std::min<int64_t>((vocab + rows_per_block - 1) / rows_per_block, (int64_t)sms * 8);
+    const size_t smem = (size_t)n * 4;
+    if (launch_pdl(lm_head_argmax_kernel, dim3(blocks), dim3(kLmThreads), smem, (cudaStream_t)stream, w, x, (int)vocab,
+                   (int)n, logits, reinterpret_cast<unsigned long long*>(best)) != cudaSuccess)
+        return CDQ_ERR_CUDA;
+    return launch_pdl(argmax_token_kernel, dim3(1), dim3(1), 0, (cudaStream_t)stream,
+                      reinterpret_cast<unsigned long long*>(best), next) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
 }
 
 }  // extern "C"

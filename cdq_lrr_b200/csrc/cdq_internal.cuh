@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "cdq.h"
 #include "cdq_common.cuh"
 
@@ -42,6 +44,30 @@ struct GemvBatch {
     int64_t total_units;       // units of every job of the launch (streaming kernel)
     GemvJob jobs[MAXJ];
 };
+
+// Launch with programmatic stream serialization: the kernel may start while
+// its predecessor on the stream is still running; it must execute
+// griddepcontrol.wait before it reads anything that predecessor writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Device side of a programmatic launch: wait for the predecessor's completion
+// (and its memory), then let the successor be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 cudaError_t upload_lattices();
 // allow_tile: the launch may take the tcgen05 tile path (the jobs' workspaces

@@ -126,6 +126,11 @@ __host__ __device__ constexpr int res_smem_bytes(int cols) { return 16 + (kResCa
 
 template <int MAXJ>
 __global__ void __launch_bounds__(kResThreads) res_sum_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    // the streaming kernel may be scheduled now (it waits for this grid's
+    // completion before it reads any residual sum); this grid itself waits
+    // for the kernel that wrote the activations
+    pdl_release();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t rsm[];
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(rsm);
     uint32_t* const ent = reinterpret_cast<uint32_t*>(rsm + 16);  // entry e of a chunk at e - (c0 & ~3)
@@ -213,8 +218,7 @@ cudaError_t launch_res(const GemvBatch<MAXJ>& b, int m, cudaStream_t stream) {
     auto kern = res_sum_kernel<MAXJ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, res_smem_bytes(CDQ_MAX_COLS));
     if (e != cudaSuccess) return e;
-    kern<<<(int)std::max<int64_t>(blocks, 1), kResThreads, smem, stream>>>(rb);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(kResThreads), (size_t)smem, stream, rb);
 }
 
 // floor(U * k / n) for U < 2^31 and k <= n < 2^16, without a 64-bit division:
@@ -366,6 +370,11 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     };
     produce(0);
     produce(1);
+    // The residual pre-pass is this launch's programmatic predecessor: the
+    // table set-up and the first copies above overlap it; its sums (and the
+    // workspace it shares with the cut row blocks) are read only after it has
+    // completed (a no-op when the launch has no such predecessor).
+    pdl_wait();
 
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t c_slot = 0, c_phase = 0;
@@ -529,8 +538,8 @@ cudaError_t launch(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sms) {
     e = launch_res(b, M, stream);
     if (e != cudaSuccess) return e;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, num_sms));
-    kern<<<grid, kSThreads, kSmemBytes, stream>>>(sb);
-    return cudaGetLastError();
+    // programmatic dependent launch: the kernel starts while the pre-pass runs
+    return launch_pdl(kern, dim3(grid), dim3(kSThreads), kSmemBytes, stream, sb);
 }
 
 }  // namespace stream

@@ -199,13 +199,15 @@ def greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool 
 
 class FusedDecoder:
     """Batch-1 greedy decoder whose one-token step runs on this library's
-    kernels only, plus torch's embedding gather, the tied bf16 lm_head GEMV
-    and argmax: per layer, the fused residual-add + RMSNorm, one grouped CDQ
-    launch for q/k/v (with their biases), the rotary embedding + cache append +
-    grouped-query attention kernel, o_proj, the second add + RMSNorm, one
-    grouped launch for gate/up, SiLU(gate) * up, down_proj. The step's token
-    and position live on the device (cdq_decode_advance), so one CUDA graph of
-    the step replays per token with no host work in between. Prefill runs the
+    kernels only: the embedding row with the first input norm; per layer, the
+    fused residual-add + RMSNorm, one grouped CDQ call for q/k/v (with their
+    biases), the rotary embedding + cache append + grouped-query attention
+    kernel, o_proj, the second add + RMSNorm, one grouped call for gate/up,
+    SiLU(gate) * up, down_proj; the final norm, the tied bf16 lm_head GEMV
+    with its argmax, and the token advance. The step's token and position live
+    on the device, so one CUDA graph of the step replays per token with no
+    host work in between; every launch is programmatically dependent on the
+    previous one, so launch latencies overlap. Prefill runs the
     HF model itself into the same static cache (the reference's forward,
     code/cdq_lrr_qwen05.py:300-330), whose [1, kv_heads, max_len, head_dim]
     tensors the attention kernel then reads and appends to."""
@@ -254,7 +256,12 @@ class FusedDecoder:
                 "down": ops.GroupedLinear([T(mlp.down_proj, self.act, self.dn)], m=1),
             })
         self.norm_w = model.model.norm.weight
-        self.lm_w = model.lm_head.weight
+        self.lm_w = model.lm_head.weight.contiguous()
+        self.embed_w = model.model.embed_tokens.weight.contiguous()
+        self.vocab = self.lm_w.shape[0]
+        self.logits = torch.zeros(1, self.vocab, dtype=bf16, device=dev)
+        self.best = z(1, torch.int64)   # the lm_head's argmax key (zero between steps)
+        self.next = z(1, torch.int64)
         self.graph = None
 
     def _call(self, name: str, *args) -> None:
@@ -263,11 +270,13 @@ class FusedDecoder:
     def _step(self) -> None:
         p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
         s = torch.cuda.current_stream(self.dev).cuda_stream
-        self.h.copy_(torch.nn.functional.embedding(self.ids, self.model.model.embed_tokens.weight)[0])
         for li, Ly in enumerate(self.layers):
             cl = self.cache.layers[li]
-            self._call("cdq_add_rmsnorm", p(self.h), p(self.dn) if li else None, p(Ly["ln1"]), self.eps,
-                       p(self.xn), self.H, s)
+            if li == 0:  # the token's embedding row and the first input norm
+                self._call("cdq_embed_rmsnorm", p(self.ids), p(self.embed_w), self.vocab, p(self.h), p(Ly["ln1"]),
+                           self.eps, p(self.xn), self.H, s)
+            else:
+                self._call("cdq_add_rmsnorm", p(self.h), p(self.dn), p(Ly["ln1"]), self.eps, p(self.xn), self.H, s)
             Ly["qkv"]()
             self._call("cdq_attn_decode", p(self.q), p(self.k), p(self.v), p(self.cos), p(self.sin), p(self.pos),
                        p(cl.keys), p(cl.values), self.max_len, self.n_heads, self.n_kv, self.hd,
@@ -278,9 +287,10 @@ class FusedDecoder:
             self._call("cdq_silu_mul", p(self.g), p(self.u), p(self.act), self.inter, s)
             Ly["down"]()
         self._call("cdq_add_rmsnorm", p(self.h), p(self.dn), p(self.norm_w), self.eps, p(self.xn), self.H, s)
-        self.logits = torch.nn.functional.linear(self.xn.view(1, -1), self.lm_w)
-        nxt = self.logits.argmax(-1)
-        self._call("cdq_decode_advance", p(nxt), p(self.ids), p(self.tokens), p(self.pos), p(self.count),
+        # the tied bf16 lm_head GEMV with its argmax fused in
+        self._call("cdq_lm_head_argmax", p(self.lm_w), p(self.xn), self.vocab, self.H, p(self.logits),
+                   p(self.best), p(self.next), s)
+        self._call("cdq_decode_advance", p(self.next), p(self.ids), p(self.tokens), p(self.pos), p(self.count),
                    self.max_len, s)
 
     @torch.no_grad()

@@ -310,6 +310,25 @@ CDQ_API cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const u
 CDQ_API cdq_status cdq_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n, void* stream);
 CDQ_API cdq_status cdq_decode_advance(const int64_t* next, int64_t* ids, int64_t* tokens, int32_t* pos,
                                       int32_t* count, int32_t cap, void* stream);
+/*
+ *   cdq_embed_rmsnorm: h = table[*ids] (embedding row, a zero row for an id
+ *     outside [0, vocab)), out = w * norm(h): the embedding lookup and the
+ *     first layer's input norm in one launch.
+ *   cdq_lm_head_argmax: logits[r] = bf16(x . w[r]) for the vocab rows of the
+ *     bf16 lm_head w [vocab][n] (fp32 accumulation; logits may be NULL), and
+ *     *next = their argmax (first index among equal values, NaN above every
+ *     number: torch.argmax on the bf16 logits). best: device uint64, zero
+ *     before the first call; the call leaves it zero. n % 8 == 0, n <= 16384.
+ *     Replaces the tied lm_head F.linear and argmax of the reference's greedy
+ *     generate (code/cdq_lrr_qwen05.py:335-340).
+ * All of these kernels, and the fused linear's, are launched programmatically
+ * dependent on their predecessor on the stream (each waits for it before
+ * touching data), so consecutive launches overlap their launch latency.
+ */
+CDQ_API cdq_status cdq_embed_rmsnorm(const int64_t* ids, const uint16_t* table, int64_t vocab, uint16_t* h,
+                                     const uint16_t* w, float eps, uint16_t* out, int32_t n, void* stream);
+CDQ_API cdq_status cdq_lm_head_argmax(const uint16_t* w, const uint16_t* x, int32_t vocab, int32_t n,
+                                      uint16_t* logits, uint64_t* best, int64_t* next, void* stream);
 
 /*
  * Bit-exact w_hat [rows, cols] bf16 from a device pack.

@@ -338,3 +338,71 @@ def test_per_layer_teacher_forced_cosine_0_9999(cdq_model, ref_model):
             worst = min(worst, cos)
             assert cos >= 0.9999, (i, cos)
     assert worst >= 0.9999
+
+
+def test_lm_head_argmax_kernel():
+    """The tied lm_head GEMV with its fused argmax: bf16 logits within one
+    rounding of torch's bf16 GEMV, the argmax equal to torch.argmax of the
+    kernel's own logits (first index among equal values; a NaN logit wins),
+    the key cleared after every call, rows not a multiple of the kernel's row
+    group."""
+    import ctypes as C
+    from cdq_lrr_b200 import _lib as L
+    lib = L.lib()
+    g = torch.Generator().manual_seed(5)
+    V, H = 5003, 896
+    w = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    x = torch.randn(H, generator=g).to(torch.bfloat16).cuda()
+    logits = torch.empty(V, dtype=torch.bfloat16, device="cuda")
+    best = torch.zeros(1, dtype=torch.int64, device="cuda")
+    nxt = torch.zeros(1, dtype=torch.int64, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        L.check(lib.cdq_lm_head_argmax(C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), V, H,
+                                       C.c_void_p(logits.data_ptr()), C.c_void_p(best.data_ptr()),
+                                       C.c_void_p(nxt.data_ptr()), C.c_void_p(s)), "cdq_lm_head_argmax")
+        torch.cuda.synchronize()
+
+    run()
+    ref = torch.nn.functional.linear(x.view(1, -1), w).float().view(-1)
+    got = logits.float()
+    assert torch.all((got - ref).abs() <= ref.abs() * 2 ** -7 + 1e-3)
+    assert int(nxt) == int(torch.argmax(logits))
+    assert int(best) == 0
+    # a tie at the maximum: the first of the equal rows wins
+    top = int(torch.argmax(logits))
+    with torch.no_grad():
+        w[V - 2].copy_(w[top])
+        w[3].copy_(w[top])
+    run()
+    assert int(nxt) == min(3, top)
+    # a NaN logit is the maximum
+    with torch.no_grad():
+        w[V - 1, 7] = float("nan")
+    run()
+    assert int(nxt) == V - 1 and int(best) == 0
+
+
+def test_embed_rmsnorm_kernel():
+    """Embedding row + the first input norm in one launch: the same bits as a
+    row copy followed by cdq_add_rmsnorm without a delta."""
+    import ctypes as C
+    from cdq_lrr_b200 import _lib as L
+    lib = L.lib()
+    g = torch.Generator().manual_seed(6)
+    V, H = 1000, 896
+    table = torch.randn(V, H, generator=g).to(torch.bfloat16).cuda()
+    wn = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda()
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for tok in (0, 17, V - 1):
+        ids = torch.tensor([tok], dtype=torch.int64, device="cuda")
+        h, out = torch.empty(H, dtype=torch.bfloat16, device="cuda"), torch.empty(H, dtype=torch.bfloat16, device="cuda")
+        L.check(lib.cdq_embed_rmsnorm(C.c_void_p(ids.data_ptr()), C.c_void_p(table.data_ptr()), V,
+                                      C.c_void_p(h.data_ptr()), C.c_void_p(wn.data_ptr()), 1e-6,
+                                      C.c_void_p(out.data_ptr()), H, s), "cdq_embed_rmsnorm")
+        h2, out2 = table[tok].clone(), torch.empty(H, dtype=torch.bfloat16, device="cuda")
+        L.check(lib.cdq_add_rmsnorm(C.c_void_p(h2.data_ptr()), None, C.c_void_p(wn.data_ptr()), 1e-6,
+                                    C.c_void_p(out2.data_ptr()), H, s), "cdq_add_rmsnorm")
+        torch.cuda.synchronize()
+        assert torch.equal(h, table[tok]) and torch.equal(out, out2)
