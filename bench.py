@@ -312,10 +312,26 @@ def run_decode(new_tokens: int, prompt_len: int = 128, alg_per_weight: float | N
     from cdq_lrr_b200.quant import CAMKII_LATTICE_16
     del model
     torch.cuda.empty_cache()
-    model = decode.build_model(seed=0, device="cuda")
-    decode.patch_cdq(model, lattice=CAMKII_LATTICE_16)
-    decode.fused_greedy_decode(model, ids, 8)
-    d16 = decode.fused_greedy_decode(model, ids, new_tokens)
+    draft = decode.build_model(seed=0, device="cuda")
+    decode.patch_cdq(draft, lattice=CAMKII_LATTICE_16)
+    decode.fused_greedy_decode(draft, ids, 8)
+    d16 = decode.fused_greedy_decode(draft, ids, new_tokens)
+    # speculative decoding: the 16-state tier drafts, the 26-state model verifies
+    target = decode.build_model(seed=0, device="cuda")
+    decode.patch_cdq(target)
+    spec = {}
+    runs = [("16_state_draft_k2", draft, 2), ("16_state_draft_k4", draft, 4),
+            ("self_draft_k4", target, 4)]  # self-draft: every proposal agrees (the loop's upper bound)
+    for tag, dm, k in runs:
+        sp = decode.speculative_greedy_decode(target, dm, ids, new_tokens, k=k)
+        spec[tag] = {"tokens_per_s": round(sp["tokens_per_s"], 2),
+                     "accepted_drafts_per_verify": round(sp["accepted_per_verify"], 3),
+                     "tokens_per_verify": round(sp["tokens_per_verify"], 3), "verifies": sp["verifies"],
+                     "verify_pass_ms": round(sp["verify_ms"], 4),
+                     "same_tokens_as_greedy": bool(torch.equal(sp["tokens"].view(-1).cpu(),
+                                                               r["tokens"].view(-1).cpu()))}
+    del target, draft
+    torch.cuda.empty_cache()
     # bytes a token must read: the 168 projections' reference records (and their
     # activations and outputs), the tied bf16 lm_head, the KV cache at the mean
     # position of the run, one embedding row
@@ -342,11 +358,16 @@ def run_decode(new_tokens: int, prompt_len: int = 128, alg_per_weight: float | N
                    "launches programmatically dependent",
            "hf_step_tokens_per_s": round(h["tokens_per_s"], 2),
            "draft_tier_16_state_tokens_per_s": round(d16["tokens_per_s"], 2),
+           "speculative": spec,
+           "speculative_note": "draft k tokens on the 16-state packs, verify k + 1 positions in one 26-state pass "
+                               "(grouped CDQ linears at m = k + 1, multi-query attention), keep the agreeing "
+                               "prefix plus the target's token; output identical to plain greedy. On this "
+                               "random-init model the 16-state and 26-state greedy choices over 151936 near-flat "
+                               "logits disagree, so drafts are rejected; the self-draft run shows the loop with "
+                               "every draft accepted",
            "hf_step": "the same model through HF's Qwen2 forward (CDQ projections patched in), CUDA graph",
            "model": "Qwen2.5-0.5B architecture, random init, 168 CDQ-26 projections, bf16 tied lm_head",
            "timing": "CUDA events around the decode loop (device time incl. host launch gaps)"}
-    del model
-    torch.cuda.empty_cache()
     return out
 
 

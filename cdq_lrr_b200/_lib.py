@@ -98,6 +98,11 @@ _SIGS = {
     "cdq_decode_advance": (C.c_int, [_P, _P, _P, _P, _P, C.c_int32, _P]),
     "cdq_embed_rmsnorm": (C.c_int, [_P, _P, C.c_int64, _P, _P, C.c_float, _P, C.c_int32, _P]),
     "cdq_lm_head_argmax": (C.c_int, [_P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
+    "cdq_add_rmsnorm_rows": (C.c_int, [_P, _P, _P, C.c_float, _P, C.c_int32, C.c_int32, _P]),
+    "cdq_embed_rmsnorm_rows": (C.c_int, [_P, _P, C.c_int64, _P, _P, C.c_float, _P, C.c_int32, C.c_int32, _P]),
+    "cdq_lm_head_argmax_rows": (C.c_int, [_P, _P, C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P]),
+    "cdq_attn_decode_multi": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32,
+                                        C.c_int32, C.c_float, _P, C.c_int32, _P]),
     "cdq_kernel_error": (C.c_int, [C.POINTER(C.c_int32)]),
     "cdq_dequant": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_quantize": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_double,

@@ -43,6 +43,7 @@ __device__ __forceinline__ float rbf(float v) { return bf(tobf(v)); }
 
 constexpr int kNormThreads = 256;
 
+// One block per row: row r of h / delta / out is the r-th vector of n values.
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __restrict__ h,
                                                                    const uint16_t* __restrict__ delta,
                                                                    const uint16_t* __restrict__ w, float eps,
@@ -50,6 +51,10 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __r
     __shared__ float red[kNormThreads / 32];
     pdl_wait();
     pdl_release();
+    const int64_t ro = (int64_t)blockIdx.x * n;
+    h += ro;
+    out += ro;
+    if (delta) delta += ro;
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += kNormThreads) {
         float v = bf(h[i]);
@@ -197,7 +202,10 @@ __global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int64
     __shared__ float red[kNormThreads / 32];
     pdl_wait();
     pdl_release();
-    const int64_t id = *ids;
+    const int64_t ro = (int64_t)blockIdx.x * n;
+    h += ro;
+    out += ro;
+    const int64_t id = ids[blockIdx.x];
     const bool ok = id >= 0 && id < vocab;  // an out-of-range id gives a zero row
     const uint16_t* row = table + (ok ? id : 0) * (int64_t)n;
     float ss = 0.f;
@@ -218,83 +226,207 @@ __global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int64
 constexpr int kLmThreads = 256;
 constexpr int kLmRows = 4;  // rows per warp step (loads in flight)
 
-// logits[r] = bf16(sum_k x[k] * w[r][k]) (fp32, lane-chunk order then a warp
-// reduction), and the step's argmax key (atomicMax of argmax_key, which the
-// advance kernel reads and clears). x is staged in shared memory as fp32.
+// For each of the M activation rows m: logits[m][r] = bf16(sum_k x[m][k] *
+// w[r][k]) (fp32, lane-chunk order then a warp reduction: the same
+// arithmetic for every M) and the row's argmax key (atomicMax into best[m],
+// which the token kernel reads and clears). x is staged in shared memory as
+// fp32.
+template <int M>
 __global__ void __launch_bounds__(kLmThreads) lm_head_argmax_kernel(const uint16_t* __restrict__ w,
                                                                     const uint16_t* __restrict__ x, int vocab,
                                                                     int n, uint16_t* __restrict__ logits,
                                                                     unsigned long long* __restrict__ best) {
-    extern __shared__ float xs[];
+    extern __shared__ float xs[];  // [M][n]
     pdl_wait();
     pdl_release();
-    for (int i = threadIdx.x; i < n; i += kLmThreads) xs[i] = bf(x[i]);
+    for (int i = threadIdx.x; i < M * n; i += kLmThreads) xs[i] = bf(x[i]);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nch = n / 8;  // 16-byte chunks per row
     const int64_t nw = (int64_t)gridDim.x * (kLmThreads / 32);
-    unsigned long long key = 0ull;
-    for (int64_t r0 = ((int64_t)blockIdx.x * (kLmThreads / 32) + warp) * kLmRows; r0 < vocab; r0 += nw * kLmRows) {
-        float acc[kLmRows];
+    unsigned long long key[M];
 #pragma unroll
-        for (int t = 0; t < kLmRows; ++t) acc[t] = 0.f;
+    for (int m = 0; m < M; ++m) key[m] = 0ull;
+    constexpr int kRows = M == 1 ? kLmRows : 1;  // vocabulary rows per warp step
+    for (int64_t r0 = ((int64_t)blockIdx.x * (kLmThreads / 32) + warp) * kRows; r0 < vocab; r0 += nw * kRows) {
+        float acc[kRows][M];
+#pragma unroll
+        for (int t = 0; t < kRows; ++t)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[t][m] = 0.f;
         for (int ch = lane; ch < nch; ch += 32) {
-            uint4 u[kLmRows];
+            uint4 u[kRows];
 #pragma unroll
-            for (int t = 0; t < kLmRows; ++t)
+            for (int t = 0; t < kRows; ++t)
                 u[t] = r0 + t < vocab ? __ldcs(reinterpret_cast<const uint4*>(w + (r0 + t) * (int64_t)n) + ch)
                                       : make_uint4(0u, 0u, 0u, 0u);
-            const float4 xa = *reinterpret_cast<const float4*>(xs + 8 * ch);
-            const float4 xb = *reinterpret_cast<const float4*>(xs + 8 * ch + 4);
 #pragma unroll
-            for (int t = 0; t < kLmRows; ++t) {
-                float a = acc[t];
-                a = fmaf(__uint_as_float(u[t].x << 16), xa.x, a);
-                a = fmaf(__uint_as_float(u[t].x & 0xFFFF0000u), xa.y, a);
-                a = fmaf(__uint_as_float(u[t].y << 16), xa.z, a);
-                a = fmaf(__uint_as_float(u[t].y & 0xFFFF0000u), xa.w, a);
-                a = fmaf(__uint_as_float(u[t].z << 16), xb.x, a);
-                a = fmaf(__uint_as_float(u[t].z & 0xFFFF0000u), xb.y, a);
-                a = fmaf(__uint_as_float(u[t].w << 16), xb.z, a);
-                a = fmaf(__uint_as_float(u[t].w & 0xFFFF0000u), xb.w, a);
-                acc[t] = a;
+            for (int m = 0; m < M; ++m) {
+                const float4 xa = *reinterpret_cast<const float4*>(xs + m * n + 8 * ch);
+                const float4 xb = *reinterpret_cast<const float4*>(xs + m * n + 8 * ch + 4);
+#pragma unroll
+                for (int t = 0; t < kRows; ++t) {
+                    float a = acc[t][m];
+                    a = fmaf(__uint_as_float(u[t].x << 16), xa.x, a);
+                    a = fmaf(__uint_as_float(u[t].x & 0xFFFF0000u), xa.y, a);
+                    a = fmaf(__uint_as_float(u[t].y << 16), xa.z, a);
+                    a = fmaf(__uint_as_float(u[t].y & 0xFFFF0000u), xa.w, a);
+                    a = fmaf(__uint_as_float(u[t].z << 16), xb.x, a);
+                    a = fmaf(__uint_as_float(u[t].z & 0xFFFF0000u), xb.y, a);
+                    a = fmaf(__uint_as_float(u[t].w << 16), xb.z, a);
+                    a = fmaf(__uint_as_float(u[t].w & 0xFFFF0000u), xb.w, a);
+                    acc[t][m] = a;
+                }
             }
         }
 #pragma unroll
-        for (int t = 0; t < kLmRows; ++t) {
-            float a = acc[t];
-            for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
-            if (r0 + t < vocab) {
-                const uint16_t v = tobf(a);
-                if (lane == 0 && logits) logits[r0 + t] = v;
-                const unsigned long long k = argmax_key(v, (uint32_t)(r0 + t));
-                key = k > key ? k : key;
+        for (int t = 0; t < kRows; ++t) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float a = acc[t][m];
+                for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+                if (r0 + t < vocab) {
+                    const uint16_t v = tobf(a);
+                    if (lane == 0 && logits) logits[(int64_t)m * vocab + r0 + t] = v;
+                    const unsigned long long k = argmax_key(v, (uint32_t)(r0 + t));
+                    key[m] = k > key[m] ? k : key[m];
+                }
             }
         }
     }
-    if (lane == 0 && key) atomicMax(best, key);
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+        if (lane == 0 && key[m]) atomicMax(best + m, key[m]);
 }
 
-// The argmax key -> the step's token, then the key is cleared for the next step.
-__global__ void argmax_token_kernel(unsigned long long* __restrict__ best, int64_t* __restrict__ next) {
+// The argmax keys -> the rows' tokens, then the keys are cleared for the next call.
+__global__ void argmax_token_kernel(unsigned long long* __restrict__ best, int64_t* __restrict__ next, int m) {
     pdl_wait();
     pdl_release();
-    const unsigned long long k = *best;
-    *next = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-    *best = 0ull;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        const unsigned long long k = best[i];
+        next[i] = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        best[i] = 0ull;
+    }
+}
+
+// Speculative verification: the rotary embedding of the keys of n_q
+// consecutive positions base..base+n_q-1 and their append (with the values)
+// to the cache, one block per (kv head, position); the same arithmetic as the
+// single-token kernel's append.
+__global__ void __launch_bounds__(kHd) rope_append_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                                                          const uint16_t* __restrict__ cos_t,
+                                                          const uint16_t* __restrict__ sin_t,
+                                                          const int32_t* __restrict__ pos_p, uint16_t* __restrict__ kc,
+                                                          uint16_t* __restrict__ vc, int max_len, int n_kv) {
+    pdl_wait();
+    pdl_release();
+    const int kvh = blockIdx.x, qi = blockIdx.y, d = threadIdx.x;
+    const int P = *pos_p + qi;
+    if (P < 0 || P >= max_len) return;
+    const uint16_t* kq = k + (int64_t)qi * n_kv * kHd;
+    const uint16_t* vq = v + (int64_t)qi * n_kv * kHd;
+    const uint16_t* cs = cos_t + (int64_t)P * kHd;
+    const uint16_t* sn = sin_t + (int64_t)P * kHd;
+    const int o = d < kHd / 2 ? d + kHd / 2 : d - kHd / 2;
+    const float sgn = d < kHd / 2 ? -1.f : 1.f;
+    const float kd = bf(kq[kvh * kHd + d]), ko = bf(kq[kvh * kHd + o]);
+    kc[((int64_t)kvh * max_len + P) * kHd + d] = tobf(rbf(rbf(kd * bf(cs[d])) + rbf(sgn * ko * bf(sn[d]))));
+    vc[((int64_t)kvh * max_len + P) * kHd + d] = vq[kvh * kHd + d];
+}
+
+// Speculative verification: attention of n_q consecutive query positions, one
+// block per (head, position), each exactly the single-token kernel's
+// attention at that position (its own key and value read back from the
+// cache, where rope_append_kernel put the same bits the single-token kernel
+// keeps in registers).
+__global__ void __launch_bounds__(kAttnThreads) attn_multi_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t,
+    const int32_t* __restrict__ pos_p, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc, int max_len,
+    int n_heads, int n_kv, float scale, uint16_t* __restrict__ out, int cap) {
+    extern __shared__ float scores[];
+    __shared__ float qe[kHd], red[kAttnThreads / 32], part[kHd];
+    const int h = blockIdx.x, qi = blockIdx.y, tid = threadIdx.x;
+    pdl_wait();
+    pdl_release();
+    const int group = n_heads / n_kv, kvh = h / group;
+    const int P = *pos_p + qi;
+    if (P < 0 || P >= max_len || P >= cap) return;
+    const uint16_t* qq = q + (int64_t)qi * n_heads * kHd;
+    uint16_t* oq = out + (int64_t)qi * n_heads * kHd;
+    const uint16_t* cs = cos_t + (int64_t)P * kHd;
+    const uint16_t* sn = sin_t + (int64_t)P * kHd;
+    if (tid < kHd) {
+        const int d = tid, o = d < kHd / 2 ? d + kHd / 2 : d - kHd / 2;
+        const float sgn = d < kHd / 2 ? -1.f : 1.f;
+        const float qd = bf(qq[h * kHd + d]), qo = bf(qq[h * kHd + o]);
+        qe[d] = rbf(rbf(qd * bf(cs[d])) + rbf(sgn * qo * bf(sn[d])));
+    }
+    __syncthreads();
+    const uint16_t* kb = kc + (int64_t)kvh * max_len * kHd;
+    float mx = -INFINITY;
+    for (int j = tid; j <= P; j += kAttnThreads) {
+        float s = 0.f;
+        const uint4* kr = reinterpret_cast<const uint4*>(kb + (int64_t)j * kHd);
+#pragma unroll
+        for (int c = 0; c < kHd / 8; ++c) {
+            const uint4 u = kr[c];
+            const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                s = fmaf(qe[8 * c + 2 * t], __uint_as_float(wv[t] << 16), s);
+                s = fmaf(qe[8 * c + 2 * t + 1], __uint_as_float(wv[t] & 0xFFFF0000u), s);
+            }
+        }
+        s *= scale;
+        scores[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k2 = 1; k2 < kAttnThreads / 32; ++k2) mx = fmaxf(mx, red[k2]);
+    __syncthreads();
+    float sum = 0.f;
+    for (int j = tid; j <= P; j += kAttnThreads) {
+        const float e = expf(scores[j] - mx);
+        scores[j] = e;
+        sum += e;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    sum = 0.f;
+    for (int k2 = 0; k2 < kAttnThreads / 32; ++k2) sum += red[k2];
+    const int d = tid & (kHd - 1), half = tid / kHd;
+    const uint16_t* vb = vc + (int64_t)kvh * max_len * kHd;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int j = half; j < P; j += 2) acc = fmaf(scores[j], bf(vb[(int64_t)j * kHd + d]), acc);
+    if ((P & 1) == half) acc = fmaf(scores[P], bf(vb[(int64_t)P * kHd + d]), acc);
+    if (half == 1) part[d] = acc;
+    __syncthreads();
+    if (half == 0) oq[h * kHd + d] = tobf((acc + part[d]) / sum);
 }
 
 }  // namespace
 
 extern "C" {
 
-cdq_status cdq_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps, uint16_t* out,
-                           int32_t n, void* stream) {
-    if (!h || !w || !out || n < 1) return CDQ_ERR_ARG;
-    return launch_pdl(add_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, (cudaStream_t)stream, h, delta, w, eps,
+cdq_status cdq_add_rmsnorm_rows(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps, uint16_t* out,
+                                int32_t n, int32_t rows, void* stream) {
+    if (!h || !w || !out || n < 1 || rows < 1 || rows > 65535) return CDQ_ERR_ARG;
+    return launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, (cudaStream_t)stream, h, delta, w, eps,
                       out, n) == cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;
+}
+
+cdq_status cdq_add_rmsnorm(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps, uint16_t* out,
+                           int32_t n, void* stream) {
+    return cdq_add_rmsnorm_rows(h, delta, w, eps, out, n, 1, stream);
 }
 
 cdq_status cdq_attn_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* cos_t,
@@ -334,31 +466,85 @@ cdq_status cdq_decode_advance(const int64_t* next, int64_t* ids, int64_t* tokens
                : CDQ_ERR_CUDA;
 }
 
+cdq_status cdq_embed_rmsnorm_rows(const int64_t* ids, const uint16_t* table, int64_t vocab, uint16_t* h,
+                                  const uint16_t* w, float eps, uint16_t* out, int32_t n, int32_t rows, void* stream) {
+    if (!ids || !table || vocab < 1 || !h || !w || !out || n < 1 || rows < 1 || rows > 65535) return CDQ_ERR_ARG;
+    return launch_pdl(embed_rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, (cudaStream_t)stream, ids, table, vocab,
+                      h, w, eps, out, (int)n) == cudaSuccess
+               ? CDQ_OK
+               : CDQ_ERR_CUDA;
+}
+
 cdq_status cdq_embed_rmsnorm(const int64_t* ids, const uint16_t* table, int64_t vocab, uint16_t* h,
                              const uint16_t* w, float eps, uint16_t* out, int32_t n, void* stream) {
-    if (!ids || !table || vocab < 1 || !h || !w || !out || n < 1) return CDQ_ERR_ARG;
-    return launch_pdl(embed_rmsnorm_kernel, dim3(1), dim3(kNormThreads), 0, (cudaStream_t)stream, ids, table, vocab,
-                      h, w, eps, out, (int)n) == cudaSuccess
+    return cdq_embed_rmsnorm_rows(ids, table, vocab, h, w, eps, out, n, 1, stream);
+}
+
+cdq_status cdq_lm_head_argmax_rows(const uint16_t* w, const uint16_t* x, int32_t vocab, int32_t n, int32_t m,
+                                   uint16_t* logits, uint64_t* best, int64_t* next, void* stream) {
+    if (!w || !x || !best || !next || vocab < 1 || n < 8 || n % 8 || n > 16384 || m < 1 || m > 8)
+        return CDQ_ERR_ARG;
+    if ((uintptr_t)w % 16 || (uintptr_t)best % 8) return CDQ_ERR_ARG;
+    int sms = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return CDQ_ERR_CUDA;
+    const int64_t rows_per_block = (kLmThreads / 32) * (m == 1 ? kLmRows : 1);
+    const int blocks = (int)std::min<int64_t>((vocab + rows_per_block - 1) / rows_per_block, (int64_t)sms * 8);
+    const size_t smem = (size_t)m * n * 4;
+    auto* best64 = reinterpret_cast<unsigned long long*>(best);
+    cudaError_t e = cudaSuccess;
+    switch (m) {
+#define CDQ_LM_CASE(MM)                                                                                           \
+    case MM:                                                                                                      \
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(lm_head_argmax_kernel<MM>,                                   \
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=   \
+                                    cudaSuccess)                                                                  \
+            return CDQ_ERR_CUDA;                                                                                  \
+        e = launch_pdl(lm_head_argmax_kernel<MM>, dim3(blocks), dim3(kLmThreads), smem, (cudaStream_t)stream, w, x, \
+                       (int)vocab, (int)n, logits, best64);                                                       \
+        break;
+        CDQ_LM_CASE(1)
+        CDQ_LM_CASE(2)
+        CDQ_LM_CASE(3)
+        CDQ_LM_CASE(4)
+        CDQ_LM_CASE(5)
+        CDQ_LM_CASE(6)
+        CDQ_LM_CASE(7)
+        CDQ_LM_CASE(8)
+#undef CDQ_LM_CASE
+    }
+    if (e != cudaSuccess) return CDQ_ERR_CUDA;
+    return launch_pdl(argmax_token_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, best64, next, (int)m) ==
+                   cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;
 }
 
 cdq_status cdq_lm_head_argmax(const uint16_t* w, const uint16_t* x, int32_t vocab, int32_t n, uint16_t* logits,
                               uint64_t* best, int64_t* next, void* stream) {
-    if (!w || !x || !best || !next || vocab < 1 || n < 8 || n % 8 || n > 16384) return CDQ_ERR_ARG;
-    if ((uintptr_t)w % 16 || (uintptr_t)best % 8) return CDQ_ERR_ARG;
-    int sms = 0, dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cdq_lm_head_argmax_rows(w, x, vocab, n, 1, logits, best, next, stream);
+}
+
+cdq_status cdq_attn_decode_multi(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* cos_t,
+                                 const uint16_t* sin_t, const int32_t* pos, uint16_t* k_cache, uint16_t* v_cache,
+                                 int32_t max_len, int32_t n_heads, int32_t n_kv, int32_t head_dim, float scale,
+                                 uint16_t* out, int32_t n_q, void* stream) {
+    if (!q || !k || !v || !cos_t || !sin_t || !pos || !k_cache || !v_cache || !out || n_q < 1 || n_q > 64)
+        return CDQ_ERR_ARG;
+    if (head_dim != kHd || n_kv < 1 || n_heads < n_kv || n_heads % n_kv || max_len < 1 || max_len > 16384)
+        return CDQ_ERR_UNSUPPORTED;
+    if ((uintptr_t)k_cache % 16 || (uintptr_t)v_cache % 16) return CDQ_ERR_ARG;
+    if (launch_pdl(rope_append_kernel, dim3(n_kv, n_q), dim3(kHd), 0, (cudaStream_t)stream, k, v, cos_t, sin_t, pos,
+                   k_cache, v_cache, (int)max_len, (int)n_kv) != cudaSuccess)
         return CDQ_ERR_CUDA;
-    const int64_t rows_per_block = (kLmThreads / 32) * kLmRows;
-    const int blocks = (int)std::min<int64_t>((vocab + rows_per_block - 1) / rows_per_block, (int64_t)sms * 8);
-    const size_t smem = (size_t)n * 4;
-    if (launch_pdl(lm_head_argmax_kernel, dim3(blocks), dim3(kLmThreads), smem, (cudaStream_t)stream, w, x, (int)vocab,
-                   (int)n, logits, reinterpret_cast<unsigned long long*>(best)) != cudaSuccess)
+    const int smem = max_len * 4;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(attn_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return CDQ_ERR_CUDA;
-    return launch_pdl(argmax_token_kernel, dim3(1), dim3(1), 0, (cudaStream_t)stream,
-                      reinterpret_cast<unsigned long long*>(best), next) == cudaSuccess
+    return launch_pdl(attn_multi_kernel, dim3(n_heads, n_q), dim3(kAttnThreads), (size_t)smem, (cudaStream_t)stream,
+                      q, cos_t, sin_t, pos, k_cache, v_cache, (int)max_len, (int)n_heads, (int)n_kv, scale, out,
+                      (int)max_len) == cudaSuccess
                ? CDQ_OK
                : CDQ_ERR_CUDA;
 }

@@ -356,3 +356,145 @@ def fused_greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph:
     return {"tokens": toks, "prefill_ms": e[0].elapsed_time(e[1]),
             "decode_ms_per_token": e[2].elapsed_time(e[3]) / steps,
             "tokens_per_s": 1e3 * steps / max(e[2].elapsed_time(e[3]), 1e-9), "graphed": use_graph}
+
+
+class VerifyStep:
+    """The target model's forward over n consecutive positions of one sequence
+    at once (the speculative verify pass): the same kernels as the fused step,
+    with n rows through the grouped CDQ linears (m = n) and a multi-query
+    attention. Every row gets exactly the arithmetic of a one-token step, so
+    its greedy tokens equal those of n sequential steps. Shares the target
+    FusedDecoder's cache, tables and position (the first row's position)."""
+
+    def __init__(self, fd: FusedDecoder, n: int):
+        from . import ops
+        self.fd, self.n = fd, n
+        bf16, dev = torch.bfloat16, fd.dev
+        z = lambda *shape, dt=bf16: torch.zeros(*shape, dtype=dt, device=dev)  # noqa: E731
+        H, inter = fd.H, fd.inter
+        qd, kvd = fd.n_heads * fd.hd, fd.n_kv * fd.hd
+        self.ids = z(n, dt=torch.long)
+        self.h, self.xn, self.o, self.dn = z(n, H), z(n, H), z(n, H), z(n, H)
+        self.q, self.k, self.v, self.att = z(n, qd), z(n, kvd), z(n, kvd), z(n, qd)
+        self.g, self.u, self.act = z(n, inter), z(n, inter), z(n, inter)
+        self.best = z(n, dt=torch.int64)
+        self.next = z(n, dt=torch.int64)
+        self.layers = []
+        for layer in fd.model.model.layers:
+            a, mlp = layer.self_attn, layer.mlp
+            T = lambda mod, x, y: ops.GemvTask(mod.device_pack, x, y, mod.bias)  # noqa: E731
+            self.layers.append({
+                "ln1": layer.input_layernorm.weight, "ln2": layer.post_attention_layernorm.weight,
+                "qkv": ops.GroupedLinear([T(a.q_proj, self.xn, self.q), T(a.k_proj, self.xn, self.k),
+                                          T(a.v_proj, self.xn, self.v)], m=n),
+                "o": ops.GroupedLinear([T(a.o_proj, self.att, self.o)], m=n),
+                "gu": ops.GroupedLinear([T(mlp.gate_proj, self.xn, self.g), T(mlp.up_proj, self.xn, self.u)], m=n),
+                "down": ops.GroupedLinear([T(mlp.down_proj, self.act, self.dn)], m=n),
+            })
+        self.graph = None
+
+    def _run(self) -> None:
+        fd, n = self.fd, self.n
+        p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+        s = torch.cuda.current_stream(fd.dev).cuda_stream
+        for li, Ly in enumerate(self.layers):
+            cl = fd.cache.layers[li]
+            if li == 0:
+                fd._call("cdq_embed_rmsnorm_rows", p(self.ids), p(fd.embed_w), fd.vocab, p(self.h), p(Ly["ln1"]),
+                         fd.eps, p(self.xn), fd.H, n, s)
+            else:
+                fd._call("cdq_add_rmsnorm_rows", p(self.h), p(self.dn), p(Ly["ln1"]), fd.eps, p(self.xn), fd.H, n, s)
+            Ly["qkv"]()
+            fd._call("cdq_attn_decode_multi", p(self.q), p(self.k), p(self.v), p(fd.cos), p(fd.sin), p(fd.pos),
+                     p(cl.keys), p(cl.values), fd.max_len, fd.n_heads, fd.n_kv, fd.hd, float(fd.hd) ** -0.5,
+                     p(self.att), n, s)
+            Ly["o"]()
+            fd._call("cdq_add_rmsnorm_rows", p(self.h), p(self.o), p(Ly["ln2"]), fd.eps, p(self.xn), fd.H, n, s)
+            Ly["gu"]()
+            fd._call("cdq_silu_mul", p(self.g), p(self.u), p(self.act), n * fd.inter, s)
+            Ly["down"]()
+        fd._call("cdq_add_rmsnorm_rows", p(self.h), p(self.dn), p(fd.norm_w), fd.eps, p(self.xn), fd.H, n, s)
+        fd._call("cdq_lm_head_argmax_rows", p(fd.lm_w), p(self.xn), fd.vocab, fd.H, n, None, p(self.best),
+                 p(self.next), s)
+
+    @torch.no_grad()
+    def capture(self) -> None:
+        s = torch.cuda.Stream(device=self.fd.dev)
+        s.wait_stream(torch.cuda.current_stream(self.fd.dev))
+        with torch.cuda.stream(s):
+            self._run()  # warm-up (writes cache slots that later passes overwrite)
+        torch.cuda.current_stream(self.fd.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._run()
+        self.graph = g
+
+    @torch.no_grad()
+    def run(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._run()
+
+
+@torch.no_grad()
+def speculative_greedy_decode(target, draft, prompt: torch.Tensor, new_tokens: int, k: int = 3,
+                              use_graph: bool = True) -> dict:
+    """Greedy decoding of `target` (the 26-state model) with `draft` (the same
+    model on the 16-state lattice) proposing k tokens at a time: the draft
+    decodes k tokens from the last accepted one, the target checks all k + 1
+    positions in one verify pass, the longest prefix where the draft agrees
+    with the target's own greedy choice is kept and the target's token at the
+    first disagreement (or after the last draft token) follows. The output
+    equals plain greedy decoding of the target token for token. Caches are
+    static: slots beyond the accepted length are simply overwritten later."""
+    P = prompt.shape[1]
+    max_len = P + new_tokens + k + 4
+    td = FusedDecoder(target, max_len)
+    dd = FusedDecoder(draft, max_len)
+    ver = VerifyStep(td, k + 1)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    e[0].record()
+    tok = td.prefill(prompt)
+    dd.prefill(prompt)
+    if use_graph:
+        dd.capture()
+        ver.capture()
+    e[1].record()
+    out = [int(tok.item())]
+    pos = P  # position of `tok`
+    verifies = accepted = 0
+    while len(out) < new_tokens:
+        dd.reset(torch.tensor([out[-1]], device=td.dev), pos)
+        for _ in range(k):
+            dd.step()
+        ver.ids[0] = out[-1]
+        ver.ids[1:].copy_(dd.tokens[:k])
+        td.pos.fill_(pos)
+        ver.run()
+        drafts, ys = dd.tokens[:k].tolist(), ver.next.tolist()
+        a = 0
+        while a < k and drafts[a] == ys[a]:
+            a += 1
+        out += drafts[:a] + [ys[a]]
+        verifies += 1
+        accepted += a
+        if a == k:  # the draft never consumed its last token: let it see it
+            dd.reset(torch.tensor([drafts[k - 1]], device=td.dev), pos + k)
+            dd.step()
+        pos += a + 1
+    e[2].record()
+    torch.cuda.synchronize()
+    ms = e[1].elapsed_time(e[2])
+    n = len(out) - 1
+    # the verify pass alone (device time of one graph replay, averaged)
+    v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    td.pos.fill_(pos)
+    v0.record()
+    for _ in range(5):
+        ver.run()
+    v1.record()
+    torch.cuda.synchronize()
+    return {"tokens": torch.tensor(out[:new_tokens]).view(1, -1), "verifies": verifies,
+            "accepted_per_verify": accepted / max(verifies, 1), "tokens_per_verify": n / max(verifies, 1),
+            "tokens_per_s": 1e3 * n / max(ms, 1e-9), "k": k, "verify_ms": v0.elapsed_time(v1) / 5}

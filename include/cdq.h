@@ -331,6 +331,39 @@ CDQ_API cdq_status cdq_lm_head_argmax(const uint16_t* w, const uint16_t* x, int3
                                       uint16_t* logits, uint64_t* best, int64_t* next, void* stream);
 
 /*
+ * Several rows or positions at once, for the speculative verify pass (k + 1
+ * consecutive positions of one sequence); every row gets exactly the
+ * arithmetic of the single-row call, so a verify pass reproduces sequential
+ * decode steps bit for bit.
+ *   cdq_add_rmsnorm_rows / cdq_embed_rmsnorm_rows: rows vectors of n (ids:
+ *     rows tokens).
+ *   cdq_lm_head_argmax_rows: m <= 8 activation rows x [m][n] -> logits
+ *     [m][vocab] (or NULL), next[m]; best: m device uint64 keys, zero before
+ *     the first call and left zero.
+ *   cdq_attn_decode_multi: n_q <= 64 queries at positions *pos .. *pos+n_q-1
+ *     (q [n_q][n_heads*64], k, v [n_q][n_kv*64], out [n_q][n_heads*64]): the
+ *     keys and values of all n_q positions are appended to the cache first,
+ *     then each query attends over positions 0..its own, as cdq_attn_decode
+ *     does for one.
+ * The reference decodes one token per step (code/cdq_lrr_qwen05.py:335-340);
+ * the draft/verify use of its two lattices follows its README's description
+ * of the 16-state tier.
+ */
+CDQ_API cdq_status cdq_add_rmsnorm_rows(uint16_t* h, const uint16_t* delta, const uint16_t* w, float eps,
+                                        uint16_t* out, int32_t n, int32_t rows, void* stream);
+CDQ_API cdq_status cdq_embed_rmsnorm_rows(const int64_t* ids, const uint16_t* table, int64_t vocab, uint16_t* h,
+                                          const uint16_t* w, float eps, uint16_t* out, int32_t n, int32_t rows,
+                                          void* stream);
+CDQ_API cdq_status cdq_lm_head_argmax_rows(const uint16_t* w, const uint16_t* x, int32_t vocab, int32_t n,
+                                           int32_t m, uint16_t* logits, uint64_t* best, int64_t* next,
+                                           void* stream);
+CDQ_API cdq_status cdq_attn_decode_multi(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                         const uint16_t* cos_t, const uint16_t* sin_t, const int32_t* pos,
+                                         uint16_t* k_cache, uint16_t* v_cache, int32_t max_len, int32_t n_heads,
+                                         int32_t n_kv, int32_t head_dim, float scale, uint16_t* out, int32_t n_q,
+                                         void* stream);
+
+/*
  * Bit-exact w_hat [rows, cols] bf16 from a device pack.
  * Replaces dequantize, code/cdq_lrr_qwen05.py:141-152, and
  * CDQLinear.dequant_weight, code/cdq_lrr_qwen05.py:188-194.

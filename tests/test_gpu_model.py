@@ -406,3 +406,56 @@ def test_embed_rmsnorm_kernel():
                                     C.c_void_p(out2.data_ptr()), H, s), "cdq_add_rmsnorm")
         torch.cuda.synchronize()
         assert torch.equal(h, table[tok]) and torch.equal(out, out2)
+
+
+def test_verify_pass_matches_sequential_steps(cdq_model):
+    """The speculative verify pass over n positions gives, bit for bit, the
+    greedy tokens and cache contents of n sequential one-token steps."""
+    from cdq_lrr_b200 import decode
+    prompt = _prompt(24, seed=8)
+    seq = decode.FusedDecoder(cdq_model, 64)
+    tok = seq.prefill(prompt)
+    toks = [int(tok)]
+    for _ in range(4):
+        seq.step()
+        toks.append(int(seq.tokens[len(toks) - 1]))
+    # the same 5 positions in one pass, fed the tokens the sequential steps saw
+    par = decode.FusedDecoder(cdq_model, 64)
+    par.prefill(prompt)
+    ver = decode.VerifyStep(par, 5)
+    ver.ids.copy_(torch.tensor(toks, device="cuda"))
+    par.pos.fill_(24)
+    ver.run()
+    torch.cuda.synchronize()
+    assert ver.next.tolist()[:4] == toks[1:]
+    for a, b in zip(seq.cache.layers, par.cache.layers):
+        assert torch.equal(a.keys[:, :, :28], b.keys[:, :, :28])
+        assert torch.equal(a.values[:, :, :28], b.values[:, :, :28])
+
+
+@pytest.mark.parametrize("k", [1, 3])
+def test_speculative_decode_matches_greedy(cdq_model, k):
+    """Draft tokens from the 16-state tier, verified k + 1 at a time by the
+    26-state model: the output equals plain greedy decoding of the 26-state
+    model token for token (the reference README's draft/verify tiers)."""
+    from cdq_lrr_b200 import decode
+    from cdq_lrr_b200.quant import CAMKII_LATTICE_16
+    draft = decode.build_model(seed=0, device="cuda")
+    decode.patch_cdq(draft, lattice=CAMKII_LATTICE_16)
+    prompt = _prompt(32, seed=4)
+    plain = decode.fused_greedy_decode(cdq_model, prompt, 40)["tokens"].view(-1).cpu()
+    spec = decode.speculative_greedy_decode(cdq_model, draft, prompt, 40, k=k)
+    assert torch.equal(spec["tokens"].view(-1).cpu(), plain)
+    assert spec["verifies"] <= 39 and 0.0 <= spec["accepted_per_verify"] <= k
+
+
+def test_speculative_self_draft_accepts_every_token(cdq_model):
+    """With the target as its own draft every proposal agrees: each verify
+    accepts all k drafts and adds the bonus token, and the output is still
+    plain greedy (the rewind-free path of the loop)."""
+    from cdq_lrr_b200 import decode
+    prompt = _prompt(32, seed=5)
+    plain = decode.fused_greedy_decode(cdq_model, prompt, 25)["tokens"].view(-1).cpu()
+    spec = decode.speculative_greedy_decode(cdq_model, cdq_model, prompt, 25, k=3)
+    assert torch.equal(spec["tokens"].view(-1).cpu(), plain)
+    assert spec["accepted_per_verify"] == 3.0 and spec["verifies"] == 6
