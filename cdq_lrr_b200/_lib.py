@@ -87,6 +87,7 @@ _SIGS = {
     "cdq_ar_set_spin_limit": (C.c_int, [C.c_int64]),
     "cdq_pack_from_reference_device": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, C.c_int64,
                                                  C.POINTER(cdq_packed), _P, _P]),
+    "cdq_check_device_pack": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
     "cdq_file_checkpoints": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), C.c_int32, _P, _P]),
     "cdq_file_decode_device": (C.c_int, [_P, C.c_int64, C.c_int32, C.c_int64, C.c_int64, C.c_int32, _P, _P,
                                          _P, _P, _P, _P, _P, _P]),

@@ -207,6 +207,43 @@ __global__ void file_decode_spans(const uint8_t* __restrict__ rec, int64_t rec_b
     }
 }
 
+// Validation of a device pack from an untrusted source (a state dict, a file
+// written by another build): one thread per (unit, lane) checks the lane's 16
+// pair codes (26 states: at most 26 * 27 + 26 = 728, the last entry of the
+// pair table the linear kernels index with the code); one thread per CSR
+// bucket checks that the bounds start at 0, never decrease and end at n_res;
+// one thread per entry checks its column against cols. Every malformed part
+// adds one to *bad.
+__global__ void check_units(Geometry g, const uint8_t* __restrict__ units, int* __restrict__ bad) {
+    const int64_t n = g.r16 * g.kp * 32;
+    for (int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; id < n; id += (int64_t)gridDim.x * blockDim.x) {
+        const int lane = (int)(id & 31);
+        const int64_t unit = id >> 5, b16 = unit / g.kp, cp = unit - b16 * g.kp;
+        uint32_t w[5];
+        for (int wd = 0; wd < 5; ++wd)
+            w[wd] = *reinterpret_cast<const uint32_t*>(units + word_offset(g, b16, cp, lane, wd));
+        int n_bad = 0;
+        for (int s = 0; s < 16; ++s) {
+            const int bit = 10 * s, wd = bit >> 5, off = bit & 31;
+            const uint64_t win = w[wd] | (wd + 1 < 5 ? (uint64_t)w[wd + 1] << 32 : 0ull);
+            n_bad += ((uint32_t)(win >> off) & 0x3FFu) > 728u;
+        }
+        if (n_bad) atomicAdd(bad, 1);
+    }
+}
+
+__global__ void check_csr(const uint32_t* __restrict__ res_ptr, int64_t buckets, const uint32_t* __restrict__ res_ent,
+                          int64_t n_res, int32_t cols, int* __restrict__ bad) {
+    const int64_t n = buckets > n_res ? buckets : n_res;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        if (i < buckets) {
+            const uint32_t a = res_ptr[i], b = res_ptr[i + 1];
+            if (b < a || (i == 0 && a != 0u) || (i == buckets - 1 && (int64_t)b != n_res)) atomicAdd(bad, 1);
+        }
+        if (i < n_res && (int32_t)(res_ent[i] >> 16) >= cols) atomicAdd(bad, 1);
+    }
+}
+
 int grid_for(int64_t n, int threads) {
     const int64_t b = (n + threads - 1) / threads;
     return (int)(b < 1 ? 1 : (b > 65535 ? 65535 : b));
@@ -253,5 +290,23 @@ extern "C" cdq_status cdq_file_decode_device(const uint8_t* records, int64_t rec
     const int64_t spans = (n_tiles + every - 1) / every;
     file_decode_spans<<<grid_for(spans, 128), 128, 0, (cudaStream_t)stream>>>(
         records, record_bytes, n_states, n_tiles, n_res, every, byte_off, res_off, q, scales_f8, ridx, rval, error);
+    return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+}
+
+extern "C" cdq_status cdq_check_device_pack(const cdq_packed* pack, int32_t* bad, void* stream) {
+    if (!pack || !bad || !pack->units || !pack->res_ptr || pack->n_res < 0 || (pack->n_res > 0 && !pack->res_ent))
+        return CDQ_ERR_ARG;
+    if (pack->n_states != 26 && pack->n_states != 16) return CDQ_ERR_STATES;
+    if (pack->rows <= 0 || pack->cols <= 0 || pack->cols % 32 || pack->cols > CDQ_MAX_COLS) return CDQ_ERR_SHAPE;
+    if ((uintptr_t)pack->units % 4 || (uintptr_t)pack->res_ptr % 4 || (uintptr_t)pack->res_ent % 4)
+        return CDQ_ERR_ARG;
+    const Geometry g = geometry(pack->rows, pack->cols, pack->n_states);
+    cudaStream_t s = (cudaStream_t)stream;
+    constexpr int kT = 256;
+    if (pack->n_states == 26)
+        check_units<<<grid_for(g.r16 * g.kp * 32, kT), kT, 0, s>>>(g, pack->units, bad);
+    const int64_t buckets = g.r16 * 16 * g.kg;
+    check_csr<<<grid_for(buckets > pack->n_res ? buckets : pack->n_res, kT), kT, 0, s>>>(
+        pack->res_ptr, buckets, pack->res_ent, pack->n_res, pack->cols, bad);
     return cudaGetLastError() == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }

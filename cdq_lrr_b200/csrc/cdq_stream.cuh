@@ -276,6 +276,62 @@ __device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const
     if (lane == 0) J.counters[b16] = 0u;
 }
 
+// One quad of UQ units (4: a full quad; 1..3: the compact last quad of a row
+// block) read from its ring slot: the lane's code words and scale half-words
+// into registers, then the slot goes back to the producer (`refill`, after
+// one register of every read has arrived, so the next copy cannot overwrite
+// bytes still being read), then the units' mmas. PH: the item holds the
+// phantom second tile of an odd tile count (unit `phantom` of this quad, -1
+// if none here), whose lanes c >= 2 take zero activations.
+template <int NS, int UQ, bool PH, typename Refill>
+__device__ __forceinline__ void quad_step(uint32_t slot, int lane, int c, const uint16_t* xq, int phantom,
+                                          uint32_t lane_base, uint32_t sig_base, float (&d)[4], Refill&& refill) {
+    using Tr = PackTraits<NS>;
+    uint4 A[4];
+    uint32_t w4[4] = {0u, 0u, 0u, 0u};
+    uint32_t s01, s23, dep;
+    if constexpr (UQ == 4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+        const uint4 W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+        const uint2 S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
+        w4[0] = W.x;
+        w4[1] = W.y;
+        w4[2] = W.z;
+        w4[3] = W.w;
+        s01 = S.x;
+        s23 = S.y;
+        dep = W.x ^ S.x ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
+    } else {
+        uint32_t h[3] = {0u, 0u, 0u};
+        dep = 0u;
+#pragma unroll
+        for (int i = 0; i < UQ; ++i) {
+            A[i] = lds_slot4(slot + 512 * i + 16 * lane);
+            if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * UQ + 4 * (UQ * lane + i));
+            h[i] = lds_slot_u16(slot + Tr::kSigOff * UQ + 2 * (UQ * (lane >> 1) + i));
+            dep ^= A[i].x ^ w4[i] ^ h[i];
+        }
+        s01 = h[0] | (h[1] << 16);
+        s23 = h[2];
+    }
+    asm volatile("" ::"r"(dep));
+    __syncwarp();
+    refill();
+#pragma unroll
+    for (int i = 0; i < UQ; ++i) {
+        uint4 xa, xb;
+        if constexpr (PH) {
+            load_x(xq, i, i == phantom, c, xa, xb);
+        } else {
+            xa = ldg_x4(xq + 64 * i);
+            xb = ldg_x4(xq + 64 * i + 8);
+        }
+        if (i & 1) unit_mma<NS, 16>(A[i], w4[i], i < 2 ? s01 : s23, xa, xb, lane_base, sig_base, d);
+        else unit_mma<NS, 0>(A[i], w4[i], i < 2 ? s01 : s23, xa, xb, lane_base, sig_base, d);
+    }
+}
+
 template <int NS, int M, int MAXJ>
 __global__ void __launch_bounds__(kSThreads, 1)
 stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
@@ -379,31 +435,47 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t c_slot = 0, c_phase = 0;
     bool failed = false;
-    for (;;) {
-        const int ustart = item_start(batch, cur);
-        if (ustart >= u_hi) break;
-        const GemvJob& J = batch.jobs[cur.j];
-        const int kg = J.kg, kp = J.kp, cols = J.cols;
+    // the current job's fields, held in registers (reloaded when the cursor
+    // enters the next job), and the current item's first unit (items are
+    // consecutive in the unit sequence, so it advances by the item's units)
+    int jk = -1, kg = 1, kp = 1, r16 = 1, cols = 0;
+    bool odd_kt = false;
+    const uint16_t* jx = nullptr;
+    float* jpart = nullptr;
+    int ustart = u_first;
+    auto refill = [&]() { produce(c_slot); };
+    while (ustart < u_hi) {
+        if (cur.j != jk) {
+            const GemvJob& J = batch.jobs[cur.j];
+            jk = cur.j;
+            kg = J.kg;
+            kp = J.kp;
+            r16 = J.r16;
+            cols = J.cols;
+            odd_kt = (J.kt & 1) != 0;
+            jx = J.x;
+            jpart = J.partial;
+        }
         const int cp0 = 16 * cur.grp;
-        const int n_units = min(16, kp - cp0), nq = (n_units + 3) >> 2;
+        const int n_units = min(16, kp - cp0);
         // a phantom second tile (odd tile count) sits in the row block's last unit
-        const int phantom_u = (J.kt & 1) && cp0 + n_units == kp ? n_units - 1 : -1;
-        const bool phantom_item = phantom_u >= 0;
-        const uint16_t* xp = J.x + (int64_t)xrow * cols + 64 * cp0 + 16 * c;
+        const bool phantom_item = odd_kt && cp0 + n_units == kp;
+        const uint16_t* xp = jx + (int64_t)xrow * cols + 64 * cp0 + 16 * c;
 
         // the group's residual sums of rows g and g + 8 (batch columns 2c, 2c + 1),
         // from the pre-pass: in flight while the quads stream
-        const int64_t rpad = (int64_t)J.r16 * 16;
+        const int64_t rpad = (int64_t)r16 * 16;
         float R[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj)
                 if (2 * c + jj < M)
-                    R[2 * h + jj] = __ldcg(J.partial + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
+                    R[2 * h + jj] = __ldcg(jpart + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
                                            cur.b16 * 16 + g + 8 * h);
 
         float d[4] = {0.f, 0.f, 0.f, 0.f};
+        const int nq = (n_units + 3) >> 2;
         for (int q = 0; q < nq; ++q) {
             if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
                 failed = true;
@@ -412,64 +484,18 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             const uint32_t slot = ring + c_slot * kQuad;
             const int uq = min(4, n_units - 4 * q);
             const uint16_t* xq = xp + 256 * q;
-            if (uq == 4 && !phantom_item) {
-                // a full quad without a phantom tile: no per-unit checks
-                uint4 A[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                const uint4 W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
-                const uint2 S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
-                // one register of every slot read: each read has landed before the slot is reused
-                uint32_t dep = W.x ^ S.x ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
-                asm volatile("" ::"r"(dep));
-                __syncwarp();
-                produce(c_slot);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 xa = ldg_x4(xq + 64 * i), xb = ldg_x4(xq + 64 * i + 8);
-                    const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
-                    if (i & 1) unit_mma<NS, 16>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
-                    else unit_mma<NS, 0>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
-                }
+            if (!phantom_item) {
+                if (uq == 4) quad_step<NS, 4, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
+                else if (uq == 2) quad_step<NS, 2, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
+                else if (uq == 3) quad_step<NS, 3, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
+                else quad_step<NS, 1, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
             } else {
-                // a short last quad (1..3 units, compact) or the quad holding a phantom tile
-                uint4 A[4];
-                uint4 W;
-                uint2 S;
-                if (uq == 4) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                    W = NS == 26 ? lds_slot4(slot + 2048 + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
-                    S = lds_slot2(slot + 4 * Tr::kSigOff + 8 * (lane >> 1));
-                } else {
-                    uint32_t w4[3] = {0u, 0u, 0u}, h[3] = {0u, 0u, 0u};
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) {
-                        A[i] = make_uint4(0u, 0u, 0u, 0u);
-                        if (i < uq) {
-                            A[i] = lds_slot4(slot + 512 * i + 16 * lane);
-                            if constexpr (NS == 26) w4[i] = lds_slot(slot + 512 * uq + 4 * (uq * lane + i));
-                            h[i] = lds_slot_u16(slot + Tr::kSigOff * uq + 2 * (uq * (lane >> 1) + i));
-                        }
-                    }
-                    A[3] = make_uint4(0u, 0u, 0u, 0u);
-                    W = make_uint4(w4[0], w4[1], w4[2], 0u);
-                    S = make_uint2(h[0] | (h[1] << 16), h[2]);
-                }
-                uint32_t dep = W.x ^ W.y ^ W.z ^ S.x ^ S.y ^ A[0].x ^ A[1].x ^ A[2].x ^ A[3].x;
-                asm volatile("" ::"r"(dep));
-                __syncwarp();
-                produce(c_slot);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (i < uq) {
-                        uint4 xa, xb;
-                        load_x(xq, i, 4 * q + i == phantom_u, c, xa, xb);
-                        const uint32_t w4 = i == 0 ? W.x : i == 1 ? W.y : i == 2 ? W.z : W.w;
-                        if (i & 1) unit_mma<NS, 16>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
-                        else unit_mma<NS, 0>(A[i], w4, i < 2 ? S.x : S.y, xa, xb, lane_base, sig_base, d);
-                    }
-                }
+                // the phantom tile is in the item's last unit, so in its last quad
+                const int ph = q == nq - 1 ? uq - 1 : -1;
+                if (uq == 4) quad_step<NS, 4, true>(slot, lane, c, xq, ph, lane_base, sig_base, d, refill);
+                else if (uq == 2) quad_step<NS, 2, true>(slot, lane, c, xq, ph, lane_base, sig_base, d, refill);
+                else if (uq == 3) quad_step<NS, 3, true>(slot, lane, c, xq, ph, lane_base, sig_base, d, refill);
+                else quad_step<NS, 1, true>(slot, lane, c, xq, ph, lane_base, sig_base, d, refill);
             }
             c_slot ^= 1u;
             c_phase ^= c_slot == 0 ? 1u : 0u;
@@ -482,17 +508,19 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         for (int e = 0; e < 4; ++e) v[e] = d[e] + R[e];
 
         const int rb0 = ustart - cp0;  // first unit of the row block
-        Cursor nxt = cur;
-        advance(batch, nxt);
-        const bool has_next = item_start(batch, nxt) < u_hi;
+        const int grp = cur.grp, b16 = cur.b16;
+        const bool last_grp = grp == kg - 1;
+        ustart += n_units;
+        const bool has_next = ustart < u_hi;
         const bool cut = kg > 1 && (rb0 < u_lo || rb0 + 16 * (kg - 1) >= u_hi);
+        const GemvJob& J = batch.jobs[jk];
         if (!cut) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) tot[e] += v[e];
-            if (cur.grp == kg - 1) {
+            if (last_grp) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int row = cur.b16 * 16 + g + 8 * h;
+                    const int row = b16 * 16 + g + 8 * h;
 #pragma unroll
                     for (int jj = 0; jj < 2; ++jj)
                         if (row < J.rows && 2 * c + jj < M) store_out(J, 2 * c + jj, row, tot[2 * h + jj]);
@@ -501,10 +529,16 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
                 for (int e = 0; e < 4; ++e) tot[e] = 0.f;
             }
         } else {
-            cut_group<M>(J, cur.b16, cur.grp, v, cur.grp == kg - 1 || !has_next,
-                         cur.grp - (rb0 < u_lo ? grp_first : 0) + 1, g, c, lane);
+            cut_group<M>(J, b16, grp, v, last_grp || !has_next, grp - (rb0 < u_lo ? grp_first : 0) + 1, g, c,
+                         lane);
         }
-        cur = nxt;
+        if (++cur.grp == kg) {
+            cur.grp = 0;
+            if (++cur.b16 == r16) {
+                cur.b16 = 0;
+                ++cur.j;
+            }
+        }
     }
     if (failed) {
         // a copy that never landed: record it, give the copies still in

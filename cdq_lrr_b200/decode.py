@@ -498,3 +498,44 @@ def speculative_greedy_decode(target, draft, prompt: torch.Tensor, new_tokens: i
     return {"tokens": torch.tensor(out[:new_tokens]).view(1, -1), "verifies": verifies,
             "accepted_per_verify": accepted / max(verifies, 1), "tokens_per_verify": n / max(verifies, 1),
             "tokens_per_s": 1e3 * n / max(ms, 1e-9), "k": k, "verify_ms": v0.elapsed_time(v1) / 5}
+
+
+def main(argv=None) -> None:
+    """Greedy generation on the random-init Qwen2.5-0.5B-architecture model
+    with CDQ-26 projections (the reference's generate loop,
+    code/cdq_lrr_qwen05.py:335-340), through the fused decode step; prints
+    the tokens per second. --eager runs the steps without the CUDA graph, each
+    step's launches inside the NVTX range "decode_step" (for a profiler's
+    launch list)."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m cdq_lrr_b200.decode")
+    ap.add_argument("--prompt", type=int, default=128, help="prompt tokens (seeded random ids)")
+    ap.add_argument("--new-tokens", type=int, default=32)
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph; steps inside NVTX ranges")
+    args = ap.parse_args(argv)
+    model = build_model(seed=0, device="cuda")
+    patch_cdq(model)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, model.config.vocab_size, (1, args.prompt), generator=g).cuda()
+    if not args.eager:
+        r = fused_greedy_decode(model, ids, args.new_tokens)
+        print(f"{r['tokens_per_s']:.1f} tok/s ({r['decode_ms_per_token']:.4f} ms per token), "
+              f"tokens {r['tokens'][0, :8].tolist()} ...")
+        return
+    with torch.no_grad():
+        dec = FusedDecoder(model, args.prompt + args.new_tokens + 2)
+        dec.prefill(ids)
+        dec._step()  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.new_tokens - 1):
+            torch.cuda.nvtx.range_push("decode_step")
+            dec._step()
+            torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+    print(f"eager: {(args.new_tokens - 1) / dt:.1f} tok/s (host launch bound)")
+
+
+if __name__ == "__main__":
+    main()

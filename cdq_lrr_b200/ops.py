@@ -64,6 +64,29 @@ class DevicePack:
         p.res_q = self.res_q.data_ptr() if self.res_q.numel() else None
         return p
 
+    def validate(self) -> "DevicePack":
+        """Checks a pack that did not come from this library's converters or
+        quantizer (for example buffers loaded from a state dict) before any
+        kernel reads it: buffer sizes and dtypes on the host, then the pair
+        codes and the residual CSR on the GPU (cdq_check_device_pack). Raises
+        CdqError (status 5, CDQ_ERR_FORMAT) on a malformed pack; returns self."""
+        _require_cuda(self.units, "DevicePack.validate")
+        s = L.sizes(self.rows, self.cols, self.n_states)
+        ok = (self.units.dtype == torch.uint8 and self.units.numel() == s.units_bytes
+              and self.res_ptr.dtype == torch.int32 and self.res_ptr.numel() == s.res_ptr_count
+              and self.res_ent.dtype == torch.int32 and self.res_ent.numel() >= self.n_res >= 0
+              and all(t.is_contiguous() and t.device == self.units.device
+                      for t in (self.units, self.res_ptr, self.res_ent)))
+        if not ok:
+            raise L.CdqError(5, "DevicePack.validate (buffer sizes)")
+        bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+        st = self.struct()
+        L.check(L.lib().cdq_check_device_pack(C.byref(st), _vp(bad), _stream(self.device)),
+                "cdq_check_device_pack")
+        if int(bad.item()):
+            raise L.CdqError(5, f"DevicePack.validate ({int(bad.item())} malformed parts)")
+        return self
+
     def tensors(self) -> dict[str, torch.Tensor]:
         return {"units": self.units, "res_ptr": self.res_ptr,
                 "res_ent": self.res_ent, "res_q": self.res_q}

@@ -269,10 +269,17 @@ class CDQLinear(nn.Module):
                 with torch.no_grad():
                     self.bias.copy_(state_dict.pop(prefix + "bias"))
             return
-        # own format: buffers may change length (residual count)
-        for k in ("units", "res_ptr", "res_ent", "res_q"):
-            if prefix + k in state_dict:
-                setattr(self, k, state_dict[prefix + k].to(self.units.device))
+        # own format: buffers may change length (residual count); they did not
+        # come through the validating converters, so they are checked before
+        # any kernel reads them
+        own = {k: state_dict[prefix + k].to(self.units.device)
+               for k in ("units", "res_ptr", "res_ent", "res_q") if prefix + k in state_dict}
+        if own and self.units.is_cuda:
+            rows, cols = self.orig_shape
+            t = {k: own.get(k, getattr(self, k)) for k in ("units", "res_ptr", "res_ent", "res_q")}
+            ops.DevicePack(rows, cols, self.n_states, int(t["res_ent"].numel()), **t).validate()
+        for k, v in own.items():
+            setattr(self, k, v)
         self._n_res = int(self.res_ent.numel())
         self._ws.clear()
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,

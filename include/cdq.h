@@ -275,6 +275,19 @@ CDQ_API cdq_status cdq_pack_from_reference_device(int32_t rows, int32_t cols, in
                                                   cdq_packed* out, int32_t* error, void* stream);
 
 /*
+ * Validation of a device pack that did not come from this library's
+ * converters or quantizer (a saved state dict, a pack built elsewhere):
+ * adds to *bad (device int32, zeroed by the caller) one per lane whose 26-state
+ * pair codes exceed 728, one per CSR bound out of order (bounds must start at
+ * 0, never decrease and end at n_res) and one per residual entry whose column
+ * is >= cols. The linear kernels trust the pack they are given; a pack with
+ * *bad != 0 must not be used. Up to two launches on `stream`.
+ * Guards the reference's CDQLinear buffer load (code/cdq_lrr_qwen05.py:155-166,
+ * via load_state_dict) when the buffers are in this library's own layout.
+ */
+CDQ_API cdq_status cdq_check_device_pack(const cdq_packed* pack, int32_t* bad, void* stream);
+
+/*
  * Quality statistics on the device (the reference's report after quantizing,
  * code/run_any_model.py:89-110): out[0..3] (device float64) = sum (a-b)^2,
  * sum a*b, sum a^2, sum b^2 over n values of a and b (dtype 0: bf16 bits,

@@ -141,3 +141,55 @@ def test_quantize_dict_matches_reference_dict(golden, golden_meta):
     assert np.array_equal(_bits(pack["scales_bf16"]).ravel(), golden[f"{nm}.scales_bf16"])
     assert np.array_equal(pack["residual_indices"].numpy(), golden[f"{nm}.residual_indices"])
     assert np.array_equal(_bits(pack["residual_values"]), golden[f"{nm}.residual_values"])
+
+
+@pytest.mark.parametrize("states", [26, 16])
+def test_own_format_state_dict_is_validated(states):
+    """CDQLinear buffers in this library's own layout, loaded from a state
+    dict, are checked before any kernel reads them: a faithful copy loads and
+    computes the same output; a 26-state pair code above 728, CSR bounds out
+    of order and a residual column beyond the weight are refused with
+    CDQ_ERR_FORMAT, and the module keeps its previous buffers."""
+    from cdq_lrr_b200 import _lib as L
+    from cdq_lrr_b200.quant import CAMKII_LATTICE, CAMKII_LATTICE_16, CDQLinear, quantize_cdq_lrr
+    lat = CAMKII_LATTICE if states == 26 else CAMKII_LATTICE_16
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(48, 256, generator=g) * 0.02).to(torch.bfloat16)
+    w[3, 7] = 0.5
+    w[40, 200] = -0.4
+    lin = CDQLinear(quantize_cdq_lrr(w.cuda(), lattice=lat), 256, 48)
+    x = (torch.randn(2, 256, generator=g)).to(torch.bfloat16).cuda()
+    want = lin(x)
+    sd = {k: v.clone() for k, v in lin.state_dict().items()}
+    assert int(sd["res_ent"].numel()) > 0
+    other = CDQLinear(quantize_cdq_lrr(torch.zeros_like(w).cuda(), lattice=lat), 256, 48)
+    other.load_state_dict(sd)
+    assert torch.equal(other(x), want)
+
+    def refused(mutate):
+        bad = {k: v.clone() for k, v in sd.items()}
+        mutate(bad)
+        tgt = CDQLinear(quantize_cdq_lrr(w.cuda(), lattice=lat), 256, 48)
+        before = tgt.units.clone()
+        with pytest.raises(L.CdqError) as ei:
+            tgt.load_state_dict(bad)
+        assert ei.value.status == 5
+        assert torch.equal(tgt.units, before)
+
+    if states == 26:
+        def big_code(sd_):  # lane 0, code word 0: slot 0 = 1023
+            sd_["units"][0] |= 0xFF
+            sd_["units"][1] |= 0x03
+        refused(big_code)
+
+    def csr_order(sd_):
+        sd_["res_ptr"][1] = sd_["res_ptr"][-1] + 1
+    refused(csr_order)
+
+    def col_out(sd_):
+        sd_["res_ent"][0] = (sd_["res_ent"][0] & 0xFFFF) | (300 << 16)
+    refused(col_out)
+
+    def short_units(sd_):
+        sd_["units"] = sd_["units"][:-16]
+    refused(short_units)
