@@ -476,7 +476,20 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
 
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         const int nq = (n_units + 3) >> 2;
-        for (int q = 0; q < nq; ++q) {
+        const int nfull = phantom_item ? 0 : (n_units >> 2);
+        int q0 = 0;
+        for (; q0 < nfull; ++q0) {  // full quads: no per-quad dispatch
+            if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
+                failed = true;
+                break;
+            }
+            quad_step<NS, 4, false>(ring + c_slot * kQuad, lane, c, xp + 256 * q0, -1, lane_base, sig_base, d,
+                                    refill);
+            c_slot ^= 1u;
+            c_phase ^= c_slot == 0 ? 1u : 0u;
+        }
+        if (failed) break;
+        for (int q = q0; q < nq; ++q) {  // the short last quad, or every quad of a phantom item
             if (!mbar_wait(bars + 8 * c_slot, c_phase)) {
                 failed = true;
                 break;
