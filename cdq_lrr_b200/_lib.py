@@ -55,6 +55,21 @@ class cdq_gemv_job(C.Structure):
                 ("out_f32", C.c_int32), ("reserved0", C.c_int32)]
 
 
+class cdq_step_layer(C.Structure):
+    _fields_ = [("q", cdq_gemv_job), ("k", cdq_gemv_job), ("v", cdq_gemv_job), ("o", cdq_gemv_job),
+                ("gate", cdq_gemv_job), ("up", cdq_gemv_job), ("down", cdq_gemv_job),
+                ("ln1", C.c_void_p), ("ln2", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p)]
+
+
+class cdq_step_model(C.Structure):
+    _fields_ = [("layers", C.c_int32), ("hidden", C.c_int32), ("heads", C.c_int32), ("kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("inter", C.c_int32), ("max_len", C.c_int32), ("token_cap", C.c_int32),
+                ("vocab", C.c_int64), ("eps", C.c_float), ("scale", C.c_float)] + [
+                (n, C.c_void_p) for n in ("embed", "norm_w", "lm_w", "cos_t", "sin_t", "pos", "ids", "tokens",
+                                          "count", "best", "next", "logits", "h0", "h1", "q", "k", "v", "att",
+                                          "o", "g", "u", "dn")]
+
+
 class cdq_quant_info(C.Structure):
     _fields_ = [("n_res", C.c_int64), ("k", C.c_int64), ("threshold", C.c_float),
                 ("topk_fallback", C.c_int32), ("mask_count", C.c_int64)]
@@ -88,6 +103,11 @@ _SIGS = {
     "cdq_pack_from_reference_device": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, _P, _P, _P, _P, C.c_int64,
                                                  C.POINTER(cdq_packed), _P, _P]),
     "cdq_check_device_pack": (C.c_int, [C.POINTER(cdq_packed), _P, _P]),
+    "cdq_step_table_bytes": (C.c_int, [C.c_int32, C.POINTER(C.c_int64)]),
+    "cdq_step_prepare": (C.c_int, [C.POINTER(cdq_step_model), C.POINTER(cdq_step_layer), _P]),
+    "cdq_decode_step": (C.c_int, [_P, C.c_int32, _P]),
+    "cdq_step_error": (C.c_int, [_P, C.POINTER(C.c_int32)]),
+    "cdq_step_reset": (C.c_int, [_P, _P]),
     "cdq_file_checkpoints": (C.c_int, [_P, C.c_int64, C.c_int32, C.POINTER(cdq_file_tensor), C.c_int32, _P, _P]),
     "cdq_file_decode_device": (C.c_int, [_P, C.c_int64, C.c_int32, C.c_int64, C.c_int64, C.c_int32, _P, _P,
                                          _P, _P, _P, _P, _P, _P]),

@@ -29,19 +29,15 @@
 #include <algorithm>
 
 #include "cdq.h"
+#include "cdq_decode_math.cuh"
 #include "cdq_internal.cuh"
 
 using cdq::launch_pdl;
 using cdq::pdl_release;
 using cdq::pdl_wait;
+using namespace cdq::dm;
 
 namespace {
-
-__device__ __forceinline__ float bf(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
-__device__ __forceinline__ uint16_t tobf(float v) { return __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
-__device__ __forceinline__ float rbf(float v) { return bf(tobf(v)); }
-
-constexpr int kNormThreads = 256;
 
 // One block per row: row r of h / delta / out is the r-th vector of n values.
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __restrict__ h,
@@ -57,120 +53,39 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(uint16_t* __r
     if (delta) delta += ro;
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += kNormThreads) {
-        float v = bf(h[i]);
+        uint16_t hv = h[i];
         if (delta) {
-            v = rbf(v + bf(delta[i]));
-            h[i] = tobf(v);
+            hv = add_bf(hv, delta[i]);
+            h[i] = hv;
         }
-        ss = fmaf(v, v, ss);
+        ss = fmaf(bf(hv), bf(hv), ss);
     }
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-    for (int k = 0; k < kNormThreads / 32; ++k) tot += red[k];
-    const float r = rsqrtf(tot / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += kNormThreads) {
-        out[i] = tobf(bf(w[i]) * rbf(bf(h[i]) * r));
-    }
+    const float r = norm_scale(norm_total(ss, red), n, eps);
+    for (int i = threadIdx.x; i < n; i += kNormThreads) out[i] = norm_out(w[i], h[i], r);
 }
 
-constexpr int kHd = 64;           // head dimension
-constexpr int kAttnThreads = 128;
-
-// One block per query head. scores[] holds the head's scores (dynamic shared memory, cap floats).
+// One block per query head.
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(
     const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
     const uint16_t* __restrict__ cos_t, const uint16_t* __restrict__ sin_t, const int32_t* __restrict__ pos_p,
     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, int max_len, int n_heads, int n_kv, float scale,
     uint16_t* __restrict__ out, int cap) {
     extern __shared__ float scores[];
-    __shared__ float qe[kHd], ke[kHd], ve[kHd], red[kAttnThreads / 32], part[kHd];
-    const int h = blockIdx.x, tid = threadIdx.x;
+    __shared__ AttnScratch S;
     pdl_wait();
     pdl_release();
-    const int group = n_heads / n_kv, kvh = h / group;
     const int P = *pos_p;
     if (P < 0 || P >= max_len || P >= cap) return;  // the host sizes the cache; nothing to attend otherwise
-    const uint16_t* cs = cos_t + (int64_t)P * kHd;
-    const uint16_t* sn = sin_t + (int64_t)P * kHd;
-    if (tid < kHd) {
-        const int d = tid, o = d < kHd / 2 ? d + kHd / 2 : d - kHd / 2;
-        const float sgn = d < kHd / 2 ? -1.f : 1.f;
-        const float qd = bf(q[h * kHd + d]), qo = bf(q[h * kHd + o]);
-        qe[d] = rbf(rbf(qd * bf(cs[d])) + rbf(sgn * qo * bf(sn[d])));
-        const float kd = bf(k[kvh * kHd + d]), ko = bf(k[kvh * kHd + o]);
-        ke[d] = rbf(rbf(kd * bf(cs[d])) + rbf(sgn * ko * bf(sn[d])));
-        ve[d] = bf(v[kvh * kHd + d]);
-        if (h % group == 0) {  // one block per kv head appends the step's k and v
-            kc[((int64_t)kvh * max_len + P) * kHd + d] = tobf(ke[d]);
-            vc[((int64_t)kvh * max_len + P) * kHd + d] = v[kvh * kHd + d];
-        }
-    }
-    __syncthreads();
-    // scores over positions 0..P (position P from this block's own k)
-    const uint16_t* kb = kc + (int64_t)kvh * max_len * kHd;
-    float mx = -INFINITY;
-    for (int j = tid; j <= P; j += kAttnThreads) {
-        float s = 0.f;
-        if (j < P) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kb + (int64_t)j * kHd);
-#pragma unroll
-            for (int c = 0; c < kHd / 8; ++c) {
-                const uint4 u = kr[c];
-                const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    s = fmaf(qe[8 * c + 2 * t], __uint_as_float(wv[t] << 16), s);
-                    s = fmaf(qe[8 * c + 2 * t + 1], __uint_as_float(wv[t] & 0xFFFF0000u), s);
-                }
-            }
-        } else {
-#pragma unroll 8
-            for (int d = 0; d < kHd; ++d) s = fmaf(qe[d], ke[d], s);
-        }
-        s *= scale;
-        scores[j] = s;
-        mx = fmaxf(mx, s);
-    }
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int k2 = 1; k2 < kAttnThreads / 32; ++k2) mx = fmaxf(mx, red[k2]);
-    __syncthreads();
-    float sum = 0.f;
-    for (int j = tid; j <= P; j += kAttnThreads) {
-        const float e = expf(scores[j] - mx);
-        scores[j] = e;
-        sum += e;
-    }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-    __syncthreads();
-    if ((tid & 31) == 0) red[tid >> 5] = sum;
-    __syncthreads();
-    sum = 0.f;
-    for (int k2 = 0; k2 < kAttnThreads / 32; ++k2) sum += red[k2];
-    // weighted values: thread (half, d) takes positions of one parity
-    const int d = tid & (kHd - 1), half = tid / kHd;
-    const uint16_t* vb = vc + (int64_t)kvh * max_len * kHd;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int j = half; j < P; j += 2) acc = fmaf(scores[j], bf(vb[(int64_t)j * kHd + d]), acc);
-    if ((P & 1) == half) acc = fmaf(scores[P], ve[d], acc);  // the step's own value
-    if (half == 1) part[d] = acc;
-    __syncthreads();
-    if (half == 0) out[h * kHd + d] = tobf((acc + part[d]) / sum);
+    attn_head(blockIdx.x, threadIdx.x, q, k, v, cos_t + (int64_t)P * kHd, sin_t + (int64_t)P * kHd, P, kc, vc,
+              max_len, n_heads, n_kv, scale, out, scores, S);
 }
 
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
                                 uint16_t* __restrict__ out, int n) {
     pdl_wait();
     pdl_release();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float x = bf(g[i]);
-        out[i] = tobf(rbf(x / (1.f + expf(-x))) * bf(u[i]));
-    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = silu_mul(g[i], u[i]);
 }
 
 __global__ void advance_kernel(const int64_t* __restrict__ next, int64_t* __restrict__ ids,
@@ -183,15 +98,6 @@ __global__ void advance_kernel(const int64_t* __restrict__ next, int64_t* __rest
     *ids = *next;
     *pos += 1;
     *count = c + 1;
-}
-
-// The argmax key of a bf16 logit: orderable bits of the value (NaN above
-// every number) above the complemented index (the first index wins ties).
-__device__ __forceinline__ unsigned long long argmax_key(uint16_t v, uint32_t idx) {
-    uint32_t b = v == 0x8000u ? 0u : v;                 // -0 equals +0
-    if ((b & 0x7FFFu) > 0x7F80u) b = 0xFFFFu;           // every NaN: the largest key
-    else b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
-    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - idx);
 }
 
 __global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int64_t* __restrict__ ids,
@@ -214,17 +120,11 @@ __global__ void __launch_bounds__(kNormThreads) embed_rmsnorm_kernel(const int64
         h[i] = v;
         ss = fmaf(bf(v), bf(v), ss);
     }
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-    for (int k = 0; k < kNormThreads / 32; ++k) tot += red[k];
-    const float r = rsqrtf(tot / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += kNormThreads) out[i] = tobf(bf(w[i]) * rbf(bf(h[i]) * r));
+    const float r = norm_scale(norm_total(ss, red), n, eps);
+    for (int i = threadIdx.x; i < n; i += kNormThreads) out[i] = norm_out(w[i], h[i], r);
 }
 
 constexpr int kLmThreads = 256;
-constexpr int kLmRows = 4;  // rows per warp step (loads in flight)
 
 // For each of the M activation rows m: logits[m][r] = bf16(sum_k x[m][k] *
 // w[r][k]) (fp32, lane-chunk order then a warp reduction: the same
@@ -242,58 +142,13 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_argmax_kernel(const uint16
     for (int i = threadIdx.x; i < M * n; i += kLmThreads) xs[i] = bf(x[i]);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nch = n / 8;  // 16-byte chunks per row
     const int64_t nw = (int64_t)gridDim.x * (kLmThreads / 32);
     unsigned long long key[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) key[m] = 0ull;
     constexpr int kRows = M == 1 ? kLmRows : 1;  // vocabulary rows per warp step
-    for (int64_t r0 = ((int64_t)blockIdx.x * (kLmThreads / 32) + warp) * kRows; r0 < vocab; r0 += nw * kRows) {
-        float acc[kRows][M];
-#pragma unroll
-        for (int t = 0; t < kRows; ++t)
-#pragma unroll
-            for (int m = 0; m < M; ++m) acc[t][m] = 0.f;
-        for (int ch = lane; ch < nch; ch += 32) {
-            uint4 u[kRows];
-#pragma unroll
-            for (int t = 0; t < kRows; ++t)
-                u[t] = r0 + t < vocab ? __ldcs(reinterpret_cast<const uint4*>(w + (r0 + t) * (int64_t)n) + ch)
-                                      : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const float4 xa = *reinterpret_cast<const float4*>(xs + m * n + 8 * ch);
-                const float4 xb = *reinterpret_cast<const float4*>(xs + m * n + 8 * ch + 4);
-#pragma unroll
-                for (int t = 0; t < kRows; ++t) {
-                    float a = acc[t][m];
-                    a = fmaf(__uint_as_float(u[t].x << 16), xa.x, a);
-                    a = fmaf(__uint_as_float(u[t].x & 0xFFFF0000u), xa.y, a);
-                    a = fmaf(__uint_as_float(u[t].y << 16), xa.z, a);
-                    a = fmaf(__uint_as_float(u[t].y & 0xFFFF0000u), xa.w, a);
-                    a = fmaf(__uint_as_float(u[t].z << 16), xb.x, a);
-                    a = fmaf(__uint_as_float(u[t].z & 0xFFFF0000u), xb.y, a);
-                    a = fmaf(__uint_as_float(u[t].w << 16), xb.z, a);
-                    a = fmaf(__uint_as_float(u[t].w & 0xFFFF0000u), xb.w, a);
-                    acc[t][m] = a;
-                }
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < kRows; ++t) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                float a = acc[t][m];
-                for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
-                if (r0 + t < vocab) {
-                    const uint16_t v = tobf(a);
-                    if (lane == 0 && logits) logits[(int64_t)m * vocab + r0 + t] = v;
-                    const unsigned long long k = argmax_key(v, (uint32_t)(r0 + t));
-                    key[m] = k > key[m] ? k : key[m];
-                }
-            }
-        }
-    }
+    for (int64_t r0 = ((int64_t)blockIdx.x * (kLmThreads / 32) + warp) * kRows; r0 < vocab; r0 += nw * kRows)
+        lm_rows<M, kRows>(w, xs, n, vocab, r0, lane, logits, key);
 #pragma unroll
     for (int m = 0; m < M; ++m)
         if (lane == 0 && key[m]) atomicMax(best + m, key[m]);
@@ -304,8 +159,7 @@ __global__ void argmax_token_kernel(unsigned long long* __restrict__ best, int64
     pdl_wait();
     pdl_release();
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
-        const unsigned long long k = best[i];
-        next[i] = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        next[i] = key_token(best[i]);
         best[i] = 0ull;
     }
 }
@@ -345,70 +199,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_multi_kernel(
     const int32_t* __restrict__ pos_p, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc, int max_len,
     int n_heads, int n_kv, float scale, uint16_t* __restrict__ out, int cap) {
     extern __shared__ float scores[];
-    __shared__ float qe[kHd], red[kAttnThreads / 32], part[kHd];
+    __shared__ AttnScratch S;
     const int h = blockIdx.x, qi = blockIdx.y, tid = threadIdx.x;
     pdl_wait();
     pdl_release();
     const int group = n_heads / n_kv, kvh = h / group;
     const int P = *pos_p + qi;
     if (P < 0 || P >= max_len || P >= cap) return;
-    const uint16_t* qq = q + (int64_t)qi * n_heads * kHd;
-    uint16_t* oq = out + (int64_t)qi * n_heads * kHd;
-    const uint16_t* cs = cos_t + (int64_t)P * kHd;
-    const uint16_t* sn = sin_t + (int64_t)P * kHd;
-    if (tid < kHd) {
-        const int d = tid, o = d < kHd / 2 ? d + kHd / 2 : d - kHd / 2;
-        const float sgn = d < kHd / 2 ? -1.f : 1.f;
-        const float qd = bf(qq[h * kHd + d]), qo = bf(qq[h * kHd + o]);
-        qe[d] = rbf(rbf(qd * bf(cs[d])) + rbf(sgn * qo * bf(sn[d])));
-    }
-    __syncthreads();
     const uint16_t* kb = kc + (int64_t)kvh * max_len * kHd;
-    float mx = -INFINITY;
-    for (int j = tid; j <= P; j += kAttnThreads) {
-        float s = 0.f;
-        const uint4* kr = reinterpret_cast<const uint4*>(kb + (int64_t)j * kHd);
-#pragma unroll
-        for (int c = 0; c < kHd / 8; ++c) {
-            const uint4 u = kr[c];
-            const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                s = fmaf(qe[8 * c + 2 * t], __uint_as_float(wv[t] << 16), s);
-                s = fmaf(qe[8 * c + 2 * t + 1], __uint_as_float(wv[t] & 0xFFFF0000u), s);
-            }
-        }
-        s *= scale;
-        scores[j] = s;
-        mx = fmaxf(mx, s);
-    }
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int k2 = 1; k2 < kAttnThreads / 32; ++k2) mx = fmaxf(mx, red[k2]);
-    __syncthreads();
-    float sum = 0.f;
-    for (int j = tid; j <= P; j += kAttnThreads) {
-        const float e = expf(scores[j] - mx);
-        scores[j] = e;
-        sum += e;
-    }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-    __syncthreads();
-    if ((tid & 31) == 0) red[tid >> 5] = sum;
-    __syncthreads();
-    sum = 0.f;
-    for (int k2 = 0; k2 < kAttnThreads / 32; ++k2) sum += red[k2];
-    const int d = tid & (kHd - 1), half = tid / kHd;
     const uint16_t* vb = vc + (int64_t)kvh * max_len * kHd;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int j = half; j < P; j += 2) acc = fmaf(scores[j], bf(vb[(int64_t)j * kHd + d]), acc);
-    if ((P & 1) == half) acc = fmaf(scores[P], bf(vb[(int64_t)P * kHd + d]), acc);
-    if (half == 1) part[d] = acc;
+    if (tid < kHd) {
+        const int d = tid;
+        S.qe[d] = rope(q + (int64_t)qi * n_heads * kHd + h * kHd, d, cos_t + (int64_t)P * kHd,
+                       sin_t + (int64_t)P * kHd);
+        // the position's own key and value, as rope_append_kernel stored them
+        // (the same bits the single-token kernel keeps in registers)
+        S.ke[d] = bf(kb[(int64_t)P * kHd + d]);
+        S.ve[d] = bf(vb[(int64_t)P * kHd + d]);
+    }
     __syncthreads();
-    if (half == 0) oq[h * kHd + d] = tobf((acc + part[d]) / sum);
+    attn_core(tid, kb, vb, P, scale, out + (int64_t)qi * n_heads * kHd + h * kHd, scores, S);
 }
 
 }  // namespace

@@ -39,6 +39,7 @@
 
 #include "cdq.h"
 #include "cdq_common.cuh"
+#include "cdq_decode_math.cuh"
 #include "cdq_internal.cuh"
 
 namespace cdq {
@@ -577,6 +578,7 @@ __global__ void __launch_bounds__(kFixThreads) fixup_kernel(const __grid_constan
 
 #include "cdq_tile.cuh"
 #include "cdq_stream.cuh"
+#include "cdq_step.cuh"
 
 // The fix-up pass over every job (one thread per padded row and batch row).
 template <int MAXJ>
@@ -718,6 +720,51 @@ cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cud
 }
 
 void gemv_set_tile_min_batch(int m) { g_tile_min_batch = m; }
+
+bool step_smem_layout(StepParams& p) {
+    constexpr uint32_t top = stream::Ring<26>::kTop > stream::Ring<16>::kTop ? stream::Ring<26>::kTop
+                                                                              : stream::Ring<16>::kTop;
+    auto up16 = [](uint64_t a) { return (a + 15) / 16 * 16; };
+    const uint64_t xs = up16(top);
+    const uint64_t xf = up16(xs + 2ull * (uint64_t)std::max(std::max(p.hidden, p.inter), p.heads * dm::kHd));
+    const uint64_t scr = up16(xf + 4ull * (uint64_t)p.hidden);
+    const uint64_t sc = up16(scr + step::kScrBytes);
+    const uint64_t end = up16(sc + 4ull * (uint64_t)p.max_len);
+    if (end > kSmemBytes) return false;
+    p.xs_addr = (uint32_t)xs;
+    p.xf_addr = (uint32_t)xf;
+    p.scr_addr = (uint32_t)scr;
+    p.sc_addr = (uint32_t)sc;
+    // the rest of the window stages residual data: a quarter bounds, the rest entries
+    const uint64_t words = (kSmemBytes - end) / 4;
+    p.rst_addr = (uint32_t)end;
+    p.rst_bnd_cap = (int32_t)(words / 4);
+    p.rst_ent_cap = (int32_t)(words - words / 4);
+    return true;
+}
+
+// One cooperative launch (every CTA resident, one per SM) of the persistent
+// decode step.
+cudaError_t step_launch(const StepParams* dev_params, int ns, int sms, cudaStream_t s) {
+    auto kern = ns == 26 ? step::decode_step_kernel<26> : step::decode_step_kernel<16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, stream::kSThreads, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)sms);
+    cfg.blockDim = dim3(stream::kSThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, dev_params);
+}
 
 cudaError_t gemv_read_error(int* out) {
     int v = 0;

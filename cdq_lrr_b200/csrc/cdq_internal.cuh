@@ -79,6 +79,71 @@ cudaError_t gemv_launch_grouped(const GemvBatch<kMaxJobs>& b, int ns, int m, cud
 cudaError_t gemv_read_error(int* out);
 void gemv_set_tile_min_batch(int m);
 
+// ---- persistent decode step (one cooperative launch per token) ----
+constexpr int kStepPhaseJobs = 3;
+// One projection group of a decoder layer (the jobs that share an input: q/k/v,
+// o, gate/up, down), laid out as the streaming kernel's batch view: units of
+// the jobs in job order (unit_begin set), x unused (the input is in shared
+// memory), m = 1.
+struct StepGroup {
+    int32_t n;
+    int32_t reserved0;
+    int64_t total_units;
+    GemvJob jobs[kStepPhaseJobs];
+};
+struct StepLayer {
+    StepGroup qkv, o, gu, down;
+    const uint16_t* ln1;
+    const uint16_t* ln2;
+    uint16_t* kc;
+    uint16_t* vc;
+};
+// The residual data one CTA needs for one projection group (the CSR bounds
+// and entries of the buckets of its items, per job), staged into its shared
+// memory by asynchronous copies issued before the barrier that precedes the
+// group: per job k, bounds [b0, b0 + nb) and entries [e0, e0 + ne). ok = 0:
+// too large for the stage buffers (the CTA reads them from global memory).
+struct StepStage {
+    int32_t n, ok, nb_total, ne_total;
+    int32_t b0[kStepPhaseJobs], nb[kStepPhaseJobs], e0[kStepPhaseJobs], ne[kStepPhaseJobs];
+};
+static_assert(sizeof(StepStage) == 64, "StepStage layout");
+
+// Everything the persistent kernel reads, in device memory: this record, then
+// the layers, then the stage descriptors [layer][group][CTA], then three sync
+// words (barrier arrivals, barrier generation, error code).
+struct StepParams {
+    int32_t layers, hidden, heads, kv_heads, inter, max_len, token_cap, n_states;
+    int64_t vocab;
+    float eps, scale;
+    const uint16_t* embed;
+    const uint16_t* norm_w;
+    const uint16_t* lm_w;
+    const uint16_t* cos_t;
+    const uint16_t* sin_t;
+    int32_t* pos;
+    int64_t* ids;
+    int64_t* tokens;
+    int32_t* count;
+    unsigned long long* best;
+    int64_t* next;
+    uint16_t* logits;
+    uint16_t* h[2];
+    uint16_t *q, *k, *v, *att, *o, *g, *u, *dn;
+    uint32_t xs_addr, xf_addr, sc_addr, scr_addr;  // shared-window addresses of the kernel's buffers
+    uint32_t rst_addr;                             // residual stage: bounds, then entries
+    int32_t rst_bnd_cap, rst_ent_cap;              // stage capacities (uint32 words)
+    int32_t n_ctas;                                // the grid the stage descriptors were made for
+    const StepLayer* layer;
+    const StepStage* stage;
+    uint32_t* sync;
+    int64_t reserved_tail;  // 16-byte multiple (the kernel copies this record into shared memory)
+};
+// Shared-window layout of the persistent kernel above the streaming rings:
+// returns false if the model's buffers do not fit.
+bool step_smem_layout(StepParams& p);
+cudaError_t step_launch(const StepParams* dev_params, int ns, int sms, cudaStream_t s);
+
 cudaError_t dequant_setup();
 cudaError_t quantize_setup();
 cudaError_t dequant_launch(const cdq_packed& w, uint16_t* out, cudaStream_t s);

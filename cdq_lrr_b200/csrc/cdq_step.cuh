@@ -1,0 +1,451 @@
+// The persistent decode step: one cooperative launch runs a whole batch-1
+// token of a Qwen2-style decoder (every layer's norms, CDQ projections,
+// attention and MLP, then the lm_head with its argmax and the token advance),
+// with grid-wide barriers between the steps that depend on one another, so
+// no launch latency, no prologue and no pair-table build is paid per
+// operation. Included by cdq_gemv.cu (it runs the streaming kernel's per-warp
+// stretch code, stream_warp, on every projection group).
+//
+// Per layer, every CTA:
+//   A  h' = h + down (layer 0: the embedding row), x = RMSNorm(h') into its own
+//      shared memory (CTA 0 also writes h' to the other hidden buffer), the
+//      residual sums of its q/k/v items from that x, then its q/k/v stretches
+//      (activations from shared memory)                         -> barrier
+//   B  CTAs 0 .. heads-1: rotary embedding, cache append and attention of
+//      one query head                                           -> barrier
+//   C  x = the attention output, residual sums and o_proj       -> barrier
+//   D  h'' = h' + o, x = RMSNorm(h''), gate/up                  -> barrier
+//   E  x = SiLU(gate) * up, down_proj                           -> barrier
+// then RMSNorm of h'' + down, the lm_head rows of every warp with their argmax
+// keys (atomicMax), a barrier, and CTA 0 turns the key into the next token.
+// Every operation uses the same device functions and arithmetic as the
+// one-kernel-per-operation step (cdq_decode_math.cuh, stream_warp, the
+// residual pre-pass's per-bucket sums), so the two steps give the same bits.
+//
+// The barrier: thread 0 of each CTA arrives on a counter; the last arrival
+// resets it and bumps a generation word that the others poll (bounded; on
+// timeout the error word is set and every CTA leaves at its next barrier).
+// The cooperative launch guarantees that all CTAs are resident, one per SM.
+
+namespace step {
+
+using namespace stream;
+
+constexpr uint32_t kBarrierPolls = 1u << 22;
+
+// The scratch region of the shared window (offsets from its start): the
+// attention scratch, the norm's warp partials, the barrier flag, then copies
+// of the step's parameters, of the projection group being run and of this
+// CTA's stage descriptor (read many times per group: shared memory instead of
+// L2 round trips).
+constexpr uint32_t al16(uint32_t b) { return (b + 15u) / 16u * 16u; }
+constexpr uint32_t kScrRed = al16(sizeof(dm::AttnScratch));
+constexpr uint32_t kScrFlag = kScrRed + 16 * 4;
+constexpr uint32_t kScrParams = al16(kScrFlag + 16);
+constexpr uint32_t kScrGroup = al16(kScrParams + sizeof(StepParams));
+constexpr uint32_t kScrStage = al16(kScrGroup + sizeof(StepGroup));
+constexpr uint32_t kScrBytes = al16(kScrStage + sizeof(StepStage));
+static_assert(sizeof(StepParams) % 16 == 0 && sizeof(StepGroup) % 16 == 0 && sizeof(StepStage) % 16 == 0,
+              "shared copies go in 16-byte words");
+
+// Copies n bytes (a multiple of 16, both 16-byte aligned) from global to
+// shared memory with the CTA's threads; the caller synchronises.
+__device__ __forceinline__ void copy_to_shared(void* dst, const void* src, uint32_t n) {
+    for (uint32_t i = threadIdx.x; i < n / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// false: the barrier gave up (or an earlier one did): the caller leaves.
+// gen: the barrier generation as thread 0 of this CTA last saw it (read once
+// at kernel start, then advanced locally). ok_s: a word of the CTA's shared
+// window (no static shared memory: the streaming layout needs the dynamic
+// window at the start of the CTA's).
+__device__ __forceinline__ bool grid_barrier(uint32_t* sync, uint32_t n_ctas, uint32_t& gen,
+                                             volatile uint32_t& ok_s) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t ok = 1u;
+        __threadfence();
+        if (atomicAdd(sync, 1u) == n_ctas - 1) {
+            atomicExch(sync, 0u);
+            __threadfence();
+            atomicAdd(sync + 1, 1u);
+        } else {
+            uint32_t polls = 0;
+            while (ld_acquire(sync + 1) == gen) {
+                if (++polls >= kBarrierPolls) {
+                    atomicExch(sync + 2, 1u);
+                    ok = 0u;
+                    break;
+                }
+                if ((polls & 255u) == 0u) {
+                    if (ld_acquire(sync + 2) != 0u) {  // another CTA gave up
+                        ok = 0u;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        ++gen;
+        __threadfence();
+        if (ld_acquire(sync + 2) != 0u) ok = 0u;
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0u;
+}
+
+// Residual sums of the items of `batch` whose first unit lies in
+// [u_lo, u_hi) (this CTA's stretches), with the activation row x in shared
+// memory: one thread per (item, row) bucket, each bucket's entries added in
+// order (the residual pre-pass's arithmetic), into the workspace slots the
+// items' warps read.
+__device__ __forceinline__ void cta_residual_sums(const StepGroup& batch, int u_lo, int u_hi, const uint16_t* xs) {
+    const Cursor c0 = first_at(batch, u_lo), c1 = first_at(batch, u_hi);
+    for (int j = c0.j; j <= c1.j && j < batch.n; ++j) {
+        const GemvJob& J = batch.jobs[j];
+        const int kg = J.kg, cols = J.cols;
+        const int i_lo = j == c0.j ? c0.b16 * kg + c0.grp : 0;
+        const int i_hi = j == c1.j ? c1.b16 * kg + c1.grp : J.r16 * kg;
+        const uint32_t n_res = J.n_res;
+        const int64_t rpad = (int64_t)J.r16 * 16;
+        const uint32_t* __restrict__ rp = J.res_ptr;
+        const uint32_t* __restrict__ re = J.res_ent;
+        for (int e = threadIdx.x; e < (i_hi - i_lo) * 16; e += kSThreads) {
+            const int it = i_lo + (e >> 4), ri = e & 15;
+            const int b16 = it / kg, grp = it - b16 * kg;
+            const int row = b16 * 16 + ri;
+            const int64_t bucket = (int64_t)row * kg + grp;
+            const uint32_t s = min(__ldg(rp + bucket), n_res);
+            const uint32_t t = min(max(__ldg(rp + bucket + 1), s), n_res);
+            float acc = 0.f;
+            for (uint32_t k0 = s; k0 < t; k0 += 8) {  // eight loads in flight, then the fmas in order
+                uint32_t en[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) en[i] = k0 + i < t ? __ldg(re + k0 + i) : 0xFFFF0000u;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t col = en[i] >> 16;
+                    if (k0 + i < t && col < (uint32_t)cols)
+                        acc = fmaf(__uint_as_float(en[i] << 16), __uint_as_float((uint32_t)xs[col] << 16), acc);
+                }
+            }
+            J.partial[(int64_t)grp * rpad + row] = acc;
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Issues this CTA's residual stage copies for a group (every thread; one
+// cp.async group per thread, waited for in run_group).
+__device__ __forceinline__ void stage_issue(const StepStage& d, const StepGroup& G, const StepParams& P) {
+    if (d.ok) {
+        uint32_t bo = P.rst_addr, eo = P.rst_addr + 4u * (uint32_t)P.rst_bnd_cap;
+        for (int k = 0; k < d.n; ++k) {
+            const GemvJob& J = G.jobs[k];
+            for (int i = threadIdx.x; i < d.nb[k]; i += kSThreads) cp_async4(bo + 4u * i, J.res_ptr + d.b0[k] + i);
+            for (int i = threadIdx.x; i < d.ne[k]; i += kSThreads) cp_async4(eo + 4u * i, J.res_ent + d.e0[k] + i);
+            bo += 4u * (uint32_t)d.nb[k];
+            eo += 4u * (uint32_t)d.ne[k];
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// cta_residual_sums from the staged bounds and entries (the same buckets, the
+// same order of fmas).
+__device__ __forceinline__ void cta_residual_sums_staged(const StepGroup& batch, const StepStage& d, int u_lo,
+                                                         int u_hi, const uint16_t* xs, const uint32_t* bnd,
+                                                         const uint32_t* ent) {
+    const Cursor c0 = first_at(batch, u_lo), c1 = first_at(batch, u_hi);
+    int bo = 0, eo = 0;
+    for (int j = 0; j < batch.n; ++j) {
+        const GemvJob& J = batch.jobs[j];
+        if (j >= c0.j && j <= c1.j) {
+            const int kg = J.kg, cols = J.cols;
+            const int i_lo = j == c0.j ? c0.b16 * kg + c0.grp : 0;
+            const int i_hi = j == c1.j ? c1.b16 * kg + c1.grp : J.r16 * kg;
+            const int64_t rpad = (int64_t)J.r16 * 16;
+            const uint32_t e0 = (uint32_t)d.e0[j], e1 = e0 + (uint32_t)d.ne[j];
+            for (int e = threadIdx.x; e < (i_hi - i_lo) * 16; e += kSThreads) {
+                const int it = i_lo + (e >> 4), ri = e & 15;
+                const int b16 = it / kg, grp = it - b16 * kg;
+                const int row = b16 * 16 + ri;
+                const int bl = row * kg + grp - d.b0[j];  // the bucket in the stage
+                const uint32_t s = min(max(bnd[bo + bl], e0), e1);
+                const uint32_t t = min(max(bnd[bo + bl + 1], s), e1);
+                float acc = 0.f;
+                for (uint32_t k = s; k < t; ++k) {
+                    const uint32_t en = ent[eo + (k - e0)], col = en >> 16;
+                    if (col < (uint32_t)cols)
+                        acc = fmaf(__uint_as_float(en << 16), __uint_as_float((uint32_t)xs[col] << 16), acc);
+                }
+                J.partial[(int64_t)grp * rpad + row] = acc;
+            }
+        }
+        bo += d.nb[j];
+        eo += d.ne[j];
+    }
+}
+
+// A warp's stretch of a projection group: opened (first two weight copies
+// issued, the rest of its weights prefetched into L2) before the barrier that
+// precedes the group, so those copies fly during the barrier and the steps
+// before the group.
+template <int NS>
+__device__ __forceinline__ Stretch open_group(const StepParams& P, int l, int gi, const StepGroup& Gg, uint32_t ring,
+                                              uint32_t bars, const RingState& rs, StepGroup& G, StepStage& D) {
+    copy_to_shared(&G, &Gg, sizeof(StepGroup));
+    copy_to_shared(&D, &P.stage[((int64_t)l * 4 + gi) * P.n_ctas + blockIdx.x], sizeof(StepStage));
+    __syncthreads();
+    stage_issue(D, G, P);
+    const int64_t U = G.total_units;
+    const int64_t nw = (int64_t)gridDim.x * kSWarps;
+    const int64_t gw = (int64_t)blockIdx.x * kSWarps + (threadIdx.x >> 5);
+    return stretch_open<NS>(G, (int)stretch_bound(U, gw, nw), (int)stretch_bound(U, gw + 1, nw), ring, bars, rs,
+                            true);
+}
+
+// Runs an opened projection group: the CTA builds the group's input in shared
+// memory (`prep`, every thread, CTA barriers allowed) and its residual sums,
+// then each warp streams its stretch. CTA-uniform result.
+template <int NS, class Prep>
+__device__ __forceinline__ bool run_group(Stretch& st, const StepGroup& G, const StepStage& d, const uint16_t* xs,
+                                          uint32_t xs_addr, const uint32_t* bnd, const uint32_t* ent, uint32_t ring,
+                                          uint32_t bars, RingState& rs, Prep&& prep) {
+    const int64_t U = G.total_units;
+    const int64_t nw = (int64_t)gridDim.x * kSWarps;
+    const int64_t cta0 = (int64_t)blockIdx.x * kSWarps;
+    prep();
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's stage copies
+    __syncthreads();                                   // everyone's
+    const int lo = (int)stretch_bound(U, cta0, nw), hi = (int)stretch_bound(U, cta0 + kSWarps, nw);
+    if (d.ok) cta_residual_sums_staged(G, d, lo, hi, xs, bnd, ent);
+    else cta_residual_sums(G, lo, hi, xs);
+    __syncthreads();
+    const bool ok = stretch_run<NS, 1, XShared>(st, G, ring, bars, rs,
+                                                [xs_addr](const uint16_t*) { return XShared{xs_addr}; });
+    return __syncthreads_and(ok) != 0;
+}
+
+// x = RMSNorm(h_in (+ delta)) with weight w into xs (shared, bf16), threads
+// 0 .. 255 in the one-kernel step's order; h_out (CTA 0 only) receives the
+// residual sum. emb: the embedding row instead of h_in + delta (layer 0).
+__device__ __forceinline__ void norm_into(const uint16_t* h_in, const uint16_t* delta, const uint16_t* emb,
+                                          bool emb_ok, const uint16_t* w, float eps, int n, uint16_t* h_out,
+                                          uint16_t* xs, float* red) {
+    using namespace dm;
+    constexpr int kKeep = 4;  // weights of the first kKeep strides held from the first pass
+    const int tid = threadIdx.x;
+    float ss = 0.f;
+    uint16_t wk[kKeep];
+    if (tid < kNormThreads) {
+        // kKeep strides at a time: every load of a batch issued before its stores
+        for (int i0 = tid; i0 < n; i0 += kKeep * kNormThreads) {
+            uint16_t a[kKeep], b[kKeep];
+#pragma unroll
+            for (int k = 0; k < kKeep; ++k) {
+                const int i = i0 + k * kNormThreads;
+                a[k] = i < n ? (emb ? (emb_ok ? emb[i] : (uint16_t)0) : h_in[i]) : (uint16_t)0;
+                b[k] = i < n && !emb ? delta[i] : (uint16_t)0;
+                if (i0 == tid) wk[k] = i < n ? w[i] : (uint16_t)0;
+            }
+#pragma unroll
+            for (int k = 0; k < kKeep; ++k) {
+                const int i = i0 + k * kNormThreads;
+                if (i < n) {
+                    const uint16_t hv = emb ? a[k] : add_bf(a[k], b[k]);
+                    xs[i] = hv;
+                    if (h_out) h_out[i] = hv;
+                    ss = fmaf(bf(hv), bf(hv), ss);
+                }
+            }
+        }
+    }
+    const float r = norm_scale(norm_total(ss, red), n, eps);
+    if (tid < kNormThreads) {
+#pragma unroll
+        for (int k = 0; k < kKeep; ++k)
+            if (tid + k * kNormThreads < n) xs[tid + k * kNormThreads] = norm_out(wk[k], xs[tid + k * kNormThreads], r);
+        for (int i = tid + kKeep * kNormThreads; i < n; i += kNormThreads) xs[i] = norm_out(w[i], xs[i], r);
+    }
+    __syncthreads();
+}
+
+// A projection group succeeded in every warp of the CTA (CTA-uniform, so the
+// CTA leaves the layer loop as a whole).
+__device__ __forceinline__ bool group_ok(bool warp_ok) { return __syncthreads_and(warp_ok) != 0; }
+
+template <int NS>
+__global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepParams* __restrict__ params) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const StepParams& Pg = *params;
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+    if (s0 > kLowStage || s0 + kSmemBytes < Ring<NS>::kTop) {
+        if (threadIdx.x == 0) atomicExch(&g_gemv_error, 1);
+        return;
+    }
+    if (Pg.n_states != NS) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + 2, 3u);
+        return;
+    }
+    if (ld_acquire(Pg.sync + 2) != 0u) return;  // an earlier step failed: reset first
+    if ((int)gridDim.x != Pg.n_ctas) {           // the stage descriptors are per CTA
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + 2, 4u);
+        return;
+    }
+    uint8_t* const base = smem - s0;  // generic pointer of shared address 0
+    StepParams& P = *reinterpret_cast<StepParams*>(base + Pg.scr_addr + kScrParams);
+    copy_to_shared(&P, &Pg, sizeof(StepParams));
+    build_tables<NS>(base);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ring = ring_of<NS>(warp);
+    const uint32_t bars = kBarAddr + warp * kSlots * 8;
+    if (lane == 0) {
+        for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    uint16_t* const xs = reinterpret_cast<uint16_t*>(base + Pg.xs_addr);
+    float* const xf = reinterpret_cast<float*>(base + Pg.xf_addr);
+    float* const scores = reinterpret_cast<float*>(base + Pg.sc_addr);
+    dm::AttnScratch& S = *reinterpret_cast<dm::AttnScratch*>(base + Pg.scr_addr);
+    float* const red = reinterpret_cast<float*>(base + Pg.scr_addr + kScrRed);
+    volatile uint32_t& bar_ok = *reinterpret_cast<volatile uint32_t*>(base + Pg.scr_addr + kScrFlag);
+    StepGroup& Gs = *reinterpret_cast<StepGroup*>(base + Pg.scr_addr + kScrGroup);
+    StepStage& Ds = *reinterpret_cast<StepStage*>(base + Pg.scr_addr + kScrStage);
+    const uint32_t* const bnd = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr);
+    const uint32_t* const ent = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr + 4u * (uint32_t)Pg.rst_bnd_cap);
+    __syncthreads();
+
+    const uint32_t n_ctas = gridDim.x;
+    const int H = P.hidden, I = P.inter;
+    const int pos = *P.pos;
+    const bool pos_ok = pos >= 0 && pos < P.max_len;
+    const int64_t id = *P.ids;
+    RingState rs{0u, 0u};
+    bool ok = true;
+    uint32_t gen = threadIdx.x == 0 ? ld_acquire(P.sync + 1) : 0u;  // barrier generation (thread 0)
+    auto barrier = [&]() { return grid_barrier(P.sync, n_ctas, gen, bar_ok); };
+    Stretch st = open_group<NS>(P, 0, 0, P.layer[0].qkv, ring, bars, rs, Gs, Ds);
+    bool live = true;  // st holds copies in flight
+    for (int l = 0; l < P.layers; ++l) {
+        const StepLayer& L = P.layer[l];
+        // A: x = RMSNorm(h + down) (layer 0: the embedding row); q, k, v
+        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+                           bars, rs, [&]() {
+            if (l == 0)
+                norm_into(nullptr, nullptr, P.embed + (id >= 0 && id < P.vocab ? id : 0) * (int64_t)H,
+                          id >= 0 && id < P.vocab, L.ln1, P.eps, H, blockIdx.x == 0 ? P.h[1] : nullptr, xs, red);
+            else
+                norm_into(P.h[0], P.dn, nullptr, false, L.ln1, P.eps, H, blockIdx.x == 0 ? P.h[1] : nullptr, xs,
+                          red);
+        });
+        live = false;
+        if (!ok) break;
+        st = open_group<NS>(P, l, 1, L.o, ring, bars, rs, Gs, Ds);
+        live = true;
+        if (!barrier()) break;
+        // B: attention, one CTA per query head
+        if ((int)blockIdx.x < P.heads && pos_ok)
+            dm::attn_head(blockIdx.x, threadIdx.x, P.q, P.k, P.v, P.cos_t + (int64_t)pos * dm::kHd,
+                          P.sin_t + (int64_t)pos * dm::kHd, pos, L.kc, L.vc, P.max_len, P.heads, P.kv_heads,
+                          P.scale, P.att, scores, S);
+        if (!barrier()) break;
+        // C: o_proj of the attention output
+        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+                           bars, rs, [&]() {
+            const uint16_t* ap = P.att;
+            const int na = P.heads * dm::kHd;
+            for (int i0 = threadIdx.x; i0 < na; i0 += 4 * kSThreads) {
+                uint16_t a[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) a[k] = i0 + k * kSThreads < na ? ap[i0 + k * kSThreads] : (uint16_t)0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (i0 + k * kSThreads < na) xs[i0 + k * kSThreads] = a[k];
+            }
+            __syncthreads();
+        });
+        live = false;
+        if (!ok) break;
+        st = open_group<NS>(P, l, 2, L.gu, ring, bars, rs, Gs, Ds);
+        live = true;
+        if (!barrier()) break;
+        // D: x = RMSNorm(h' + o); gate, up
+        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+                           bars, rs, [&]() {
+            norm_into(P.h[1], P.o, nullptr, false, L.ln2, P.eps, H, blockIdx.x == 0 ? P.h[0] : nullptr, xs, red);
+        });
+        live = false;
+        if (!ok) break;
+        st = open_group<NS>(P, l, 3, L.down, ring, bars, rs, Gs, Ds);
+        live = true;
+        if (!barrier()) break;
+        // E: x = SiLU(gate) * up; down
+        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+                           bars, rs, [&]() {
+            const uint16_t* gp = P.g;
+            const uint16_t* up = P.u;
+            for (int i0 = threadIdx.x; i0 < I; i0 += 8 * kSThreads) {  // eight loads in flight per thread
+                uint16_t a[8], b[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int i = i0 + k * kSThreads;
+                    a[k] = i < I ? gp[i] : (uint16_t)0;
+                    b[k] = i < I ? up[i] : (uint16_t)0;
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (i0 + k * kSThreads < I) xs[i0 + k * kSThreads] = dm::silu_mul(a[k], b[k]);
+            }
+            __syncthreads();
+        });
+        live = false;
+        if (!ok) break;
+        if (l + 1 < P.layers) {
+            st = open_group<NS>(P, l + 1, 0, P.layer[l + 1].qkv, ring, bars, rs, Gs, Ds);
+            live = true;
+        }
+        if (!barrier()) break;
+    }
+    if (live) stretch_drain<NS>(st, bars, rs);  // left early with copies in flight
+    if (!ok) {
+        if (threadIdx.x == 0) atomicExch(P.sync + 2, 2u);
+        return;
+    }
+    if (ld_acquire(P.sync + 2) != 0u) return;
+    // the final norm of h'' + down, then this CTA's lm_head rows
+    norm_into(P.h[0], P.dn, nullptr, false, P.norm_w, P.eps, H, nullptr, xs, red);
+    for (int i = threadIdx.x; i < H; i += kSThreads) xf[i] = dm::bf(xs[i]);
+    __syncthreads();
+    unsigned long long key[1] = {0ull};
+    const int64_t nwarps = (int64_t)n_ctas * kSWarps;
+    for (int64_t r0 = ((int64_t)blockIdx.x * kSWarps + warp) * dm::kLmRows; r0 < P.vocab;
+         r0 += nwarps * dm::kLmRows)
+        dm::lm_rows<1, dm::kLmRows>(P.lm_w, xf, H, P.vocab, r0, lane, P.logits, key);
+    if (lane == 0 && key[0]) atomicMax(P.best, key[0]);
+    if (!barrier()) return;
+    // the greedy token, recorded; the next step's input and position
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const int64_t tok = dm::key_token(*P.best);
+        *P.best = 0ull;
+        *P.next = tok;
+        const int c = *P.count;
+        if (c < P.token_cap) P.tokens[c] = tok;
+        *P.ids = tok;
+        *P.pos = pos + 1;
+        *P.count = c + 1;
+    }
+}
+
+}  // namespace step

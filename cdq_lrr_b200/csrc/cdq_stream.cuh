@@ -65,15 +65,17 @@ struct Cursor {
 };
 
 // First unit of the item (the launch's unit count once past the last job).
-template <int MAXJ>
-__device__ __forceinline__ int item_start(const GemvBatch<MAXJ>& b, const Cursor& c) {
+// B: a batch view with n, total_units and jobs[] (GemvBatch, or the
+// persistent decode kernel's per-projection-group view).
+template <class B>
+__device__ __forceinline__ int item_start(const B& b, const Cursor& c) {
     if (c.j >= b.n) return (int)b.total_units;
     const GemvJob& J = b.jobs[c.j];
     return (int)J.unit_begin + c.b16 * J.kp + 16 * c.grp;
 }
 
-template <int MAXJ>
-__device__ __forceinline__ void advance(const GemvBatch<MAXJ>& b, Cursor& c) {
+template <class B>
+__device__ __forceinline__ void advance(const B& b, Cursor& c) {
     const GemvJob& J = b.jobs[c.j];
     if (++c.grp == J.kg) {
         c.grp = 0;
@@ -85,8 +87,8 @@ __device__ __forceinline__ void advance(const GemvBatch<MAXJ>& b, Cursor& c) {
 }
 
 // The first item whose first unit is >= u (u in [0, total_units]).
-template <int MAXJ>
-__device__ __forceinline__ Cursor first_at(const GemvBatch<MAXJ>& b, int u) {
+template <class B>
+__device__ __forceinline__ Cursor first_at(const B& b, int u) {
     int lo = 0, hi = b.n - 1;
     while (lo < hi) {  // last job with unit_begin <= u (uniform reads of the launch record)
         const int mid = (lo + hi + 1) >> 1;
@@ -276,6 +278,29 @@ __device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const
     if (lane == 0) J.counters[b16] = 0u;
 }
 
+// Activations of a unit: 16 bf16 per lane as two 16-byte loads, from global
+// memory through the L1 cache (XGlobal) or from shared memory (XShared: the
+// persistent decode kernel keeps each projection group's input there).
+struct XGlobal {
+    const uint16_t* p;
+    __device__ __forceinline__ XGlobal at(int64_t off) const { return XGlobal{p + off}; }
+    __device__ __forceinline__ void load(int off, uint4& a, uint4& b) const {
+        a = ldg_x4(p + off);
+        b = ldg_x4(p + off + 8);
+    }
+};
+struct XShared {
+    uint32_t addr;
+    __device__ __forceinline__ XShared at(int64_t off) const { return XShared{addr + 2u * (uint32_t)off}; }
+    __device__ __forceinline__ void load(int off, uint4& a, uint4& b) const {
+        const uint32_t q = addr + 2u * (uint32_t)off;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w) : "r"(q));
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+                     : "r"(q + 16));
+    }
+};
+
 // One quad of UQ units (4: a full quad; 1..3: the compact last quad of a row
 // block) read from its ring slot: the lane's code words and scale half-words
 // into registers, then the slot goes back to the producer (`refill`, after
@@ -283,8 +308,8 @@ __device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const
 // bytes still being read), then the units' mmas. PH: the item holds the
 // phantom second tile of an odd tile count (unit `phantom` of this quad, -1
 // if none here), whose lanes c >= 2 take zero activations.
-template <int NS, int UQ, bool PH, typename Refill>
-__device__ __forceinline__ void quad_step(uint32_t slot, int lane, int c, const uint16_t* xq, int phantom,
+template <int NS, int UQ, bool PH, class X, typename Refill>
+__device__ __forceinline__ void quad_step(uint32_t slot, int lane, int c, const X& xq, int phantom,
                                           uint32_t lane_base, uint32_t sig_base, float (&d)[4], Refill&& refill) {
     using Tr = PackTraits<NS>;
     uint4 A[4];
@@ -320,32 +345,20 @@ __device__ __forceinline__ void quad_step(uint32_t slot, int lane, int c, const 
     refill();
 #pragma unroll
     for (int i = 0; i < UQ; ++i) {
-        uint4 xa, xb;
-        if constexpr (PH) {
-            load_x(xq, i, i == phantom, c, xa, xb);
-        } else {
-            xa = ldg_x4(xq + 64 * i);
-            xb = ldg_x4(xq + 64 * i + 8);
-        }
+        uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+        // the phantom tile's lanes c >= 2 take zero activations
+        if (!PH || i != phantom || c < 2) xq.load(64 * i, xa, xb);
         if (i & 1) unit_mma<NS, 16>(A[i], w4[i], i < 2 ? s01 : s23, xa, xb, lane_base, sig_base, d);
         else unit_mma<NS, 0>(A[i], w4[i], i < 2 ? s01 : s23, xa, xb, lane_base, sig_base, d);
     }
 }
 
-template <int NS, int M, int MAXJ>
-__global__ void __launch_bounds__(kSThreads, 1)
-stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+// The pair table (lane-private copies) and the fp8 scale table of a
+// streaming kernel's shared window; every thread of the block takes part (no
+// barrier inside).
+template <int NS>
+__device__ __forceinline__ void build_tables(uint8_t* base) {
     using Tr = PackTraits<NS>;
-    constexpr uint32_t kU = Tr::kUnit;
-    using Rg = Ring<NS>;
-    constexpr uint32_t kQuad = Rg::kQuad;
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
-    if (s0 > kLowStage || s0 + kSmemBytes < Rg::kTop) {
-        if (threadIdx.x == 0) atomicExch(&g_gemv_error, 1);
-        return;
-    }
-    uint8_t* const base = smem - s0;  // generic pointer of shared address 0
     for (int i = threadIdx.x; i < Tr::kPairs * 32; i += blockDim.x) {
         const uint32_t p = (uint32_t)i >> 5, l = (uint32_t)i & 31;
         uint32_t lo, hi, addr;
@@ -364,76 +377,132 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const uint32_t s = fp8_to_bf16((uint8_t)i);
         *reinterpret_cast<uint32_t*>(base + kSigAddr + 4 * i) = s | (s << 16);
     }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const uint32_t ring = ring_of<NS>(warp);
-    const uint32_t bars = kBarAddr + warp * kSlots * 8;
-    if (lane == 0) {
-        for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Where a warp's two-slot ring stands between calls of stream_warp: the slot
+// the next quad lands in and that slot's mbarrier phase. Every call consumes
+// every copy it issues, so the next call starts with an empty ring.
+struct RingState {
+    uint32_t slot, phase;
+};
+
+// A warp's place in one stretch [u_lo, u_hi) of a batch's unit sequence: the
+// consumer's first item and the producer's position. The producer (lane 0
+// issues; every lane keeps the same cursor) walks the quads of
+// [u_first, u_end), which are consecutive in each job's units buffer.
+struct Stretch {
+    Cursor cur;
+    int u_lo, u_hi, u_first, grp_first;
+    int pj, p_left, p_kp, p_r, p_rb;
+    const uint8_t* p_ptr;
+    int opened;  // copies stretch_open issued (0 .. 2)
+};
+
+// Issues the next quad's copy into `slot` (the slot the consumer has just
+// read, or one of the first two).
+template <int NS, class B>
+__device__ __forceinline__ void stretch_produce(Stretch& st, const B& batch, uint32_t slot, uint32_t ring,
+                                                uint32_t bars) {
+    constexpr uint32_t kU = PackTraits<NS>::kUnit;
+    if (st.p_left <= 0) return;
+    const int u = min(4, st.p_kp - st.p_r);
+    const uint32_t bytes = (uint32_t)u * kU;
+    if ((threadIdx.x & 31) == 0) {
+        const uint32_t bar = bars + 8 * slot;
+        slot_arm(bar, bytes);
+        bulk_copy(ring + slot * Ring<NS>::kQuad, st.p_ptr, bytes, bar);
     }
-    __syncthreads();
+    st.p_ptr += bytes;
+    st.p_left -= u;
+    st.p_r += u;
+    if (st.p_r == st.p_kp) {
+        st.p_r = 0;
+        if (--st.p_rb == 0 && st.p_left > 0) {
+            const GemvJob& J = batch.jobs[++st.pj];
+            st.p_kp = J.kp;
+            st.p_rb = J.r16;
+            st.p_ptr = J.units;
+        }
+    }
+}
 
-    // this warp's stretch of the unit sequence
-    const int64_t U = batch.total_units;
-    const int64_t nw = (int64_t)gridDim.x * kSWarps;
-    const int64_t gw = (int64_t)blockIdx.x * kSWarps + warp;
-    const int u_lo = (int)stretch_bound(U, gw, nw), u_hi = (int)stretch_bound(U, gw + 1, nw);
-    Cursor cur = first_at(batch, u_lo);
-    const int u_first = item_start(batch, cur);
-    if (u_first >= u_hi) return;  // no item starts in this stretch
+// Opens a warp's stretch: finds its first item, issues the first two copies
+// into the ring (rs: where the ring stands) and, with prefetch_l2, asks L2 for
+// every other byte of the stretch's weights (small stretches, so the later
+// copies come from L2).
+template <int NS, class B>
+__device__ __forceinline__ Stretch stretch_open(const B& batch, int u_lo, int u_hi, uint32_t ring, uint32_t bars,
+                                                const RingState& rs, bool prefetch_l2) {
+    constexpr uint32_t kU = PackTraits<NS>::kUnit;
+    Stretch st;
+    st.opened = 0;
+    st.cur = first_at(batch, u_lo);
+    st.u_lo = u_lo;
+    st.u_hi = u_hi;
+    st.u_first = item_start(batch, st.cur);
+    st.grp_first = st.cur.grp;  // first group of a row block cut at the stretch's start
+    st.p_left = 0;
+    if (st.u_first >= u_hi) return st;  // no item starts in this stretch
     const int u_end = item_start(batch, first_at(batch, u_hi));
-    const int grp_first = cur.grp;  // first group of a row block cut at the stretch's start
+    st.pj = st.cur.j;
+    st.p_left = u_end - st.u_first;
+    const GemvJob& J = batch.jobs[st.pj];
+    st.p_kp = J.kp;
+    st.p_r = 16 * st.cur.grp;
+    st.p_rb = J.r16 - st.cur.b16;
+    st.p_ptr = J.units + ((int64_t)st.cur.b16 * J.kp + st.p_r) * kU;
+    if (prefetch_l2 && (threadIdx.x & 31) == 0) {
+        int left = st.p_left, pj = st.pj;
+        const uint8_t* ptr = st.p_ptr;
+        int in_job = st.p_rb * st.p_kp - st.p_r;  // units from p_ptr to the job's end
+        while (left > 0) {
+            const int u = min(left, in_job);
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"((uint32_t)u * kU) : "memory");
+            left -= u;
+            if (left > 0) {
+                const GemvJob& Jn = batch.jobs[++pj];
+                ptr = Jn.units;
+                in_job = Jn.r16 * Jn.kp;
+            }
+        }
+    }
+    const int before = st.p_left;
+    stretch_produce<NS>(st, batch, rs.slot, ring, bars);
+    const int after1 = st.p_left;
+    stretch_produce<NS>(st, batch, rs.slot ^ 1u, ring, bars);
+    st.opened = (before > 0) + (after1 > 0);
+    return st;
+}
 
+// Lets the copies an opened stretch issued land before the warp leaves
+// without running it (an error path): bounded waits, ring state unchanged.
+template <int NS>
+__device__ __forceinline__ void stretch_drain(const Stretch& st, uint32_t bars, const RingState& rs) {
+    uint32_t slot = rs.slot, phase = rs.phase;
+    for (int k = 0; k < st.opened; ++k) {
+        (void)mbar_wait(bars + 8 * slot, phase);
+        slot ^= 1u;
+        phase ^= slot == 0 ? 1u : 0u;
+    }
+}
+
+// Runs an opened stretch: its items decoded, multiplied, finished with the
+// residual sums from the workspace, and the outputs written (cut row blocks
+// through the arrival counters). xsrc(J.x) gives a job's activation source
+// (XGlobal or XShared). Returns false if a copy never landed (error code 2
+// recorded, in-flight copies drained).
+template <int NS, int M, class X, class B, class XSrc>
+__device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_t ring, uint32_t bars,
+                                            RingState& rs, XSrc&& xsrc) {
+    constexpr uint32_t kQuad = Ring<NS>::kQuad;
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    if (st.u_first >= st.u_hi) return true;
     const uint32_t lane_base = NS == 26 ? (kLat26Xor | (4u * lane)) : (kLat16Base + 4u * lane);
     const uint32_t sig_base = kSigAddr;
     const int xrow = g < M ? g : 0;  // batch rows >= M: their mma columns are never stored
 
-    // Producer (lane 0 issues; every lane keeps the same cursor): the quads of
-    // [u_first, u_end), which are consecutive in each job's units buffer.
-    int pj = cur.j;
-    int p_left = (int)(u_end - u_first);
-    int p_kp, p_r, p_rb;
-    const uint8_t* p_ptr;
-    {
-        const GemvJob& J = batch.jobs[pj];
-        p_kp = J.kp;
-        p_r = 16 * cur.grp;
-        p_rb = J.r16 - cur.b16;
-        p_ptr = J.units + ((int64_t)cur.b16 * J.kp + p_r) * kU;
-    }
-    // into `slot`: the slot the consumer has just read (two copies run ahead)
-    auto produce = [&](uint32_t slot) {
-        if (p_left <= 0) return;
-        const int u = min(4, p_kp - p_r);
-        const uint32_t bytes = (uint32_t)u * kU;
-        if (lane == 0) {
-            const uint32_t bar = bars + 8 * slot;
-            slot_arm(bar, bytes);
-            bulk_copy(ring + slot * kQuad, p_ptr, bytes, bar);
-        }
-        p_ptr += bytes;
-        p_left -= u;
-        p_r += u;
-        if (p_r == p_kp) {
-            p_r = 0;
-            if (--p_rb == 0 && p_left > 0) {
-                const GemvJob& J = batch.jobs[++pj];
-                p_kp = J.kp;
-                p_rb = J.r16;
-                p_ptr = J.units;
-            }
-        }
-    };
-    produce(0);
-    produce(1);
-    // The residual pre-pass is this launch's programmatic predecessor: the
-    // table set-up and the first copies above overlap it; its sums (and the
-    // workspace it shares with the cut row blocks) are read only after it has
-    // completed (a no-op when the launch has no such predecessor).
-    pdl_wait();
-
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t c_slot = 0, c_phase = 0;
+    uint32_t c_slot = rs.slot, c_phase = rs.phase;
     bool failed = false;
     // the current job's fields, held in registers (reloaded when the cursor
     // enters the next job), and the current item's first unit (items are
@@ -442,8 +511,10 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
     bool odd_kt = false;
     const uint16_t* jx = nullptr;
     float* jpart = nullptr;
-    int ustart = u_first;
-    auto refill = [&]() { produce(c_slot); };
+    int ustart = st.u_first;
+    Cursor cur = st.cur;
+    const int u_lo = st.u_lo, u_hi = st.u_hi, grp_first = st.grp_first;
+    auto refill = [&]() { stretch_produce<NS>(st, batch, c_slot, ring, bars); };
     while (ustart < u_hi) {
         if (cur.j != jk) {
             const GemvJob& J = batch.jobs[cur.j];
@@ -460,7 +531,7 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
         const int n_units = min(16, kp - cp0);
         // a phantom second tile (odd tile count) sits in the row block's last unit
         const bool phantom_item = odd_kt && cp0 + n_units == kp;
-        const uint16_t* xp = jx + (int64_t)xrow * cols + 64 * cp0 + 16 * c;
+        const X xp = xsrc(jx).at((int64_t)xrow * cols + 64 * cp0 + 16 * c);
 
         // the group's residual sums of rows g and g + 8 (batch columns 2c, 2c + 1),
         // from the pre-pass: in flight while the quads stream
@@ -483,7 +554,7 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
                 failed = true;
                 break;
             }
-            quad_step<NS, 4, false>(ring + c_slot * kQuad, lane, c, xp + 256 * q0, -1, lane_base, sig_base, d,
+            quad_step<NS, 4, false>(ring + c_slot * kQuad, lane, c, xp.at(256 * q0), -1, lane_base, sig_base, d,
                                     refill);
             c_slot ^= 1u;
             c_phase ^= c_slot == 0 ? 1u : 0u;
@@ -496,7 +567,7 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             }
             const uint32_t slot = ring + c_slot * kQuad;
             const int uq = min(4, n_units - 4 * q);
-            const uint16_t* xq = xp + 256 * q;
+            const X xq = xp.at(256 * q);
             if (!phantom_item) {
                 if (uq == 4) quad_step<NS, 4, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
                 else if (uq == 2) quad_step<NS, 2, false>(slot, lane, c, xq, -1, lane_base, sig_base, d, refill);
@@ -563,6 +634,54 @@ stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
             c_phase ^= c_slot == 0 ? 1u : 0u;
         }
     }
+    rs.slot = c_slot;
+    rs.phase = c_phase;
+    return !failed;
+}
+
+// One warp's stretch [u_lo, u_hi) of `batch` in one go: open it, run
+// `after_issue` once the first two copies are in flight (before any
+// activation or workspace read: the standalone kernel's programmatic-
+// dependency wait), then run it.
+template <int NS, int M, class X, class B, class XSrc, class AfterIssue>
+__device__ __forceinline__ bool stream_warp(const B& batch, int u_lo, int u_hi, uint32_t ring, uint32_t bars,
+                                            RingState& rs, XSrc&& xsrc, AfterIssue&& after_issue) {
+    Stretch st = stretch_open<NS>(batch, u_lo, u_hi, ring, bars, rs, false);
+    after_issue();
+    return stretch_run<NS, M, X>(st, batch, ring, bars, rs, xsrc);
+}
+
+template <int NS, int M, int MAXJ>
+__global__ void __launch_bounds__(kSThreads, 1)
+stream_kernel(const __grid_constant__ GemvBatch<MAXJ> batch) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(smem);
+    if (s0 > kLowStage || s0 + kSmemBytes < Ring<NS>::kTop) {
+        if (threadIdx.x == 0) atomicExch(&g_gemv_error, 1);
+        return;
+    }
+    build_tables<NS>(smem - s0);  // smem - s0: generic pointer of shared address 0
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ring = ring_of<NS>(warp);
+    const uint32_t bars = kBarAddr + warp * kSlots * 8;
+    if (lane == 0) {
+        for (int k = 0; k < kSlots; ++k) mbar_init(bars + 8 * k);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    // this warp's stretch of the unit sequence
+    const int64_t U = batch.total_units;
+    const int64_t nw = (int64_t)gridDim.x * kSWarps;
+    const int64_t gw = (int64_t)blockIdx.x * kSWarps + warp;
+    RingState rs{0u, 0u};
+    // The residual pre-pass is this launch's programmatic predecessor: the
+    // table set-up and the first copies overlap it; its sums (and the
+    // workspace it shares with the cut row blocks) are read only after it has
+    // completed (a no-op when the launch has no such predecessor).
+    (void)stream_warp<NS, M, XGlobal>(
+        batch, (int)stretch_bound(U, gw, nw), (int)stretch_bound(U, gw + 1, nw), ring, bars, rs,
+        [](const uint16_t* x) { return XGlobal{x}; }, []() { pdl_wait(); });
 }
 
 // Two launches: the residual pre-pass, then the streaming kernel (the jobs'

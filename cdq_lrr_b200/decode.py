@@ -14,6 +14,7 @@ replayed per token.
 """
 from __future__ import annotations
 
+import ctypes as C
 import time
 
 import torch
@@ -210,9 +211,14 @@ class FusedDecoder:
     previous one, so launch latencies overlap. Prefill runs the
     HF model itself into the same static cache (the reference's forward,
     code/cdq_lrr_qwen05.py:300-330), whose [1, kv_heads, max_len, head_dim]
-    tensors the attention kernel then reads and appends to."""
+    tensors the attention kernel then reads and appends to.
 
-    def __init__(self, model, max_len: int):
+    persistent=True runs the same step as one cooperative launch of the
+    persistent decode-step kernel (cdq_decode_step: every layer, the lm_head
+    and the advance in one kernel with grid-wide barriers), which computes the
+    same bits without a launch per operation."""
+
+    def __init__(self, model, max_len: int, persistent: bool = False):
         from transformers import StaticCache
         from . import _lib as L
         from . import ops
@@ -263,6 +269,49 @@ class FusedDecoder:
         self.best = z(1, torch.int64)   # the lm_head's argmax key (zero between steps)
         self.next = z(1, torch.int64)
         self.graph = None
+        self.persistent = persistent
+        self.table = None  # the persistent step's table, prepared once the cache exists (after prefill)
+
+    def _prepare_persistent(self) -> None:
+        """The persistent step's table: the model's shapes and buffers and,
+        per layer, the seven projection jobs of the grouped calls above."""
+        L = self.L
+        p = lambda t: t.data_ptr()  # noqa: E731
+        M = L.cdq_step_model()
+        M.layers, M.hidden, M.heads, M.kv_heads = len(self.layers), self.H, self.n_heads, self.n_kv
+        M.head_dim, M.inter, M.max_len, M.token_cap = self.hd, self.inter, self.max_len, self.max_len
+        M.vocab, M.eps, M.scale = self.vocab, self.eps, float(self.hd) ** -0.5
+        self.h1 = torch.zeros_like(self.h)
+        for name, t in (("embed", self.embed_w), ("norm_w", self.norm_w), ("lm_w", self.lm_w), ("cos_t", self.cos),
+                        ("sin_t", self.sin), ("pos", self.pos), ("ids", self.ids), ("tokens", self.tokens),
+                        ("count", self.count), ("best", self.best), ("next", self.next), ("logits", self.logits),
+                        ("h0", self.h), ("h1", self.h1), ("q", self.q), ("k", self.k), ("v", self.v),
+                        ("att", self.att), ("o", self.o), ("g", self.g), ("u", self.u), ("dn", self.dn)):
+            setattr(M, name, p(t))
+        layers = (L.cdq_step_layer * len(self.layers))()
+        ns = set()
+        for li, (Ly, dst) in enumerate(zip(self.layers, layers)):
+            qkv, o, gu, down = Ly["qkv"].jobs, Ly["o"].jobs, Ly["gu"].jobs, Ly["down"].jobs
+            dst.q, dst.k, dst.v, dst.o = qkv[0], qkv[1], qkv[2], o[0]
+            dst.gate, dst.up, dst.down = gu[0], gu[1], down[0]
+            dst.ln1, dst.ln2 = p(Ly["ln1"]), p(Ly["ln2"])
+            cl = self.cache.layers[li]
+            dst.k_cache, dst.v_cache = p(cl.keys), p(cl.values)
+            ns.update(t.pack.n_states for g in ("qkv", "o", "gu", "down") for t in Ly[g].tasks)
+        if len(ns) != 1:
+            raise ValueError("the persistent step needs one lattice size for every projection")
+        self.n_states = ns.pop()
+        nbytes = C.c_int64()
+        L.check(L.lib().cdq_step_table_bytes(len(self.layers), C.byref(nbytes)), "cdq_step_table_bytes")
+        self.table = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.dev)
+        self._step_model, self._step_layers = M, layers
+        L.check(L.lib().cdq_step_prepare(C.byref(M), layers, self.table.data_ptr()), "cdq_step_prepare")
+
+    def step_error(self) -> int:
+        """The persistent step's error word (0: none)."""
+        code = C.c_int32()
+        self.L.check(self.L.lib().cdq_step_error(self.table.data_ptr(), C.byref(code)), "cdq_step_error")
+        return code.value
 
     def _call(self, name: str, *args) -> None:
         self.L.check(getattr(self.L.lib(), name)(*args), name)
@@ -270,6 +319,11 @@ class FusedDecoder:
     def _step(self) -> None:
         p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
         s = torch.cuda.current_stream(self.dev).cuda_stream
+        if self.persistent:
+            if self.table is None:
+                self._prepare_persistent()
+            self._call("cdq_decode_step", p(self.table), self.n_states, s)
+            return
         for li, Ly in enumerate(self.layers):
             cl = self.cache.layers[li]
             if li == 0:  # the token's embedding row and the first input norm
@@ -301,6 +355,8 @@ class FusedDecoder:
                          position_ids=pos[None], use_cache=True, logits_to_keep=1)
         tok = out.logits[:, -1].argmax(-1)
         self.reset(tok, n)
+        if self.persistent and self.table is None:
+            self._prepare_persistent()  # the static cache's tensors exist now
         return tok
 
     def reset(self, tok: torch.Tensor, position: int) -> None:
@@ -336,10 +392,12 @@ class FusedDecoder:
 
 
 @torch.no_grad()
-def fused_greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True) -> dict:
-    """greedy_decode's contract on the fused decode step (FusedDecoder)."""
+def fused_greedy_decode(model, prompt: torch.Tensor, new_tokens: int, use_graph: bool = True,
+                        persistent: bool = False) -> dict:
+    """greedy_decode's contract on the fused decode step (FusedDecoder;
+    persistent: the one-launch step)."""
     P = prompt.shape[1]
-    dec = FusedDecoder(model, P + new_tokens + 2)
+    dec = FusedDecoder(model, P + new_tokens + 2, persistent=persistent)
     e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     e[0].record()
     tok = dec.prefill(prompt)
@@ -512,18 +570,19 @@ def main(argv=None) -> None:
     ap.add_argument("--prompt", type=int, default=128, help="prompt tokens (seeded random ids)")
     ap.add_argument("--new-tokens", type=int, default=32)
     ap.add_argument("--eager", action="store_true", help="no CUDA graph; steps inside NVTX ranges")
+    ap.add_argument("--persistent", action="store_true", help="the one-launch persistent decode step")
     args = ap.parse_args(argv)
     model = build_model(seed=0, device="cuda")
     patch_cdq(model)
     g = torch.Generator().manual_seed(7)
     ids = torch.randint(0, model.config.vocab_size, (1, args.prompt), generator=g).cuda()
     if not args.eager:
-        r = fused_greedy_decode(model, ids, args.new_tokens)
-        print(f"{r['tokens_per_s']:.1f} tok/s ({r['decode_ms_per_token']:.4f} ms per token), "
+        r = fused_greedy_decode(model, ids, args.new_tokens, persistent=args.persistent)
+        print(f"{'persistent ' if args.persistent else ''}{r['tokens_per_s']:.1f} tok/s ({r['decode_ms_per_token']:.4f} ms per token), "
               f"tokens {r['tokens'][0, :8].tolist()} ...")
         return
     with torch.no_grad():
-        dec = FusedDecoder(model, args.prompt + args.new_tokens + 2)
+        dec = FusedDecoder(model, args.prompt + args.new_tokens + 2, persistent=args.persistent)
         dec.prefill(ids)
         dec._step()  # warm-up
         torch.cuda.synchronize()

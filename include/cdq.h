@@ -275,6 +275,72 @@ CDQ_API cdq_status cdq_pack_from_reference_device(int32_t rows, int32_t cols, in
                                                   cdq_packed* out, int32_t* error, void* stream);
 
 /*
+ * Persistent decode step: one cooperative launch (one CTA per SM, all
+ * resident) runs a whole batch-1 greedy token of a Qwen2-style decoder with
+ * CDQ projections: per layer the residual add + RMSNorm, q/k/v (with biases),
+ * rotary embedding + cache append + grouped-query attention, o_proj, the
+ * second add + RMSNorm, gate/up, SiLU(gate) * up, down_proj; then the final
+ * norm, the tied bf16 lm_head with its argmax, and the token advance
+ * (tokens[count] = token, ids = token, pos + 1, count + 1), with grid-wide
+ * barriers between dependent steps. Every operation computes exactly what the
+ * one-kernel-per-operation step computes (cdq_embed_rmsnorm, cdq_add_rmsnorm,
+ * cdq_linear_grouped, cdq_attn_decode, cdq_silu_mul, cdq_lm_head_argmax,
+ * cdq_decode_advance), bit for bit. Replaces the reference's generate loop
+ * step (code/cdq_lrr_qwen05.py:335-340: one HF forward of the patched model).
+ */
+typedef struct cdq_step_layer {
+    /* m = 1 jobs: w, bias, workspace as for cdq_linear; y must be the model's
+     * buffer of that projection (q, k, v, o, g, u, dn below); x a valid
+     * activation buffer as for cdq_linear (not read: the persistent kernel
+     * keeps each projection group's input in shared memory); out_f32 = 0.
+     * All seven of one lattice size. */
+    cdq_gemv_job q, k, v, o, gate, up, down;
+    const uint16_t* ln1;  /* input_layernorm weight [hidden] */
+    const uint16_t* ln2;  /* post_attention_layernorm weight [hidden] */
+    uint16_t* k_cache;    /* [kv_heads, max_len, 64] bf16, 16-byte aligned */
+    uint16_t* v_cache;
+} cdq_step_layer;
+
+typedef struct cdq_step_model {
+    int32_t layers, hidden, heads, kv_heads, head_dim, inter, max_len, token_cap;
+    int64_t vocab;
+    float eps, scale;                  /* RMSNorm epsilon, attention scale */
+    const uint16_t* embed;             /* [vocab, hidden] */
+    const uint16_t* norm_w;            /* final norm weight [hidden] */
+    const uint16_t* lm_w;              /* [vocab, hidden], 16-byte aligned */
+    const uint16_t* cos_t;             /* [max_len, 64] rotary tables */
+    const uint16_t* sin_t;
+    int32_t* pos;                      /* the step's position (device) */
+    int64_t* ids;                      /* the step's input token */
+    int64_t* tokens;                   /* [token_cap] generated tokens */
+    int32_t* count;                    /* tokens generated so far */
+    uint64_t* best;                    /* argmax key, zero between steps */
+    int64_t* next;                     /* the step's greedy token */
+    uint16_t* logits;                  /* NULL or [vocab] bf16 */
+    uint16_t* h0;                      /* two hidden-state buffers [hidden] */
+    uint16_t* h1;
+    uint16_t *q, *k, *v, *att, *o, *g, *u, *dn; /* projection inputs and outputs */
+} cdq_step_model;
+
+/* Bytes of device memory the step's table takes for `layers` layers. */
+CDQ_API cdq_status cdq_step_table_bytes(int32_t layers, int64_t* bytes);
+/* Checks the model and writes its table to `table` (device memory of
+ * cdq_step_table_bytes, 256-byte aligned; synchronous copy). The table holds
+ * pointers: every buffer must outlive it. CDQ_ERR_UNSUPPORTED when the shapes
+ * do not fit the kernel (head_dim != 64, more heads than SMs, buffers beyond
+ * the shared window), CDQ_ERR_SHAPE on projection shapes that do not match the
+ * model. */
+CDQ_API cdq_status cdq_step_prepare(const cdq_step_model* model, const cdq_step_layer* layers, void* table);
+/* One token on `stream` (capturable in a CUDA graph). n_states: the lattice
+ * size the table was prepared with. */
+CDQ_API cdq_status cdq_decode_step(const void* table, int32_t n_states, void* stream);
+/* The step's sticky error word (0: none; 1: a grid barrier gave up; 2: a
+ * weight copy never landed; 3: the table was prepared for another lattice
+ * size); synchronous read. cdq_step_reset clears it and the barrier state. */
+CDQ_API cdq_status cdq_step_error(const void* table, int32_t* code);
+CDQ_API cdq_status cdq_step_reset(void* table, void* stream);
+
+/*
  * Validation of a device pack that did not come from this library's
  * converters or quantizer (a saved state dict, a pack built elsewhere):
  * adds to *bad (device int32, zeroed by the caller) one per lane whose 26-state

@@ -459,3 +459,55 @@ def test_speculative_self_draft_accepts_every_token(cdq_model):
     spec = decode.speculative_greedy_decode(cdq_model, cdq_model, prompt, 25, k=3)
     assert torch.equal(spec["tokens"].view(-1).cpu(), plain)
     assert spec["accepted_per_verify"] == 3.0 and spec["verifies"] == 6
+
+
+def test_persistent_step_matches_one_kernel_steps(cdq_model):
+    """The persistent decode step (one cooperative launch per token) gives,
+    bit for bit, the logits, tokens and cache contents of the
+    one-kernel-per-operation step, eagerly and replayed from a CUDA graph."""
+    from cdq_lrr_b200 import decode
+    prompt = _prompt(24, seed=13)
+    a = decode.FusedDecoder(cdq_model, 64)
+    b = decode.FusedDecoder(cdq_model, 64, persistent=True)
+    ta, tb = a.prefill(prompt), b.prefill(prompt)
+    assert torch.equal(ta, tb)
+    for _ in range(6):
+        a.step()
+        b.step()
+        torch.cuda.synchronize()
+        assert torch.equal(a.logits, b.logits)
+        assert torch.equal(a.next, b.next) and torch.equal(a.pos, b.pos) and torch.equal(a.count, b.count)
+    assert b.step_error() == 0
+    for x, y in zip(a.cache.layers, b.cache.layers):
+        assert torch.equal(x.keys[:, :, :30], y.keys[:, :, :30])
+        assert torch.equal(x.values[:, :, :30], y.values[:, :, :30])
+    plain = decode.fused_greedy_decode(cdq_model, prompt, 24)["tokens"].view(-1).cpu()
+    pers = decode.fused_greedy_decode(cdq_model, prompt, 24, persistent=True)
+    assert torch.equal(pers["tokens"].view(-1).cpu(), plain)
+
+
+def test_persistent_step_16_state_and_error_word():
+    """The 16-state draft tier on the persistent step equals its one-kernel
+    step; a table run with the wrong lattice size sets error word 3 and
+    touches nothing; cdq_step_reset clears it."""
+    from cdq_lrr_b200 import decode
+    from cdq_lrr_b200.quant import CAMKII_LATTICE_16
+    m16 = decode.build_model(seed=0, device="cuda")
+    decode.patch_cdq(m16, lattice=CAMKII_LATTICE_16)
+    prompt = _prompt(16, seed=14)
+    plain = decode.fused_greedy_decode(m16, prompt, 12)["tokens"].view(-1).cpu()
+    pers = decode.fused_greedy_decode(m16, prompt, 12, persistent=True)["tokens"].view(-1).cpu()
+    assert torch.equal(pers, plain)
+    fd = decode.FusedDecoder(m16, 32, persistent=True)
+    fd.prefill(prompt)
+    pos = fd.pos.clone()
+    s = torch.cuda.current_stream().cuda_stream
+    fd._call("cdq_decode_step", fd.table.data_ptr(), 26, s)  # prepared for 16 states
+    torch.cuda.synchronize()
+    assert fd.step_error() == 3 and torch.equal(fd.pos, pos)
+    fd._call("cdq_step_reset", fd.table.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert fd.step_error() == 0
+    fd.step()
+    torch.cuda.synchronize()
+    assert fd.step_error() == 0 and int(fd.pos) == int(pos) + 1
