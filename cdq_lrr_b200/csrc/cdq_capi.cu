@@ -418,7 +418,7 @@ cdq_status cdq_step_error(const void* table, int32_t* code) {
     StepParams p;
     if (cudaMemcpy(&p, table, sizeof p, cudaMemcpyDeviceToHost) != cudaSuccess) return CDQ_ERR_CUDA;
     uint32_t w = 0;
-    if (cudaMemcpy(&w, p.sync + 2, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return CDQ_ERR_CUDA;
+    if (cudaMemcpy(&w, p.sync + 4, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return CDQ_ERR_CUDA;
     *code = (int32_t)w;
     return CDQ_OK;
 }
@@ -427,7 +427,7 @@ cdq_status cdq_step_reset(void* table, void* stream) {
     if (!table) return CDQ_ERR_ARG;
     StepParams p;
     if (cudaMemcpy(&p, table, sizeof p, cudaMemcpyDeviceToHost) != cudaSuccess) return CDQ_ERR_CUDA;
-    return cudaMemsetAsync(p.sync, 0, 16, (cudaStream_t)stream) == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
+    return cudaMemsetAsync(p.sync, 0, 32, (cudaStream_t)stream) == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }
 
 cdq_status cdq_dequant(const cdq_packed* w, uint16_t* w_hat, void* stream) {

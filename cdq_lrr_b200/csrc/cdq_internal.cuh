@@ -110,8 +110,8 @@ struct StepStage {
 static_assert(sizeof(StepStage) == 64, "StepStage layout");
 
 // Everything the persistent kernel reads, in device memory: this record, then
-// the layers, then the stage descriptors [layer][group][CTA], then three sync
-// words (barrier arrivals, barrier generation, error code).
+// the layers, then the stage descriptors [layer][group][CTA], then the sync
+// words (64-bit barrier arrivals, 64-bit completed launches, 32-bit error).
 struct StepParams {
     int32_t layers, hidden, heads, kv_heads, inter, max_len, token_cap, n_states;
     int64_t vocab;

@@ -22,9 +22,9 @@
 // one-kernel-per-operation step (cdq_decode_math.cuh, stream_warp, the
 // residual pre-pass's per-bucket sums), so the two steps give the same bits.
 //
-// The barrier: thread 0 of each CTA arrives on a counter; the last arrival
-// resets it and bumps a generation word that the others poll (bounded; on
-// timeout the error word is set and every CTA leaves at its next barrier).
+// The barrier: thread 0 of each CTA adds an arrival to a monotonic counter
+// and polls it until every CTA has arrived (bounded; on timeout the error word
+// is set and every CTA leaves at its next barrier).
 // The cooperative launch guarantees that all CTAs are resident, one per SM.
 
 namespace step {
@@ -61,41 +61,48 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
     return v;
 }
 
-// false: the barrier gave up (or an earlier one did): the caller leaves.
-// gen: the barrier generation as thread 0 of this CTA last saw it (read once
-// at kernel start, then advanced locally). ok_s: a word of the CTA's shared
-// window (no static shared memory: the streaming layout needs the dynamic
-// window at the start of the CTA's).
-__device__ __forceinline__ bool grid_barrier(uint32_t* sync, uint32_t n_ctas, uint32_t& gen,
-                                             volatile uint32_t& ok_s) {
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Sync words of the step's table (32-bit word offsets).
+constexpr int kSyncArrivals = 0;  // u64: barrier arrivals, monotonic over launches
+constexpr int kSyncLaunches = 2;  // u64: completed launches
+constexpr int kSyncError = 4;     // u32: the sticky error code
+
+// The grid barrier: thread 0 of every CTA adds one arrival to a monotonic
+// counter and waits until it reaches `target` (this barrier's count: every
+// CTA of every earlier barrier of every earlier launch), so no reset and no
+// second word are needed. false: the barrier gave up (or an earlier one did):
+// the caller leaves. ok_s: a word of the CTA's shared window (no static
+// shared memory: the streaming layout needs the dynamic window at the start
+// of the CTA's).
+__device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long target, volatile uint32_t& ok_s) {
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t ok = 1u;
+        auto* arrivals = reinterpret_cast<unsigned long long*>(sync + kSyncArrivals);
         __threadfence();
-        if (atomicAdd(sync, 1u) == n_ctas - 1) {
-            atomicExch(sync, 0u);
-            __threadfence();
-            atomicAdd(sync + 1, 1u);
-        } else {
-            uint32_t polls = 0;
-            while (ld_acquire(sync + 1) == gen) {
-                if (++polls >= kBarrierPolls) {
-                    atomicExch(sync + 2, 1u);
+        atomicAdd(arrivals, 1ull);
+        uint32_t polls = 0;
+        while (ld_acquire64(arrivals) < target) {
+            if (++polls >= kBarrierPolls) {
+                atomicExch(sync + kSyncError, 1u);
+                ok = 0u;
+                break;
+            }
+            if ((polls & 255u) == 0u) {
+                if (ld_acquire(sync + kSyncError) != 0u) {  // another CTA gave up
                     ok = 0u;
                     break;
                 }
-                if ((polls & 255u) == 0u) {
-                    if (ld_acquire(sync + 2) != 0u) {  // another CTA gave up
-                        ok = 0u;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
+                __nanosleep(64);
             }
         }
-        ++gen;
         __threadfence();
-        if (ld_acquire(sync + 2) != 0u) ok = 0u;
+        if (ld_acquire(sync + kSyncError) != 0u) ok = 0u;
         ok_s = ok;
     }
     __syncthreads();
@@ -296,12 +303,12 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         return;
     }
     if (Pg.n_states != NS) {
-        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + 2, 3u);
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + kSyncError, 3u);
         return;
     }
-    if (ld_acquire(Pg.sync + 2) != 0u) return;  // an earlier step failed: reset first
+    if (ld_acquire(Pg.sync + kSyncError) != 0u) return;  // an earlier step failed: reset first
     if ((int)gridDim.x != Pg.n_ctas) {           // the stage descriptors are per CTA
-        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + 2, 4u);
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(Pg.sync + kSyncError, 4u);
         return;
     }
     uint8_t* const base = smem - s0;  // generic pointer of shared address 0
@@ -334,8 +341,18 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     const int64_t id = *P.ids;
     RingState rs{0u, 0u};
     bool ok = true;
-    uint32_t gen = threadIdx.x == 0 ? ld_acquire(P.sync + 1) : 0u;  // barrier generation (thread 0)
-    auto barrier = [&]() { return grid_barrier(P.sync, n_ctas, gen, bar_ok); };
+    // this launch's barriers: 5 per layer and the final one, n_ctas arrivals each
+    unsigned long long target = 0ull;
+    if (threadIdx.x == 0) {
+        const unsigned long long launches =
+            ld_acquire64(reinterpret_cast<const unsigned long long*>(P.sync + kSyncLaunches));
+        target = (launches * (unsigned long long)(5 * P.layers + 1) + 1ull) * n_ctas;
+    }
+    auto barrier = [&]() {
+        const bool b = grid_barrier(P.sync, target, bar_ok);
+        target += n_ctas;
+        return b;
+    };
     Stretch st = open_group<NS>(P, 0, 0, P.layer[0].qkv, ring, bars, rs, Gs, Ds);
     bool live = true;  // st holds copies in flight
     for (int l = 0; l < P.layers; ++l) {
@@ -420,10 +437,10 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     }
     if (live) stretch_drain<NS>(st, bars, rs);  // left early with copies in flight
     if (!ok) {
-        if (threadIdx.x == 0) atomicExch(P.sync + 2, 2u);
+        if (threadIdx.x == 0) atomicExch(P.sync + kSyncError, 2u);
         return;
     }
-    if (ld_acquire(P.sync + 2) != 0u) return;
+    if (ld_acquire(P.sync + kSyncError) != 0u) return;
     // the final norm of h'' + down, then this CTA's lm_head rows
     norm_into(P.h[0], P.dn, nullptr, false, P.norm_w, P.eps, H, nullptr, xs, red);
     for (int i = threadIdx.x; i < H; i += kSThreads) xf[i] = dm::bf(xs[i]);
@@ -437,6 +454,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     if (!barrier()) return;
     // the greedy token, recorded; the next step's input and position
     if (blockIdx.x == 0 && threadIdx.x == 0) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(P.sync + kSyncLaunches), 1ull);  // every CTA has passed
         const int64_t tok = dm::key_token(*P.best);
         *P.best = 0ull;
         *P.next = tok;
