@@ -322,7 +322,8 @@ typedef struct cdq_step_model {
     uint16_t *q, *k, *v, *att, *o, *g, *u, *dn; /* projection inputs and outputs */
 } cdq_step_model;
 
-/* Bytes of device memory the step's table takes for `layers` layers. */
+/* Bytes of device memory the step's table takes for `layers` layers on the
+ * current device (it holds per-SM residual stage descriptors). */
 CDQ_API cdq_status cdq_step_table_bytes(int32_t layers, int64_t* bytes);
 /* Checks the model and writes its table to `table` (device memory of
  * cdq_step_table_bytes, 256-byte aligned; synchronous copy). The table holds
