@@ -73,6 +73,9 @@ def parse_args():
     ap.add_argument("--tp7b", type=int, default=1,
                     help="1: add the tensor-parallel Qwen2.5-7B-shape stack over all ranks to the default "
                          "line (0: skip)")
+    ap.add_argument("--batch-sweep", type=int, default=1,
+                    help="1: add the batch 1/4/16/64 sweep of the same projections to the line (tile path "
+                         "from batch 16, and the streaming path at 16 and 64 beside it)")
     ap.add_argument("--decode-tokens", type=int, default=256,
                     help="greedy tokens decoded after a 128-token prompt by the full "
                          "Qwen2.5-0.5B-architecture model (0: skip the decode measurement)")
@@ -563,6 +566,13 @@ def run_ours(args) -> None:
     if rank == 0 and ws_ == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
 
+    bsweep = None
+    if rank == 0 and ws_ == 1 and args.batch_sweep:
+        packs = [t.pack for t in tasks]
+        bsweep = batch_sweep(packs, (1, 4, 16, 64), 50, 5, 16, dev)
+        bsweep += batch_sweep(packs, (16, 64), 50, 5, 65, dev)
+        torch.cuda.synchronize()
+
     dec = None
     if rank == 0 and ws_ == 1 and args.decode_tokens > 0:
         n_weights = sum(r * c for _, r, c in layer_list())
@@ -599,6 +609,7 @@ def run_ours(args) -> None:
             "clocks": sampler.summary(t0, t1),
             "cpu_baseline": cpu,
             "decode": dec,
+            "batch_sweep": bsweep,
             "tp7b": tp7,
         }
         print(json.dumps(line), flush=True)
@@ -641,55 +652,71 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_msweep(args) -> None:
-    """Batch sweep (1, 4, 16, 64) over the 168 Qwen2.5-0.5B-shape projections:
-    seeded random valid packs, one grouped launch pair per step (batches above
-    8 decode each unit once and multiply ceil(M/8) n-tiles of 8 rows)."""
+def batch_sweep(packs, batches, steps: int, warmup: int, tile_min_batch: int, device) -> list[dict]:
+    """Grouped calls over `packs` at each batch size (seeded activations), one
+    CUDA graph per step, timed with CUDA events: the path (the tcgen05 tile
+    path from tile_min_batch rows, else the streaming kernels), ms per step,
+    algorithmic GB/s (packs read once per step + activations + outputs) and
+    TFLOP/s."""
     import torch
+    from cdq_lrr_b200 import _lib as L
     from cdq_lrr_b200 import ops
     from cdq_lrr_b200.synth import synth_activation
+    ref_bytes = sum(p.reference_bytes() for p in packs)
+    out = []
+    L.set_tile_min_batch(tile_min_batch)
+    try:
+        for M in batches:
+            tasks = []
+            io_bytes = 0
+            for i, p in enumerate(packs):
+                x = synth_activation(M, p.cols, seed=10000 + i, device=device)
+                y = torch.empty(M, p.rows, dtype=torch.bfloat16, device=device)
+                io_bytes += (x.numel() + y.numel()) * 2
+                tasks.append(ops.GemvTask(p, x, y))
+            g = ops.GroupedLinear(tasks, m=M)
+            stream = torch.cuda.Stream(device=device)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                g()
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    graph.replay()
+            stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(steps):
+                    graph.replay()
+                e1.record(stream)
+            stream.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            flops = 2.0 * M * sum(p.rows * p.cols for p in packs)
+            path = ("tcgen05 tile" if M >= tile_min_batch else
+                    "mma.sync stream" if M <= 8 else "mma.sync wide stream")
+            out.append({"batch": M, "path": path, "ms_per_step": round(ms, 5),
+                        "gb_s": round((ref_bytes + io_bytes) / (ms * 1e-3) / 1e9, 2),
+                        "tflop_s": round(flops / (ms * 1e-3) / 1e12, 3)})
+            del graph, g, tasks
+    finally:
+        L.set_tile_min_batch(16)
+    return out
+
+
+def run_msweep(args) -> None:
+    """Batch sweep (1, 4, 16, 64) over the 168 Qwen2.5-0.5B-shape projections:
+    seeded random valid packs, one grouped call per step (batches above 8
+    decode each unit once and multiply ceil(M/8) n-tiles of 8 rows)."""
+    import torch
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(0)
     packs = [random_pack(rows, cols, seed=i, device=dev) for i, (_, rows, cols) in enumerate(layer_list())]
-    ref_bytes = sum(p.reference_bytes() for p in packs)
-    sweep = []
-    for M in (1, 4, 16, 64):
-        tasks = []
-        io_bytes = 0
-        for i, p in enumerate(packs):
-            x = synth_activation(M, p.cols, seed=10000 + i, device=dev)
-            y = torch.empty(M, p.rows, dtype=torch.bfloat16, device=dev)
-            io_bytes += (x.numel() + y.numel()) * 2
-            tasks.append(ops.GemvTask(p, x, y))
-        g = ops.GroupedLinear(tasks, m=M)
-        stream = torch.cuda.Stream(device=dev)
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                g()
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            g()
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                graph.replay()
-        stream.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            e1.record(stream)
-        stream.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        flops = 2.0 * M * sum(p.rows * p.cols for p in packs)
-        sweep.append({"batch": M, "path": "tcgen05 tile" if M >= args.tile_min_batch else "mma.sync stream",
-                      "ms_per_step": round(ms, 5),
-                      "gb_s": round((ref_bytes + io_bytes) / (ms * 1e-3) / 1e9, 2),
-                      "tflop_s": round(flops / (ms * 1e-3) / 1e12, 3),
-                      "weight_passes": 1})
-        del graph
+    sweep = batch_sweep(packs, (1, 4, 16, 64), args.steps, args.warmup, args.tile_min_batch, dev)
     first = sweep[0]
     line = {"metric": METRIC, "value": first["gb_s"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": first["ms_per_step"], "higher_is_better": True,
