@@ -44,7 +44,8 @@ constexpr uint32_t kScrFlag = kScrRed + 16 * 4;
 constexpr uint32_t kScrParams = al16(kScrFlag + 16);
 constexpr uint32_t kScrGroup = al16(kScrParams + sizeof(StepParams));
 constexpr uint32_t kScrStage = al16(kScrGroup + sizeof(StepGroup));
-constexpr uint32_t kScrBytes = al16(kScrStage + sizeof(StepStage));
+constexpr uint32_t kScrSync = al16(kScrStage + sizeof(StepStage));
+constexpr uint32_t kScrBytes = al16(kScrSync + 32);
 static_assert(sizeof(StepParams) % 16 == 0 && sizeof(StepGroup) % 16 == 0 && sizeof(StepStage) % 16 == 0,
               "shared copies go in 16-byte words");
 
@@ -114,7 +115,8 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long 
 // memory: one thread per (item, row) bucket, each bucket's entries added in
 // order (the residual pre-pass's arithmetic), into the workspace slots the
 // items' warps read.
-__device__ __forceinline__ void cta_residual_sums(const StepGroup& batch, int u_lo, int u_hi, const uint16_t* xs) {
+__device__ __forceinline__ void cta_residual_sums(const StepGroup& batch, int u_lo, int u_hi, const uint16_t* xs,
+                                                  int tid, int nthreads) {
     const Cursor c0 = first_at(batch, u_lo), c1 = first_at(batch, u_hi);
     for (int j = c0.j; j <= c1.j && j < batch.n; ++j) {
         const GemvJob& J = batch.jobs[j];
@@ -125,7 +127,7 @@ __device__ __forceinline__ void cta_residual_sums(const StepGroup& batch, int u_
         const int64_t rpad = (int64_t)J.r16 * 16;
         const uint32_t* __restrict__ rp = J.res_ptr;
         const uint32_t* __restrict__ re = J.res_ent;
-        for (int e = threadIdx.x; e < (i_hi - i_lo) * 16; e += kSThreads) {
+        for (int e = tid; e < (i_hi - i_lo) * 16; e += nthreads) {
             const int it = i_lo + (e >> 4), ri = e & 15;
             const int b16 = it / kg, grp = it - b16 * kg;
             const int row = b16 * 16 + ri;
@@ -173,7 +175,7 @@ __device__ __forceinline__ void stage_issue(const StepStage& d, const StepGroup&
 // same order of fmas).
 __device__ __forceinline__ void cta_residual_sums_staged(const StepGroup& batch, const StepStage& d, int u_lo,
                                                          int u_hi, const uint16_t* xs, const uint32_t* bnd,
-                                                         const uint32_t* ent) {
+                                                         const uint32_t* ent, int tid, int nthreads) {
     const Cursor c0 = first_at(batch, u_lo), c1 = first_at(batch, u_hi);
     int bo = 0, eo = 0;
     for (int j = 0; j < batch.n; ++j) {
@@ -184,7 +186,7 @@ __device__ __forceinline__ void cta_residual_sums_staged(const StepGroup& batch,
             const int i_hi = j == c1.j ? c1.b16 * kg + c1.grp : J.r16 * kg;
             const int64_t rpad = (int64_t)J.r16 * 16;
             const uint32_t e0 = (uint32_t)d.e0[j], e1 = e0 + (uint32_t)d.ne[j];
-            for (int e = threadIdx.x; e < (i_hi - i_lo) * 16; e += kSThreads) {
+            for (int e = tid; e < (i_hi - i_lo) * 16; e += nthreads) {
                 const int it = i_lo + (e >> 4), ri = e & 15;
                 const int b16 = it / kg, grp = it - b16 * kg;
                 const int row = b16 * 16 + ri;
@@ -223,25 +225,68 @@ __device__ __forceinline__ Stretch open_group(const StepParams& P, int l, int gi
                             true);
 }
 
+// Shared words of run_group: a byte per warp (it has items) and the flag that
+// publishes the group's residual sums.
+struct GroupSync {
+    uint8_t busy[kSWarps];
+    uint32_t r_flag;
+};
+
 // Runs an opened projection group: the CTA builds the group's input in shared
-// memory (`prep`, every thread, CTA barriers allowed) and its residual sums,
-// then each warp streams its stretch. CTA-uniform result.
+// memory (`prep`, every thread, CTA barriers allowed), then the warps that
+// have items start streaming while the others compute this CTA's residual
+// sums; an item's warp waits for them (flag `token`, bounded) only at the
+// item's end. Without idle warps everyone sums first. CTA-uniform result.
 template <int NS, class Prep>
 __device__ __forceinline__ bool run_group(Stretch& st, const StepGroup& G, const StepStage& d, const uint16_t* xs,
                                           uint32_t xs_addr, const uint32_t* bnd, const uint32_t* ent, uint32_t ring,
-                                          uint32_t bars, RingState& rs, Prep&& prep) {
+                                          uint32_t bars, RingState& rs, GroupSync& gs, uint32_t token,
+                                          Prep&& prep) {
     const int64_t U = G.total_units;
     const int64_t nw = (int64_t)gridDim.x * kSWarps;
     const int64_t cta0 = (int64_t)blockIdx.x * kSWarps;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool has = st.u_first < st.u_hi;
     prep();
     asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's stage copies
-    __syncthreads();                                   // everyone's
+    if (lane == 0) gs.busy[warp] = has ? 1 : 0;
+    __syncthreads();  // everyone's stage copies and busy bytes
+    uint32_t mask = 0;
+#pragma unroll
+    for (int w = 0; w < kSWarps; ++w) mask |= (uint32_t)gs.busy[w] << w;
+    const int n_busy = __popc(mask);
     const int lo = (int)stretch_bound(U, cta0, nw), hi = (int)stretch_bound(U, cta0 + kSWarps, nw);
-    if (d.ok) cta_residual_sums_staged(G, d, lo, hi, xs, bnd, ent);
-    else cta_residual_sums(G, lo, hi, xs);
-    __syncthreads();
-    const bool ok = stretch_run<NS, 1, XShared>(st, G, ring, bars, rs,
-                                                [xs_addr](const uint16_t*) { return XShared{xs_addr}; });
+    auto sums = [&](int tid, int nthreads) {
+        if (d.ok) cta_residual_sums_staged(G, d, lo, hi, xs, bnd, ent, tid, nthreads);
+        else cta_residual_sums(G, lo, hi, xs, tid, nthreads);
+    };
+    if (n_busy == kSWarps) {  // no idle warp: sum first
+        sums(threadIdx.x, kSThreads);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&gs.r_flag) = token;
+        __syncthreads();
+    } else if (!has) {  // an idle warp: its share of the sums, then the flag
+        const int rank = __popc(~mask & ((1u << warp) - 1u)), n_idle = kSWarps - n_busy;
+        sums(rank * 32 + lane, n_idle * 32);
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(n_idle * 32) : "memory");
+        if (rank == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(&gs.r_flag) = token;
+    }
+    bool ok = true;
+    if (has) {
+        auto r_ready = [&]() {
+            const volatile uint32_t* f = &gs.r_flag;
+            for (uint32_t polls = 0; *f != token; ++polls) {
+                if (polls >= kBarrierPolls) return false;
+                if (polls > 64) __nanosleep(32);
+            }
+            __threadfence();
+            return true;
+        };
+        ok = stretch_run<NS, 1, XShared>(st, G, ring, bars, rs,
+                                         [xs_addr](const uint16_t*) { return XShared{xs_addr}; }, r_ready);
+    }
     return __syncthreads_and(ok) != 0;
 }
 
@@ -330,6 +375,8 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     volatile uint32_t& bar_ok = *reinterpret_cast<volatile uint32_t*>(base + Pg.scr_addr + kScrFlag);
     StepGroup& Gs = *reinterpret_cast<StepGroup*>(base + Pg.scr_addr + kScrGroup);
     StepStage& Ds = *reinterpret_cast<StepStage*>(base + Pg.scr_addr + kScrStage);
+    GroupSync& gsync = *reinterpret_cast<GroupSync*>(base + Pg.scr_addr + kScrSync);
+    if (threadIdx.x == 0) gsync.r_flag = 0u;  // tokens of this launch start at 1
     const uint32_t* const bnd = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr);
     const uint32_t* const ent = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr + 4u * (uint32_t)Pg.rst_bnd_cap);
     __syncthreads();
@@ -359,7 +406,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         const StepLayer& L = P.layer[l];
         // A: x = RMSNorm(h + down) (layer 0: the embedding row); q, k, v
         ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
-                           bars, rs, [&]() {
+                           bars, rs, gsync, 4u * l + 1u, [&]() {
             if (l == 0)
                 norm_into(nullptr, nullptr, P.embed + (id >= 0 && id < P.vocab ? id : 0) * (int64_t)H,
                           id >= 0 && id < P.vocab, L.ln1, P.eps, H, blockIdx.x == 0 ? P.h[1] : nullptr, xs, red);
@@ -380,7 +427,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         if (!barrier()) break;
         // C: o_proj of the attention output
         ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
-                           bars, rs, [&]() {
+                           bars, rs, gsync, 4u * l + 2u, [&]() {
             const uint16_t* ap = P.att;
             const int na = P.heads * dm::kHd;
             for (int i0 = threadIdx.x; i0 < na; i0 += 4 * kSThreads) {
@@ -400,7 +447,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         if (!barrier()) break;
         // D: x = RMSNorm(h' + o); gate, up
         ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
-                           bars, rs, [&]() {
+                           bars, rs, gsync, 4u * l + 3u, [&]() {
             norm_into(P.h[1], P.o, nullptr, false, L.ln2, P.eps, H, blockIdx.x == 0 ? P.h[0] : nullptr, xs, red);
         });
         live = false;
@@ -410,7 +457,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         if (!barrier()) break;
         // E: x = SiLU(gate) * up; down
         ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
-                           bars, rs, [&]() {
+                           bars, rs, gsync, 4u * l + 4u, [&]() {
             const uint16_t* gp = P.g;
             const uint16_t* up = P.u;
             for (int i0 = threadIdx.x; i0 < I; i0 += 8 * kSThreads) {  // eight loads in flight per thread

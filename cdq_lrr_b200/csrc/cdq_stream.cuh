@@ -491,9 +491,18 @@ __device__ __forceinline__ void stretch_drain(const Stretch& st, uint32_t bars, 
 // through the arrival counters). xsrc(J.x) gives a job's activation source
 // (XGlobal or XShared). Returns false if a copy never landed (error code 2
 // recorded, in-flight copies drained).
-template <int NS, int M, class X, class B, class XSrc>
+// No residual-sum wait: the sums are complete before the stretch runs.
+struct RReady {
+    __device__ __forceinline__ bool operator()() const { return true; }
+};
+
+template <int NS, int M, class X, class B, class XSrc, class RWait = RReady>
 __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_t ring, uint32_t bars,
-                                            RingState& rs, XSrc&& xsrc) {
+                                            RingState& rs, XSrc&& xsrc, RWait&& r_ready = RWait{}) {
+    // LATE: the residual sums may still be in the making while the stretch
+    // runs (r_ready() waits for them): read at each item's end instead of its
+    // start
+    constexpr bool LATE = !std::is_same<std::decay_t<RWait>, RReady>::value;
     constexpr uint32_t kQuad = Ring<NS>::kQuad;
     const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     if (st.u_first >= st.u_hi) return true;
@@ -537,13 +546,16 @@ __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_
         // from the pre-pass: in flight while the quads stream
         const int64_t rpad = (int64_t)r16 * 16;
         float R[4] = {0.f, 0.f, 0.f, 0.f};
+        auto load_r = [&]() {
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj)
-                if (2 * c + jj < M)
-                    R[2 * h + jj] = __ldcg(jpart + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
-                                           cur.b16 * 16 + g + 8 * h);
+                for (int jj = 0; jj < 2; ++jj)
+                    if (2 * c + jj < M)
+                        R[2 * h + jj] = __ldcg(jpart + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
+                                               cur.b16 * 16 + g + 8 * h);
+        };
+        if (!LATE) load_r();
 
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         const int nq = (n_units + 3) >> 2;
@@ -586,6 +598,13 @@ __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_
         }
         if (failed) break;
 
+        if (LATE) {
+            if (!r_ready()) {
+                failed = true;
+                break;
+            }
+            load_r();
+        }
         // (row g + 8h, batch column 2c + j) of this lane's mma fragment: e = 2h + j
         float v[4];
 #pragma unroll
