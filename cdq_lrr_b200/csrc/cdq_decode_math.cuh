@@ -129,9 +129,21 @@ __device__ __forceinline__ void attn_core(int tid, const uint16_t* kb, const uin
     // weighted values: thread (slice t, element d) takes positions j = t mod kVSlices
     const int d = tid & (kHd - 1), t = (tid / kHd) % kVSlices;
     if (act) {
+        // positions j = t, t + kVSlices, ... below P in order; the value loads of
+        // 16 positions are issued before their fmas
+        constexpr int kBatch = 16;
         float acc = 0.f;
-#pragma unroll 4
-        for (int j = t; j < P; j += kVSlices) acc = fmaf(scores[j], bf(vb[(int64_t)j * kHd + d]), acc);
+        for (int j0 = t; j0 < P; j0 += kBatch * kVSlices) {
+            uint16_t vv[kBatch];
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const int j = j0 + k * kVSlices;
+                vv[k] = j < P ? vb[(int64_t)j * kHd + d] : (uint16_t)0;
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k)
+                if (j0 + k * kVSlices < P) acc = fmaf(scores[j0 + k * kVSlices], bf(vv[k]), acc);
+        }
         if (P % kVSlices == t) acc = fmaf(scores[P], S.ve[d], acc);  // the position's own value
         S.part[t][d] = acc;
     }
