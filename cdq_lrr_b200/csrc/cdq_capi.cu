@@ -96,9 +96,7 @@ cdq_status linear_common(const cdq_packed* w, const uint16_t* x, int64_t m, void
     if (st) return st;
     b.jobs[0].item_begin = 0;
     b.total_items = (int64_t)b.jobs[0].r16 * b.jobs[0].kg;
-    b.total_row_blocks = b.jobs[0].r16;
     b.m = (int32_t)m;
-    b.finish_single = 0;
     cudaError_t e = gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms);
     return e == cudaSuccess ? CDQ_OK : CDQ_ERR_CUDA;
 }
@@ -171,7 +169,6 @@ cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, vo
             std::unique_ptr<GemvBatch<kMaxJobs>> b(new GemvBatch<kMaxJobs>);
             b->n = 0;
             b->m = (int32_t)m;
-            b->finish_single = 0;
             int64_t items = 0, blocks = 0;
             for (size_t s1 = s0; s1 < std::min(idx.size(), s0 + (size_t)kMaxJobs); ++s1) {
                 const cdq_gemv_job& jb = jobs[idx[s1]];
@@ -187,7 +184,6 @@ cdq_status cdq_linear_grouped(const cdq_gemv_job* jobs, int32_t n, int64_t m, vo
                 if (items >= INT32_MAX || blocks >= INT32_MAX) return CDQ_ERR_SHAPE;
             }
             b->total_items = items;
-            b->total_row_blocks = (int32_t)blocks;
             cudaError_t e = gemv_launch_grouped(*b, ns, (int)m, (cudaStream_t)stream, sms);
             if (e != cudaSuccess) return CDQ_ERR_CUDA;
         }

@@ -305,23 +305,6 @@ __device__ __forceinline__ void store_out(const GemvJob& J, int n, int row, floa
     }
 }
 
-// Activations of unit column block `unit` (64 columns) for this lane; the
-// phantom second tile of an odd tile count takes zeros (lanes c >= 2).
-__device__ __forceinline__ void load_x(const uint16_t* xp, int unit, bool phantom, int c, uint4& xa,
-                                       uint4& xb) {
-    if (!phantom) {
-        xa = ldg_x4(xp + 64 * unit);
-        xb = ldg_x4(xp + 64 * unit + 8);
-    } else {
-        xa = make_uint4(0u, 0u, 0u, 0u);
-        xb = xa;
-        if (c < 2) {
-            xa = ldg_x4(xp + 64 * unit);
-            xb = ldg_x4(xp + 64 * unit + 8);
-        }
-    }
-}
-
 // Where a work item lives: its job, row block, residual group and units.
 struct ItemInfo {
     int job, b16, grp, cp0, n_units;
@@ -608,7 +591,6 @@ cudaError_t launch_one(const GemvBatch<MAXJ>& b, cudaStream_t stream, int num_sm
     // launch; larger launches keep the two passes (the rows' residual tail
     // would stall warps that have more items to stream)
     GemvBatch<MAXJ> sb = b;
-    sb.finish_single = 0;
     e = stream::launch_res(b, b.m, stream);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, kSmemBytes, stream>>>(sb);
@@ -872,9 +854,7 @@ extern "C" cdq_status cdq_linear_noalloc(const cdq_packed* w, const uint16_t* x,
     J.counters = static_cast<uint32_t*>(scratch);
     J.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + gemv_counter_bytes(g));
     b.total_items = (int64_t)J.r16 * J.kg;
-    b.total_row_blocks = J.r16;
     b.m = (int32_t)m;
-    b.finish_single = 0;
     // the streaming paths only: the scratch holds counters and group sums, no prepared activations
     return gemv_launch_single(b, w->n_states, (int)m, (cudaStream_t)stream, sms, false) == cudaSuccess
                ? CDQ_OK

@@ -38,9 +38,7 @@ template <int MAXJ>
 struct GemvBatch {
     int64_t total_items;
     int32_t n;
-    int32_t total_row_blocks;  // fix-up pass work
     int32_t m;                 // batch rows of every job of the launch
-    int32_t finish_single;     // streaming pass finishes single-group jobs itself (small launches)
     int64_t total_units;       // units of every job of the launch (streaming kernel)
     GemvJob jobs[MAXJ];
 };

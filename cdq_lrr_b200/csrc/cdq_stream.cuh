@@ -74,18 +74,6 @@ __device__ __forceinline__ int item_start(const B& b, const Cursor& c) {
     return (int)J.unit_begin + c.b16 * J.kp + 16 * c.grp;
 }
 
-template <class B>
-__device__ __forceinline__ void advance(const B& b, Cursor& c) {
-    const GemvJob& J = b.jobs[c.j];
-    if (++c.grp == J.kg) {
-        c.grp = 0;
-        if (++c.b16 == J.r16) {
-            c.b16 = 0;
-            ++c.j;
-        }
-    }
-}
-
 // The first item whose first unit is >= u (u in [0, total_units]).
 template <class B>
 __device__ __forceinline__ Cursor first_at(const B& b, int u) {
