@@ -76,7 +76,8 @@ constexpr int kSyncError = 4;     // u32: the sticky error code
 // The grid barrier: thread 0 of every CTA adds one arrival to a monotonic
 // counter and waits until it reaches `target` (this barrier's count: every
 // CTA of every earlier barrier of every earlier launch), so no reset and no
-// second word are needed. false: the barrier gave up (or an earlier one did):
+// second word are needed. false: the barrier gave up (or found the error word
+// set by a CTA that failed while it waited):
 // the caller leaves. ok_s: a word of the CTA's shared window (no static
 // shared memory: the streaming layout needs the dynamic window at the start
 // of the CTA's).
@@ -102,8 +103,11 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long 
                 __nanosleep(64);
             }
         }
-        __threadfence();
-        if (ld_acquire(sync + kSyncError) != 0u) ok = 0u;
+        // Reaching the target needs no second look at the error word: a CTA
+        // that fails leaves without arriving, so the barrier after its
+        // failure never completes and the others find the error in their
+        // polls. The acquire load that saw the target orders this CTA's later
+        // reads (through the CTA barrier below) after every arrival's writes.
         ok_s = ok;
     }
     __syncthreads();
@@ -404,6 +408,16 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     bool live = true;  // st holds copies in flight
     for (int l = 0; l < P.layers; ++l) {
         const StepLayer& L = P.layer[l];
+        // the cache rows 0 .. pos-1 that step B reads, asked of L2 now (the
+        // first block of each kv head's query group), so that the attention's
+        // key and value loads do not wait on HBM
+        if (pos_ok && pos > 0 && threadIdx.x == 0 && (int)blockIdx.x < P.heads &&
+            (int)blockIdx.x % (P.heads / P.kv_heads) == 0) {
+            const int64_t off = (int64_t)((int)blockIdx.x / (P.heads / P.kv_heads)) * P.max_len * dm::kHd;
+            const uint32_t bytes = (uint32_t)pos * dm::kHd * 2u;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.kc + off), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.vc + off), "r"(bytes) : "memory");
+        }
         // A: x = RMSNorm(h + down) (layer 0: the embedding row); q, k, v
         ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 1u, [&]() {
