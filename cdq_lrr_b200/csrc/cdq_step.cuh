@@ -35,16 +35,17 @@ constexpr uint32_t kBarrierPolls = 1u << 22;
 
 // The scratch region of the shared window (offsets from its start): the
 // attention scratch, the norm's warp partials, the barrier flag, then copies
-// of the step's parameters, of the projection group being run and of this
-// CTA's stage descriptor (read many times per group: shared memory instead of
-// L2 round trips).
+// of the step's parameters and two buffers of a projection group's
+// descriptor with this CTA's stage descriptor: the group being run and the
+// next one, fetched while this one runs (read many times per group: shared
+// memory instead of L2 round trips).
 constexpr uint32_t al16(uint32_t b) { return (b + 15u) / 16u * 16u; }
 constexpr uint32_t kScrRed = al16(sizeof(dm::AttnScratch));
 constexpr uint32_t kScrFlag = kScrRed + 16 * 4;
 constexpr uint32_t kScrParams = al16(kScrFlag + 16);
-constexpr uint32_t kScrGroup = al16(kScrParams + sizeof(StepParams));
-constexpr uint32_t kScrStage = al16(kScrGroup + sizeof(StepGroup));
-constexpr uint32_t kScrSync = al16(kScrStage + sizeof(StepStage));
+constexpr uint32_t kScrGroupBuf = al16(sizeof(StepGroup) + sizeof(StepStage));  // a group and its stage
+constexpr uint32_t kScrGroup = al16(kScrParams + sizeof(StepParams));            // two such buffers
+constexpr uint32_t kScrSync = kScrGroup + 2 * kScrGroupBuf;
 constexpr uint32_t kScrBytes = al16(kScrSync + 32);
 static_assert(sizeof(StepParams) % 16 == 0 && sizeof(StepGroup) % 16 == 0 && sizeof(StepStage) % 16 == 0,
               "shared copies go in 16-byte words");
@@ -211,16 +212,42 @@ __device__ __forceinline__ void cta_residual_sums_staged(const StepGroup& batch,
     }
 }
 
+// Projection group (l, gi) of the table and this CTA's stage descriptor for it.
+__device__ __forceinline__ const StepGroup* group_of(const StepParams& P, int l, int gi) {
+    return &P.layer[l].qkv + gi;  // qkv, o, gu, down are consecutive
+}
+__device__ __forceinline__ const StepStage* stage_of(const StepParams& P, int l, int gi) {
+    return &P.stage[((int64_t)l * 4 + gi) * P.n_ctas + blockIdx.x];
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Issues the copies of group (l, gi)'s descriptors into the shared buffer at
+// `dst` (every thread; one cp.async group per thread, waited for with the
+// stage copies in run_group).
+__device__ __forceinline__ void fetch_group(const StepParams& P, int l, int gi, uint32_t dst) {
+    const uint4* g = reinterpret_cast<const uint4*>(group_of(P, l, gi));
+    const uint4* d = reinterpret_cast<const uint4*>(stage_of(P, l, gi));
+    for (uint32_t i = threadIdx.x; i < sizeof(StepGroup) / 16; i += blockDim.x) cp_async16(dst + 16 * i, g + i);
+    for (uint32_t i = threadIdx.x; i < sizeof(StepStage) / 16; i += blockDim.x)
+        cp_async16(dst + sizeof(StepGroup) + 16 * i, d + i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // A warp's stretch of a projection group: opened (first two weight copies
 // issued, the rest of its weights prefetched into L2) before the barrier that
 // precedes the group, so those copies fly during the barrier and the steps
-// before the group.
+// before the group. G, D: the group's descriptors, already in shared memory
+// (fetched while the previous group ran); the next group's are fetched into
+// the other buffer (next_buf) now.
 template <int NS>
-__device__ __forceinline__ Stretch open_group(const StepParams& P, int l, int gi, const StepGroup& Gg, uint32_t ring,
-                                              uint32_t bars, const RingState& rs, StepGroup& G, StepStage& D) {
-    copy_to_shared(&G, &Gg, sizeof(StepGroup));
-    copy_to_shared(&D, &P.stage[((int64_t)l * 4 + gi) * P.n_ctas + blockIdx.x], sizeof(StepStage));
-    __syncthreads();
+__device__ __forceinline__ Stretch open_group(const StepParams& P, int l, int gi, uint32_t ring, uint32_t bars,
+                                              const RingState& rs, const StepGroup& G, const StepStage& D,
+                                              uint32_t next_buf) {
+    const int nl = gi == 3 ? l + 1 : l, ngi = gi == 3 ? 0 : gi + 1;
+    if (nl < P.layers) fetch_group(P, nl, ngi, next_buf);
     stage_issue(D, G, P);
     const int64_t U = G.total_units;
     const int64_t nw = (int64_t)gridDim.x * kSWarps;
@@ -234,6 +261,27 @@ __device__ __forceinline__ Stretch open_group(const StepParams& P, int l, int gi
 struct GroupSync {
     uint8_t busy[kSWarps];
     uint32_t r_flag;
+};
+
+// stretch_run's residual-sum wait in run_group: the group's sums are
+// published all at once, by the flag taking the group's token.
+struct RToken {
+    const uint32_t* flag;
+    uint32_t token;
+    __device__ __forceinline__ bool poll() const {
+        if (*reinterpret_cast<const volatile uint32_t*>(flag) != token) return false;
+        __threadfence();
+        return true;
+    }
+    __device__ __forceinline__ bool operator()() const {
+        const volatile uint32_t* f = flag;
+        for (uint32_t polls = 0; *f != token; ++polls) {
+            if (polls >= kBarrierPolls) return false;
+            if (polls > 64) __nanosleep(32);
+        }
+        __threadfence();
+        return true;
+    }
 };
 
 // Runs an opened projection group: the CTA builds the group's input in shared
@@ -279,17 +327,9 @@ __device__ __forceinline__ bool run_group(Stretch& st, const StepGroup& G, const
     }
     bool ok = true;
     if (has) {
-        auto r_ready = [&]() {
-            const volatile uint32_t* f = &gs.r_flag;
-            for (uint32_t polls = 0; *f != token; ++polls) {
-                if (polls >= kBarrierPolls) return false;
-                if (polls > 64) __nanosleep(32);
-            }
-            __threadfence();
-            return true;
-        };
         ok = stretch_run<NS, 1, XShared>(st, G, ring, bars, rs,
-                                         [xs_addr](const uint16_t*) { return XShared{xs_addr}; }, r_ready);
+                                         [xs_addr](const uint16_t*) { return XShared{xs_addr}; },
+                                         RToken{&gs.r_flag, token});
     }
     return __syncthreads_and(ok) != 0;
 }
@@ -377,10 +417,11 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
     dm::AttnScratch& S = *reinterpret_cast<dm::AttnScratch*>(base + Pg.scr_addr);
     float* const red = reinterpret_cast<float*>(base + Pg.scr_addr + kScrRed);
     volatile uint32_t& bar_ok = *reinterpret_cast<volatile uint32_t*>(base + Pg.scr_addr + kScrFlag);
-    StepGroup& Gs = *reinterpret_cast<StepGroup*>(base + Pg.scr_addr + kScrGroup);
-    StepStage& Ds = *reinterpret_cast<StepStage*>(base + Pg.scr_addr + kScrStage);
+    const uint32_t gbuf0 = Pg.scr_addr + kScrGroup;  // shared addresses of the two group buffers
     GroupSync& gsync = *reinterpret_cast<GroupSync*>(base + Pg.scr_addr + kScrSync);
     if (threadIdx.x == 0) gsync.r_flag = 0u;  // tokens of this launch start at 1
+    copy_to_shared(base + gbuf0, group_of(Pg, 0, 0), sizeof(StepGroup));  // the first group's descriptors
+    copy_to_shared(base + gbuf0 + sizeof(StepGroup), stage_of(Pg, 0, 0), sizeof(StepStage));
     const uint32_t* const bnd = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr);
     const uint32_t* const ent = reinterpret_cast<const uint32_t*>(base + Pg.rst_addr + 4u * (uint32_t)Pg.rst_bnd_cap);
     __syncthreads();
@@ -404,7 +445,18 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         target += n_ctas;
         return b;
     };
-    Stretch st = open_group<NS>(P, 0, 0, P.layer[0].qkv, ring, bars, rs, Gs, Ds);
+    // the group descriptors in use alternate between the two shared buffers:
+    // a group's are fetched while the group before it runs
+    int cur = 1;
+    auto Gs = [&]() -> const StepGroup& { return *reinterpret_cast<const StepGroup*>(base + gbuf0 + cur * kScrGroupBuf); };
+    auto Ds = [&]() -> const StepStage& {
+        return *reinterpret_cast<const StepStage*>(base + gbuf0 + cur * kScrGroupBuf + sizeof(StepGroup));
+    };
+    auto open = [&](int l, int gi) {
+        cur ^= 1;
+        return open_group<NS>(P, l, gi, ring, bars, rs, Gs(), Ds(), gbuf0 + (cur ^ 1) * kScrGroupBuf);
+    };
+    Stretch st = open(0, 0);
     bool live = true;  // st holds copies in flight
     for (int l = 0; l < P.layers; ++l) {
         const StepLayer& L = P.layer[l];
@@ -419,7 +471,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.vc + off), "r"(bytes) : "memory");
         }
         // A: x = RMSNorm(h + down) (layer 0: the embedding row); q, k, v
-        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+        ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 1u, [&]() {
             if (l == 0)
                 norm_into(nullptr, nullptr, P.embed + (id >= 0 && id < P.vocab ? id : 0) * (int64_t)H,
@@ -430,7 +482,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
-        st = open_group<NS>(P, l, 1, L.o, ring, bars, rs, Gs, Ds);
+        st = open(l, 1);
         live = true;
         if (!barrier()) break;
         // B: attention, one CTA per query head
@@ -440,7 +492,7 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
                           P.scale, P.att, scores, S);
         if (!barrier()) break;
         // C: o_proj of the attention output
-        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+        ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 2u, [&]() {
             const uint16_t* ap = P.att;
             const int na = P.heads * dm::kHd;
@@ -456,21 +508,21 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
-        st = open_group<NS>(P, l, 2, L.gu, ring, bars, rs, Gs, Ds);
+        st = open(l, 2);
         live = true;
         if (!barrier()) break;
         // D: x = RMSNorm(h' + o); gate, up
-        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+        ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 3u, [&]() {
             norm_into(P.h[1], P.o, nullptr, false, L.ln2, P.eps, H, blockIdx.x == 0 ? P.h[0] : nullptr, xs, red);
         });
         live = false;
         if (!ok) break;
-        st = open_group<NS>(P, l, 3, L.down, ring, bars, rs, Gs, Ds);
+        st = open(l, 3);
         live = true;
         if (!barrier()) break;
         // E: x = SiLU(gate) * up; down
-        ok = run_group<NS>(st, Gs, Ds, xs, P.xs_addr, bnd, ent, ring,
+        ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 4u, [&]() {
             const uint16_t* gp = P.g;
             const uint16_t* up = P.u;
@@ -491,12 +543,13 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         live = false;
         if (!ok) break;
         if (l + 1 < P.layers) {
-            st = open_group<NS>(P, l + 1, 0, P.layer[l + 1].qkv, ring, bars, rs, Gs, Ds);
+            st = open(l + 1, 0);
             live = true;
         }
         if (!barrier()) break;
     }
     if (live) stretch_drain<NS>(st, bars, rs);  // left early with copies in flight
+    asm volatile("cp.async.wait_all;" ::: "memory");  // a descriptor fetch still in flight (error paths)
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(P.sync + kSyncError, 2u);
         return;

@@ -479,8 +479,11 @@ __device__ __forceinline__ void stretch_drain(const Stretch& st, uint32_t bars, 
 // through the arrival counters). xsrc(J.x) gives a job's activation source
 // (XGlobal or XShared). Returns false if a copy never landed (error code 2
 // recorded, in-flight copies drained).
-// No residual-sum wait: the sums are complete before the stretch runs.
+// The residual-sum wait of stretch_run: poll() says without waiting whether
+// the sums are published, operator() waits for them (bounded; false: gave
+// up). RReady: no wait, the sums are complete before the stretch runs.
 struct RReady {
+    __device__ __forceinline__ bool poll() const { return true; }
     __device__ __forceinline__ bool operator()() const { return true; }
 };
 
@@ -488,8 +491,8 @@ template <int NS, int M, class X, class B, class XSrc, class RWait = RReady>
 __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_t ring, uint32_t bars,
                                             RingState& rs, XSrc&& xsrc, RWait&& r_ready = RWait{}) {
     // LATE: the residual sums may still be in the making while the stretch
-    // runs (r_ready() waits for them): read at each item's end instead of its
-    // start
+    // runs: an item reads them as soon as a poll between its quads finds them
+    // published, else at its end after r_ready() has waited for them
     constexpr bool LATE = !std::is_same<std::decay_t<RWait>, RReady>::value;
     constexpr uint32_t kQuad = Ring<NS>::kQuad;
     const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -543,7 +546,16 @@ __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_
                         R[2 * h + jj] = __ldcg(jpart + ((int64_t)(2 * c + jj) * kg + cur.grp) * rpad +
                                                cur.b16 * 16 + g + 8 * h);
         };
+        bool r_have = !LATE;
         if (!LATE) load_r();
+        auto poll_r = [&]() {
+            if constexpr (LATE) {
+                if (!r_have && r_ready.poll()) {
+                    r_have = true;
+                    load_r();
+                }
+            }
+        };
 
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         const int nq = (n_units + 3) >> 2;
@@ -558,6 +570,7 @@ __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_
                                     refill);
             c_slot ^= 1u;
             c_phase ^= c_slot == 0 ? 1u : 0u;
+            poll_r();
         }
         if (failed) break;
         for (int q = q0; q < nq; ++q) {  // the short last quad, or every quad of a phantom item
@@ -586,7 +599,7 @@ __device__ __forceinline__ bool stretch_run(Stretch& st, const B& batch, uint32_
         }
         if (failed) break;
 
-        if (LATE) {
+        if (LATE && !r_have) {
             if (!r_ready()) {
                 failed = true;
                 break;
