@@ -66,6 +66,10 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // (and its memory), then let the successor be scheduled.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;"); }
+// Release/acquire fence at GPU scope: with a relaxed atomic or flag after it
+// (release) or before it (acquire), the ordering that a GPU-wide hand-off of
+// data needs, without the total order of a sequentially consistent fence.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 cudaError_t upload_lattices();
 // allow_tile: the launch may take the tcgen05 tile path (the jobs' workspaces

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long 
     if (threadIdx.x == 0) {
         uint32_t ok = 1u;
         auto* arrivals = reinterpret_cast<unsigned long long*>(sync + kSyncArrivals);
-        __threadfence();
+        fence_acq_rel_gpu();  // release: the CTA's writes before its arrival
         atomicAdd(arrivals, 1ull);
         uint32_t polls = 0;
         while (ld_acquire64(arrivals) < target) {
@@ -264,13 +264,16 @@ struct GroupSync {
 };
 
 // stretch_run's residual-sum wait in run_group: the group's sums are
-// published all at once, by the flag taking the group's token.
+// published all at once, by the flag taking the group's token. The writers
+// are warps of this CTA that fence at GPU scope before the flag is set, so a
+// reader that has seen the flag needs only CTA-scope ordering before its
+// loads of the sums (a GPU-scope fence here cost about a microsecond).
 struct RToken {
     const uint32_t* flag;
     uint32_t token;
     __device__ __forceinline__ bool poll() const {
         if (*reinterpret_cast<const volatile uint32_t*>(flag) != token) return false;
-        __threadfence();
+        __threadfence_block();
         return true;
     }
     __device__ __forceinline__ bool operator()() const {
@@ -279,7 +282,7 @@ struct RToken {
             if (polls >= kBarrierPolls) return false;
             if (polls > 64) __nanosleep(32);
         }
-        __threadfence();
+        __threadfence_block();
         return true;
     }
 };
@@ -314,14 +317,14 @@ __device__ __forceinline__ bool run_group(Stretch& st, const StepGroup& G, const
     };
     if (n_busy == kSWarps) {  // no idle warp: sum first
         sums(threadIdx.x, kSThreads);
-        __threadfence();
+        fence_acq_rel_gpu();  // release: the sums before the flag
         __syncthreads();
         if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&gs.r_flag) = token;
         __syncthreads();
     } else if (!has) {  // an idle warp: its share of the sums, then the flag
         const int rank = __popc(~mask & ((1u << warp) - 1u)), n_idle = kSWarps - n_busy;
         sums(rank * 32 + lane, n_idle * 32);
-        __threadfence();
+        fence_acq_rel_gpu();  // release: the sums before the flag
         asm volatile("bar.sync 1, %0;" ::"r"(n_idle * 32) : "memory");
         if (rank == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(&gs.r_flag) = token;
     }

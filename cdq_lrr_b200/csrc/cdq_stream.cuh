@@ -241,14 +241,14 @@ __device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const
         }
     }
     if (!report) return;
-    __threadfence();
+    fence_acq_rel_gpu();  // release: the group values before the count
     __syncwarp();
     uint32_t before = 0;
     if (lane == 0) before = atomicAdd(J.counters + b16, (uint32_t)done);
     before = __shfl_sync(0xFFFFFFFFu, before, 0);
     if (before + (uint32_t)done != (uint32_t)kg) return;
     // every group has arrived: add them in group order
-    __threadfence();
+    fence_acq_rel_gpu();  // acquire: the other groups' values after the count
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int row = b16 * 16 + g + 8 * h;
