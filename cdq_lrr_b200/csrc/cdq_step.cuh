@@ -24,7 +24,10 @@
 //
 // The barrier: thread 0 of each CTA adds an arrival to a monotonic counter
 // and polls it until every CTA has arrived (bounded; on timeout the error word
-// is set and every CTA leaves at its next barrier).
+// is set and every CTA leaves at its next barrier). After a projection step a
+// CTA arrives first, then opens the next projection group (descriptors,
+// residual stage, first weight copies), then waits: the opening overlaps the
+// wait for the slowest CTA instead of delaying this CTA's arrival.
 // The cooperative launch guarantees that all CTAs are resident, one per SM.
 
 namespace step {
@@ -82,13 +85,22 @@ constexpr int kSyncError = 4;     // u32: the sticky error code
 // the caller leaves. ok_s: a word of the CTA's shared window (no static
 // shared memory: the streaming layout needs the dynamic window at the start
 // of the CTA's).
-__device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long target, volatile uint32_t& ok_s) {
+// It comes in two halves: grid_arrive (the CTA's writes are done and its
+// arrival counted) and grid_wait; work between them must not read anything
+// another CTA wrote before the barrier (the step opens its next projection
+// group there, which reads only weights and descriptors).
+__device__ __forceinline__ void grid_arrive(uint32_t* sync) {
     __syncthreads();
+    if (threadIdx.x == 0) {
+        fence_acq_rel_gpu();  // release: the CTA's writes before its arrival
+        atomicAdd(reinterpret_cast<unsigned long long*>(sync + kSyncArrivals), 1ull);
+    }
+}
+
+__device__ __forceinline__ bool grid_wait(uint32_t* sync, unsigned long long target, volatile uint32_t& ok_s) {
     if (threadIdx.x == 0) {
         uint32_t ok = 1u;
         auto* arrivals = reinterpret_cast<unsigned long long*>(sync + kSyncArrivals);
-        fence_acq_rel_gpu();  // release: the CTA's writes before its arrival
-        atomicAdd(arrivals, 1ull);
         uint32_t polls = 0;
         while (ld_acquire64(arrivals) < target) {
             if (++polls >= kBarrierPolls) {
@@ -113,6 +125,11 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long 
     }
     __syncthreads();
     return ok_s != 0u;
+}
+
+__device__ __forceinline__ bool grid_barrier(uint32_t* sync, unsigned long long target, volatile uint32_t& ok_s) {
+    grid_arrive(sync);
+    return grid_wait(sync, target, ok_s);
 }
 
 // Residual sums of the items of `batch` whose first unit lies in
@@ -443,10 +460,15 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
             ld_acquire64(reinterpret_cast<const unsigned long long*>(P.sync + kSyncLaunches));
         target = (launches * (unsigned long long)(5 * P.layers + 1) + 1ull) * n_ctas;
     }
-    auto barrier = [&]() {
-        const bool b = grid_barrier(P.sync, target, bar_ok);
+    auto arrive = [&]() { grid_arrive(P.sync); };
+    auto wait = [&]() {
+        const bool b = grid_wait(P.sync, target, bar_ok);
         target += n_ctas;
         return b;
+    };
+    auto barrier = [&]() {
+        arrive();
+        return wait();
     };
     // the group descriptors in use alternate between the two shared buffers:
     // a group's are fetched while the group before it runs
@@ -485,9 +507,10 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
+        arrive();  // this group's outputs are written: the next group opens while the others finish
         st = open(l, 1);
         live = true;
-        if (!barrier()) break;
+        if (!wait()) break;
         // B: attention, one CTA per query head
         if ((int)blockIdx.x < P.heads && pos_ok)
             dm::attn_head(blockIdx.x, threadIdx.x, P.q, P.k, P.v, P.cos_t + (int64_t)pos * dm::kHd,
@@ -511,9 +534,10 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
+        arrive();  // this group's outputs are written: the next group opens while the others finish
         st = open(l, 2);
         live = true;
-        if (!barrier()) break;
+        if (!wait()) break;
         // D: x = RMSNorm(h' + o); gate, up
         ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 3u, [&]() {
@@ -521,9 +545,10 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
+        arrive();  // this group's outputs are written: the next group opens while the others finish
         st = open(l, 3);
         live = true;
-        if (!barrier()) break;
+        if (!wait()) break;
         // E: x = SiLU(gate) * up; down
         ok = run_group<NS>(st, Gs(), Ds(), xs, P.xs_addr, bnd, ent, ring,
                            bars, rs, gsync, 4u * l + 4u, [&]() {
@@ -545,11 +570,12 @@ __global__ void __launch_bounds__(kSThreads, 1) decode_step_kernel(const StepPar
         });
         live = false;
         if (!ok) break;
+        arrive();
         if (l + 1 < P.layers) {
             st = open(l + 1, 0);
             live = true;
         }
-        if (!barrier()) break;
+        if (!wait()) break;
     }
     if (live) stretch_drain<NS>(st, bars, rs);  // left early with copies in flight
     asm volatile("cp.async.wait_all;" ::: "memory");  // a descriptor fetch still in flight (error paths)
