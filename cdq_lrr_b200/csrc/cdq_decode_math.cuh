@@ -109,6 +109,17 @@ __device__ __forceinline__ void attn_core(int tid, const uint16_t* kb, const uin
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
         if ((tid & 31) == 0) S.red[tid >> 5] = mx;
     }
+    // the weighted values: thread (slice t, element d) takes positions j = t mod
+    // kVSlices; the value loads of its first 16 positions are issued here, in
+    // flight during the two reductions
+    const int d = tid & (kHd - 1), t = (tid / kHd) % kVSlices;
+    constexpr int kBatch = 16;
+    uint16_t vv0[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+        const int j = t + k * kVSlices;
+        vv0[k] = act && j < P ? vb[(int64_t)j * kHd + d] : (uint16_t)0;
+    }
     __syncthreads();
     mx = S.red[0];
     for (int k2 = 1; k2 < kAttnThreads / 32; ++k2) mx = fmaxf(mx, S.red[k2]);
@@ -126,19 +137,16 @@ __device__ __forceinline__ void attn_core(int tid, const uint16_t* kb, const uin
     __syncthreads();
     sum = 0.f;
     for (int k2 = 0; k2 < kAttnThreads / 32; ++k2) sum += S.red[k2];
-    // weighted values: thread (slice t, element d) takes positions j = t mod kVSlices
-    const int d = tid & (kHd - 1), t = (tid / kHd) % kVSlices;
     if (act) {
         // positions j = t, t + kVSlices, ... below P in order; the value loads of
         // 16 positions are issued before their fmas
-        constexpr int kBatch = 16;
         float acc = 0.f;
         for (int j0 = t; j0 < P; j0 += kBatch * kVSlices) {
             uint16_t vv[kBatch];
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
                 const int j = j0 + k * kVSlices;
-                vv[k] = j < P ? vb[(int64_t)j * kHd + d] : (uint16_t)0;
+                vv[k] = j0 == t ? vv0[k] : j < P ? vb[(int64_t)j * kHd + d] : (uint16_t)0;
             }
 #pragma unroll
             for (int k = 0; k < kBatch; ++k)
