@@ -4,7 +4,7 @@
 // with grid-wide barriers between the steps that depend on one another, so
 // no launch latency, no prologue and no pair-table build is paid per
 // operation. Included by cdq_gemv.cu (it runs the streaming kernel's per-warp
-// stretch code, stream_warp, on every projection group).
+// stretch code, stretch_open and stretch_run, on every projection group).
 //
 // Per layer, every CTA:
 //   A  h' = h + down (layer 0: the embedding row), x = RMSNorm(h') into its own
@@ -19,7 +19,7 @@
 // then RMSNorm of h'' + down, the lm_head rows of every warp with their argmax
 // keys (atomicMax), a barrier, and CTA 0 turns the key into the next token.
 // Every operation uses the same device functions and arithmetic as the
-// one-kernel-per-operation step (cdq_decode_math.cuh, stream_warp, the
+// one-kernel-per-operation step (cdq_decode_math.cuh, the stretch code, the
 // residual pre-pass's per-bucket sums), so the two steps give the same bits.
 //
 // The barrier: thread 0 of each CTA adds an arrival to a monotonic counter
@@ -307,8 +307,9 @@ struct RToken {
 // Runs an opened projection group: the CTA builds the group's input in shared
 // memory (`prep`, every thread, CTA barriers allowed), then the warps that
 // have items start streaming while the others compute this CTA's residual
-// sums; an item's warp waits for them (flag `token`, bounded) only at the
-// item's end. Without idle warps everyone sums first. CTA-uniform result.
+// sums; an item's warp reads them once a poll between its quads finds the
+// flag `token` set (a bounded wait at the item's end at the latest). Without
+// idle warps everyone sums first. CTA-uniform result.
 template <int NS, class Prep>
 __device__ __forceinline__ bool run_group(Stretch& st, const StepGroup& G, const StepStage& d, const uint16_t* xs,
                                           uint32_t xs_addr, const uint32_t* bnd, const uint32_t* ent, uint32_t ring,
