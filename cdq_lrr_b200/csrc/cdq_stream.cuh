@@ -249,6 +249,7 @@ __device__ __noinline__ void cut_group(const GemvJob& J, int b16, int grp, const
     if (before + (uint32_t)done != (uint32_t)kg) return;
     // every group has arrived: add them in group order
     fence_acq_rel_gpu();  // acquire: the other groups' values after the count
+    __syncwarp();         // ... for every lane, through lane 0's acquire
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const int row = b16 * 16 + g + 8 * h;
